@@ -1,0 +1,177 @@
+/*
+ * gtmoe.h -- C ABI of libgtmoe.so, a B200 (sm_100a) implementation of the
+ * forward path of GoTransformers' mixtureofexperts package.
+ *
+ * The Go reference has no FFI for this path; its seam is the
+ * transformer.FeedForwardLayer interface (transformer/block.go:24-29) that
+ * *mixtureofexperts.MixtureOfExperts implements.  A Go wrapper type loads this
+ * library at run time with purego, the way gpu/library_unix.go:19-33 and
+ * gpu/vulkan.go:443-518 load Vulkan, so CGO_ENABLED=0 builds keep working.
+ * Every entry point below names the reference function it replaces.
+ *
+ * Conventions
+ *  - Every function returning int returns 0 on success or a negative
+ *    GTMOE_E* code; gtmoe_last_error() then holds a message for the calling
+ *    thread.  Argument errors are the misuse the reference panics on.
+ *  - Pointers may be host memory (Go slices) or CUDA device memory; the
+ *    library detects which.  Host pointers are only read or written during
+ *    the call.  Weights are copied to the device at set time.
+ *  - A handle serialises its own calls with a mutex; separate handles may be
+ *    used from separate threads.
+ *  - There is no CPU fallback: without a usable sm_100 GPU gtmoe_create
+ *    fails with GTMOE_ENODEVICE.
+ */
+#ifndef GTMOE_H
+#define GTMOE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GTMOE_VERSION 100
+
+/* lowprecision.Precision (lowprecision/lowprecision.go:9-16). */
+#define GTMOE_FLOAT64 0
+#define GTMOE_FLOAT32 1
+#define GTMOE_INT8 2
+#define GTMOE_FP4 3
+
+/* Element types of activations passed across the boundary. */
+#define GTMOE_DTYPE_F64 0
+#define GTMOE_DTYPE_F32 1
+#define GTMOE_DTYPE_BF16 2
+
+/* Which experts / which layer of a GatedFeedForward
+ * (feedforward/gatedfeedforward.go:11-16). */
+#define GTMOE_SHARED 0
+#define GTMOE_ROUTED 1
+#define GTMOE_GATE 0
+#define GTMOE_UP 1
+#define GTMOE_DOWN 2
+
+/* Error codes. */
+#define GTMOE_OK 0
+#define GTMOE_EINVAL (-1)    /* bad argument (the reference panics)        */
+#define GTMOE_ENODEVICE (-2) /* no usable sm_100 device                    */
+#define GTMOE_ECUDA (-3)     /* CUDA runtime error                         */
+#define GTMOE_ENOTREADY (-4) /* weights missing, or Forward not yet called */
+#define GTMOE_ENOMEM (-5)    /* device allocation failed                   */
+#define GTMOE_ETIMEOUT (-6)  /* a bounded device-side wait gave up         */
+#define GTMOE_ENCCL (-7)     /* NCCL error (expert parallel only)          */
+
+/* Constructor arguments of NewMixtureOfExperts / NewClampedMixtureOfExperts
+ * (mixtureofexperts/mixtureofexperts.go:33-70) plus the precision that
+ * Layer.CompressWeights gave the expert layers (perceptron/layer.go:52-61). */
+typedef struct gtmoe_config {
+    int32_t d_model;           /* vectorSize                                */
+    int32_t hidden;            /* expertHiddenSize                          */
+    int32_t n_shared;          /* numberOfSharedExperts  (>= 0)             */
+    int32_t n_routed;          /* numberOfRoutedExperts  (>= 1)             */
+    int32_t experts_per_token; /* expertsPerToken, 1..n_routed              */
+    int32_t hash_routing;      /* MixtureOfExperts.UseHashRouting           */
+    int32_t clamped;           /* 1 = NewClampedMixtureOfExperts            */
+    int32_t weight_precision;  /* GTMOE_FLOAT64/FLOAT32/INT8/FP4 of experts */
+    double clamp_limit;        /* clampLimit (> 0 when clamped)             */
+} gtmoe_config;
+
+typedef struct gtmoe_handle *gtmoe_t;
+
+/* GTMOE_VERSION of the loaded library. */
+int gtmoe_version(void);
+
+/* Message for the last failed call on this thread ("" if none). */
+const char *gtmoe_last_error(void);
+
+/* buildMixtureOfExperts (mixtureofexperts.go:47-70): validates the same
+ * arguments and creates a handle on CUDA device `device`.  Weights start
+ * unset; Forward fails with GTMOE_ENOTREADY until every layer is set. */
+int gtmoe_create(const gtmoe_config *cfg, int device, gtmoe_t *out);
+
+/* Expert-parallel variant: this process is rank `rank` of `n_ranks`, one per
+ * GPU.  Routed experts are owned contiguously by index, E/n_ranks per rank
+ * (E must divide evenly).  Router and shared experts are replicated.
+ * nccl_id is the 128-byte ncclUniqueId from gtmoe_ep_unique_id() on rank 0,
+ * distributed by the caller.  No counterpart in the reference (it has no
+ * multi-GPU MoE); Forward keeps the reference's per-token semantics. */
+int gtmoe_ep_unique_id(void *nccl_id_128);
+int gtmoe_create_ep(const gtmoe_config *cfg, int device, int n_ranks, int rank, const void *nccl_id_128,
+                    gtmoe_t *out);
+
+/* Frees every device allocation of the handle.  NULL is ignored. */
+void gtmoe_destroy(gtmoe_t h);
+
+/* Runs the handle's work on `stream` (a cudaStream_t; NULL = the handle's
+ * own stream). */
+int gtmoe_set_stream(gtmoe_t h, void *stream);
+
+/* RouterLayer weights and biases (perceptron.Layer d -> E, Linear;
+ * mixtureofexperts.go:60; Layer.SetWeights/SetBiases layer.go:234-254).
+ * precision GTMOE_FLOAT64 takes values = double[E*d] and scales = NULL;
+ * a compressed router (transformer/memory.go:25-34 compresses it too) takes
+ * the RowsSnapshot arrays as in gtmoe_set_expert_layer.  bias = double[E] or
+ * NULL for zeros. */
+int gtmoe_set_router(gtmoe_t h, int precision, const void *values, const float *scales, const double *bias);
+
+/* MixtureOfExperts.BalanceBiases (mixtureofexperts.go:21), double[E]. */
+int gtmoe_set_balance(gtmoe_t h, const double *balance);
+int gtmoe_get_balance(gtmoe_t h, double *balance);
+
+/* One perceptron.Layer of one expert, as lowprecision.Rows.Snapshot()
+ * returns it (lowprecision/rows.go:148-170; Layer.SetCompressedWeights
+ * layer.go:63-73):
+ *   GTMOE_FLOAT64: values = double[rows*width],  scales = NULL
+ *   GTMOE_FLOAT32: values = float[rows*width],   scales = NULL
+ *   GTMOE_INT8:    values = int8[rows*width],    scales = float[rows*ceil(width/16)]
+ *   GTMOE_FP4:     values = uint8[rows*((width+1)/2)] (low nibble = even
+ *                  element), scales = float[rows*ceil(width/16)]
+ * gate/up are hidden x d_model, down is d_model x hidden (outputs x inputs,
+ * row-major, layer.go:34).  bias = double[rows] or NULL for zeros.
+ * precision must equal cfg.weight_precision. */
+int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, int precision, const void *values,
+                           const float *scales, int rows, int width, const double *bias);
+
+/* MixtureOfExperts.Forward (mixtureofexperts.go:122-216).
+ *   x         T x d_model, x_dtype GTMOE_DTYPE_*
+ *   token_ids T int64 ids; required with hash routing, else may be NULL
+ *   residual  NULL, or T x d_model in out_dtype: added to the output (the
+ *             residual of transformer.Block.Forward, block.go:77; the
+ *             reference's Forward itself returns no residual)
+ *   out       T x d_model in out_dtype
+ * Optional (NULL to skip), all in the reference's order:
+ *   chosen    int32[T*k]  lastChosenExperts
+ *   gates     double[T*k] lastGates
+ *   perm      int32[T*k]  lastRowsForExpert concatenated, e = 0..E-1
+ *   load      int64[E]    lastExpertLoad
+ * In expert-parallel handles T and x are this rank's tokens, and perm and
+ * load cover the experts this rank owns.
+ * With host output pointers the call returns after the results are there;
+ * with device pointers it is asynchronous on the handle's stream. */
+int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
+                  void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load);
+
+/* MixtureOfExperts.LastExpertLoad (mixtureofexperts.go:287-291), int64[E]
+ * (this rank's experts under expert parallelism).  GTMOE_ENOTREADY before
+ * the first Forward. */
+int gtmoe_last_expert_load(gtmoe_t h, int64_t *load);
+
+/* MixtureOfExperts.UpdateBalance (mixtureofexperts.go:293-310) from the last
+ * Forward's load.  No-op with hash routing or before the first Forward. */
+int gtmoe_update_balance(gtmoe_t h, double rate);
+
+/* lowprecision.RowsFromMatrix (lowprecision/rows.go:276-283, Rows.Append
+ * rows.go:38-79) on the GPU: quantises rows x width float64 values into the
+ * RowsSnapshot arrays described above.  Bit-identical to the reference
+ * quantiser.  Any mix of host and device pointers. */
+int gtmoe_quantize_rows(int precision, const double *values, int64_t rows, int width, void *codes, float *scales);
+
+/* Benchmark input generator, no counterpart in the reference: fills n values
+ * of dtype on device memory `dev` with stddev * N(0,1) samples, value i
+ * derived only from (seed, i) by SplitMix64 + Box-Muller. */
+int gtmoe_fill_normal(void *dev, int dtype, int64_t n, uint64_t seed, double stddev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
