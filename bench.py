@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""MoE-layer forward benchmark (BASELINE metric: MoE-layer tokens/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5] [--impl ours|reference]
+
+One step = one MixtureOfExperts.Forward of the config's whole token batch
+(whole-job: all ranks' tokens).  Under torchrun (N > 1) each rank owns T/N
+tokens; the default workload is BASELINE config 5 (65536 tokens x d 4096,
+256 routed experts + 1 shared, hidden 2048, top-8, FP4 experts, bf16
+activations, Zipf(1.0) router bias), the configuration the metric is quoted
+on at 1/2/4/8 GPUs.  Inputs are seeded synthetic data of the config's shape
+(no dataset exists for this path); every input exceeds the 126 MB L2 (x is
+512 MiB, the expert weights 4.85 GB), so no L2 flush is needed between steps.
+
+Rank 0 prints one JSON line.  `value` is device-resident throughput (CUDA
+events on the launching stream, max over ranks); `e2e` is the same metric
+through the C-ABI call with pinned host buffers, host<->device copies inside
+the timed region; `roofline` is the dominant kernel (the grouped expert
+GEMMs) timed live by the library's per-phase CUDA events; `cpu_baseline` is
+the CPU oracle (a C float64 restatement of the reference algorithm, all host
+cores) on a seeded token sample.
+
+`--impl reference` times the reference's CPU algorithm instead (the oracle
+port; the Go reference cannot be built here) on the same config, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--config", default="c5")
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--mode", default="auto", choices=["auto", "ep", "replicas"],
+                   help="multi-GPU mode: expert parallel (NCCL all-to-all) or token-sharded replicas")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=15.0)
+    return p.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            j = json.load(f)
+        return {"hbm_gbs": j["hbm_gbs"], "bf16_tflops": j["bf16_tflops"],
+                "bf16_tflops_sustained": j.get("bf16_tflops_sustained", j["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------- clocks
+
+CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p for p in vis.split(",") if p.strip()]
+        try:
+            return int(parts[local_rank])
+        except (ValueError, IndexError):
+            return local_rank
+    return local_rank
+
+
+class ClockSampler:
+    def __init__(self):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self, gpu_index: int):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [q.strip() for q in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                if int(parts[0]) != gpu_index:
+                    continue
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU oracle
+
+def oracle_spec(cfg, host):
+    from oracle import oracle as O
+
+    wr, rb = host[("router",)]
+    router = O.Layer(O.FLOAT64, cfg.n_routed, cfg.d, np.ascontiguousarray(wr).reshape(-1), None,
+                     np.ascontiguousarray(rb, np.float64))
+    experts = []
+    for e in range(cfg.n_shared + cfg.n_routed):
+        layers = []
+        for which, (rows, width) in enumerate([(cfg.h, cfg.d), (cfg.h, cfg.d), (cfg.d, cfg.h)]):
+            codes, scales = host[(e, which)]
+            layers.append(O.Layer(cfg.precision, rows, width, codes, scales, None))
+        experts.append(tuple(layers))
+    return O.MoESpec(d=cfg.d, h=cfg.h, n_shared=cfg.n_shared, n_routed=cfg.n_routed, k=cfg.k, router=router,
+                     experts=experts)
+
+
+def time_oracle(spec, x_all, budget_s: float, threads: int, min_tokens: int = 2):
+    """Runs the oracle on a seeded token sample sized for ~budget_s seconds;
+    returns (tokens/s, tokens, seconds)."""
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(123)
+    T = x_all.shape[0]
+    probe = np.sort(rng.choice(T, size=min(min_tokens, T), replace=False))
+    t0 = time.perf_counter()
+    O.moe_forward(spec, x_all[probe], probe.astype(np.int64), threads=threads)
+    per_tok = max((time.perf_counter() - t0) / len(probe), 1e-6)
+    n = int(min(T, max(min_tokens, budget_s / per_tok)))
+    sample = np.sort(rng.choice(T, size=n, replace=False))
+    t0 = time.perf_counter()
+    O.moe_forward(spec, x_all[sample], sample.astype(np.int64), threads=threads)
+    dt = time.perf_counter() - t0
+    return n / dt, n, dt
+
+
+# ------------------------------------------------------------------ main
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and not (world == 1 and args.gpus == 1):
+        print(f"bench.py: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+
+    from gotransformers_b200 import synthetic
+
+    cfg = synthetic.CONFIGS[args.config]
+    metric = "MoE-layer tokens/s"
+    if args.impl == "reference":
+        return run_reference(args, cfg, rank, world, local_rank, metric)
+
+    import torch
+    import torch.distributed as dist
+
+    from gotransformers_b200 import _lib
+    from gotransformers_b200 import moe as M
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    mode = args.mode
+    if mode == "auto":
+        mode = "replicas" if world == 1 else "ep"
+    if world > 1 and mode == "ep":
+        try:
+            probe_id = bytearray(128)
+            _lib.check(_lib.lib().gtmoe_ep_unique_id((__import__("ctypes").c_char * 128).from_buffer(probe_id)))
+        except _lib.GtmoeError:
+            mode = "replicas"
+
+    T_total = cfg.T
+    if T_total % world:
+        raise SystemExit(f"{T_total} tokens do not split over {world} ranks")
+    T_local = T_total // world
+    if world > 1 and mode == "ep":
+        nccl_id = bytearray(128)
+        if rank == 0:
+            import ctypes
+
+            _lib.check(_lib.lib().gtmoe_ep_unique_id((ctypes.c_char * 128).from_buffer(nccl_id)))
+        obj = [bytes(nccl_id)]
+        dist.broadcast_object_list(obj, src=0)
+        moe = M.MixtureOfExperts(cfg.d, cfg.h, cfg.n_shared, cfg.n_routed, cfg.k, weight_precision=cfg.precision,
+                                 device=local_rank, ep_ranks=world, ep_rank=rank, nccl_id=obj[0])
+    else:
+        moe = M.MixtureOfExperts(cfg.d, cfg.h, cfg.n_shared, cfg.n_routed, cfg.k, weight_precision=cfg.precision,
+                                 device=local_rank)
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
+    host = synthetic.load_config_on_gpu(cfg, moe, keep_host=want_cpu, device=local_rank)
+    x = synthetic.make_x_on_gpu(cfg, T=T_local, offset_rows=rank * T_local, device=local_rank)
+    out = torch.empty((T_local, cfg.d), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    moe.set_stream(stream.cuda_stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        moe.forward(x, out=out, want_routing=False)
+    torch.cuda.synchronize(dev)
+    barrier()
+
+    L = _lib.lib()
+    _lib.check(L.gtmoe_set_timing(moe.handle, 1))
+    sampler = ClockSampler()
+    torch.cuda.synchronize(dev)
+    barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        moe.forward(x, out=out, want_routing=False)
+    ev1.record(stream)
+    ev1.synchronize()
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop(physical_gpu_index(local_rank))
+    ms = ev0.elapsed_time(ev1) / args.steps
+    import ctypes
+
+    phase_ms = (ctypes.c_double * _lib.N_PHASES)()
+    calls, launches = ctypes.c_int64(), ctypes.c_int64()
+    _lib.check(L.gtmoe_read_timing(moe.handle, phase_ms, _lib.N_PHASES, ctypes.byref(calls), ctypes.byref(launches)))
+    _lib.check(L.gtmoe_set_timing(moe.handle, 0))
+    phases = {n: phase_ms[i] / max(calls.value, 1) for i, n in enumerate(_lib.PHASES)}
+
+    # end to end through the C ABI with pinned host buffers
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((T_local, cfg.d), dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):
+        moe.forward(x_host, out=out_host, want_routing=False)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps // 2)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        moe.forward(x_host, out=out_host, want_routing=False)
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+        ph = torch.tensor([phases[n] for n in _lib.PHASES], dtype=torch.float64, device=dev)
+        dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+        phases = {n: float(ph[i]) for i, n in enumerate(_lib.PHASES)}
+
+    peaks = measured_peaks()
+    # dominant kernel: the grouped gate/up GEMM (2/3 of the expert FLOPs)
+    rows_local = T_local * (cfg.k + cfg.n_shared) if mode != "ep" else None
+    gate_up_flops = T_local * (cfg.k + cfg.n_shared) * 4.0 * cfg.d * cfg.h
+    down_flops = T_local * (cfg.k + cfg.n_shared) * 2.0 * cfg.d * cfg.h
+    kern = max((("expert_gate_up", gate_up_flops), ("expert_down", down_flops)),
+               key=lambda kv: phases[kv[0]])
+    kname, kflops = kern
+    kms = phases[kname]
+    achieved = kflops / (kms * 1e-3) / 1e12 if kms > 0 else 0.0
+    traffic = profiled_traffic(kname, cfg.name, T_local)
+    roofline = {"kernel": kname, "bound": "tensor", "achieved": round(achieved, 2),
+                "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": traffic,
+                "peak_source": f"{peaks['source']} bf16 sustained (kernel timed inside a long step loop)",
+                "algorithmic_flops_per_launch": kflops, "avg_ms": round(kms, 4)}
+
+    cpu_baseline = None
+    if want_cpu:
+        spec = oracle_spec(cfg, host)
+        x_cpu = x.to(torch.float64).cpu().numpy()
+        threads = os.cpu_count() or 1
+        v, n, dt = time_oracle(spec, x_cpu, args.cpu_seconds, threads)
+        cpu_baseline = {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                        "sample": f"{n} seeded tokens of {cfg.name} ({dt:.1f} s), C float64 restatement of "
+                                  f"the reference CPU path; row independence makes a token sample valid"}
+
+    if rank == 0:
+        value = T_total / (ms * 1e-3)
+        line = {
+            "metric": metric, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 activations, N(0,1/fan_in) weights quantised by the reference "
+                    "quantiser, Zipf router bias)",
+            "config": {"workload": f"BASELINE {cfg.name}: {cfg.T} tokens x d {cfg.d}, {cfg.n_routed} routed + "
+                                   f"{cfg.n_shared} shared SwiGLU experts (hidden {cfg.h}), top-{cfg.k}, "
+                                   f"{['Float64', 'Float32', 'Int8', 'FP4'][cfg.precision]} experts",
+                       "tokens": cfg.T, "d_model": cfg.d, "hidden": cfg.h, "n_routed": cfg.n_routed,
+                       "n_shared": cfg.n_shared, "top_k": cfg.k,
+                       "parallelism": f"{mode}{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (x 512 MiB, weights 4.85 GB): no flush"},
+            "e2e": {"value": round(T_total / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(T_local * cfg.d * 2), "d2h_bytes_per_step": int(T_local * cfg.d * 2)},
+            "roofline": roofline,
+            "cpu_baseline": cpu_baseline,
+            "phases_ms": {k: round(v, 4) for k, v in phases.items()},
+            "gpu_launches": int(launches.value),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    moe.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def profiled_traffic(kernel: str, config: str, T_local: int):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary
+    (profiles/traffic.json), scaled by tokens when captured on a smaller
+    case; None when no capture exists."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        j = json.load(f)
+    ent = j.get(f"{kernel}:{config}")
+    if not ent:
+        return None
+    return int(ent["bytes_per_launch"] * T_local / ent["tokens"])
+
+
+def run_reference(args, cfg, rank, world, local_rank, metric):
+    """The reference's CPU algorithm (the C float64 oracle port; the Go
+    reference has no toolchain here) on the host cores, rank 0 only.  Inputs
+    are the same seeded weights and activations as the GPU arm, generated with
+    the library's GPU generator and quantiser (input preparation only, not
+    timed)."""
+    if rank != 0:
+        return
+    import torch
+
+    from gotransformers_b200 import moe as M
+    from gotransformers_b200 import synthetic
+
+    torch.cuda.set_device(local_rank)
+    moe = M.MixtureOfExperts(cfg.d, cfg.h, cfg.n_shared, cfg.n_routed, cfg.k, weight_precision=cfg.precision,
+                             device=local_rank)
+    host = synthetic.load_config_on_gpu(cfg, moe, keep_host=True, device=local_rank)
+    x = synthetic.make_x_on_gpu(cfg, device=local_rank).to(torch.float64).cpu().numpy()
+    moe.close()
+    spec = oracle_spec(cfg, host)
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(7)
+    # size each step for ~ (a few minutes / steps)
+    probe = np.sort(rng.choice(cfg.T, size=2, replace=False))
+    t0 = time.perf_counter()
+    O.moe_forward(spec, x[probe], probe.astype(np.int64), threads=threads)
+    per_tok = max((time.perf_counter() - t0) / 2, 1e-6)
+    budget = 120.0 / max(args.steps + args.warmup, 1)
+    n = int(min(cfg.T, max(2, budget / per_tok)))
+    sample = np.sort(rng.choice(cfg.T, size=n, replace=False))
+    for _ in range(args.warmup):
+        O.moe_forward(spec, x[sample], sample.astype(np.int64), threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.moe_forward(spec, x[sample], sample.astype(np.int64), threads=threads)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    value = n / (ms * 1e-3)
+    line = {
+        "impl": "reference", "metric": metric, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"BASELINE {cfg.name}", "tokens_per_step": n},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{n} seeded tokens of {cfg.name} per step; C float64 restatement of the "
+                                   f"reference CPU path (no Go toolchain on this image)"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

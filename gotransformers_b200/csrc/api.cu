@@ -1,0 +1,734 @@
+// api.cu -- the C ABI of libgtmoe.so (include/gtmoe.h): handles, weight
+// upload, and the Forward orchestration
+//   router -> dispatch -> gather -> grouped SwiGLU -> combine
+// of MixtureOfExperts.Forward (mixtureofexperts/mixtureofexperts.go:122-216).
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "handle.h"
+
+namespace gtmoe {
+
+static thread_local char g_error[2048];
+
+void set_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_error, sizeof(g_error), fmt, ap);
+    va_end(ap);
+}
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_error, sizeof(g_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+static std::atomic<int64_t> g_launches{0};
+void note_launches(int n) { g_launches += n; }
+int64_t launches_so_far() { return g_launches.load(); }
+
+static bool is_device_ptr(const void *p) {
+    if (!p) return false;
+    cudaPointerAttributes at;
+    cudaError_t e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+static size_t precision_bytes(int precision, int64_t rows, int width) {
+    switch (precision) {
+    case GTMOE_FLOAT64: return (size_t)rows * width * 8;
+    case GTMOE_FLOAT32: return (size_t)rows * width * 4;
+    case GTMOE_INT8: return (size_t)rows * width;
+    default: return (size_t)rows * fp4_row_bytes(width);
+    }
+}
+
+}  // namespace gtmoe
+
+using namespace gtmoe;
+
+int gtmoe_handle::phase_begin(int p) {
+    if (!timing) return 0;
+    if (tev_used == tev.size()) {
+        PhaseEvents pe;
+        for (int i = 0; i < GTMOE_N_PHASES; i++) {
+            GT_CUDA(cudaEventCreate(&pe.start[i]));
+            GT_CUDA(cudaEventCreate(&pe.stop[i]));
+        }
+        tev.push_back(pe);
+    }
+    GT_CUDA(cudaEventRecord(tev[tev_used].start[p], stream));
+    return 0;
+}
+
+int gtmoe_handle::phase_end(int p) {
+    if (!timing) return 0;
+    GT_CUDA(cudaEventRecord(tev[tev_used].stop[p], stream));
+    return 0;
+}
+
+namespace gtmoe {
+
+int layer_index(const gtmoe_handle *h, int kind, int index, int which) {
+    int S = h->cfg.n_shared;
+    if (kind == GTMOE_SHARED) return 3 * index + which;
+    return 3 * (S + index - h->e_begin) + which;
+}
+
+static int validate_config(const gtmoe_config *c) {
+    if (!c) return fail(GTMOE_EINVAL, "config is NULL");
+    if (c->d_model < 1 || c->hidden < 1)
+        return fail(GTMOE_EINVAL, "NewMixtureOfExperts: needs d_model >= 1 and hidden >= 1, got %d and %d",
+                    c->d_model, c->hidden);
+    if (c->n_shared < 0)
+        return fail(GTMOE_EINVAL, "NewMixtureOfExperts: number of shared experts can't be negative, got %d",
+                    c->n_shared);
+    if (c->n_routed < 1)
+        return fail(GTMOE_EINVAL, "NewMixtureOfExperts: needs at least 1 routed expert, got %d", c->n_routed);
+    if (c->experts_per_token < 1 || c->experts_per_token > c->n_routed)
+        return fail(GTMOE_EINVAL, "NewMixtureOfExperts: experts per token must be between 1 and %d, got %d",
+                    c->n_routed, c->experts_per_token);
+    if (c->clamped && !(c->clamp_limit > 0))
+        return fail(GTMOE_EINVAL, "NewClampedSwiGLU: limit must be above 0, got %g", c->clamp_limit);
+    if (c->weight_precision < GTMOE_FLOAT64 || c->weight_precision > GTMOE_FP4)
+        return fail(GTMOE_EINVAL, "unknown precision %d", c->weight_precision);
+    if (c->n_routed > kMaxRoutedExperts)
+        return fail(GTMOE_EINVAL, "this build supports at most %d routed experts, got %d", kMaxRoutedExperts,
+                    c->n_routed);
+    if (c->experts_per_token > kMaxTopK)
+        return fail(GTMOE_EINVAL, "this build supports at most %d experts per token, got %d", kMaxTopK,
+                    c->experts_per_token);
+    return 0;
+}
+
+static int open_device(int device) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(GTMOE_ENODEVICE, "no CUDA device: %s", e == cudaSuccess ? "count is 0" : cudaGetErrorString(e));
+    }
+    if (device < 0 || device >= n) return fail(GTMOE_ENODEVICE, "device %d does not exist (%d devices)", device, n);
+    cudaDeviceProp p;
+    GT_CUDA(cudaGetDeviceProperties(&p, device));
+    if (p.major != 10)
+        return fail(GTMOE_ENODEVICE, "device %d is sm_%d%d; libgtmoe.so is built for sm_100a only", device, p.major,
+                    p.minor);
+    GT_CUDA(cudaSetDevice(device));
+    return 0;
+}
+
+int create_handle(const gtmoe_config *cfg, int device, int n_ranks, int rank, gtmoe_t *out) {
+    if (!out) return fail(GTMOE_EINVAL, "out is NULL");
+    *out = nullptr;
+    GT_CHECK(validate_config(cfg));
+    GT_CHECK(open_device(device));
+    if (n_ranks < 1 || rank < 0 || rank >= n_ranks || cfg->n_routed % n_ranks != 0)
+        return fail(GTMOE_EINVAL, "%d routed experts cannot be split evenly over %d ranks (rank %d)", cfg->n_routed,
+                    n_ranks, rank);
+    gtmoe_handle *h = new gtmoe_handle();
+    h->cfg = *cfg;
+    h->device = device;
+    h->n_ranks = n_ranks;
+    h->rank = rank;
+    h->e_local = cfg->n_routed / n_ranks;
+    h->e_begin = rank * h->e_local;
+    h->layers.resize((size_t)3 * (cfg->n_shared + h->e_local));
+    h->h_bal.assign(cfg->n_routed, 0.0);
+    cudaError_t e = cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete h;
+        return fail(GTMOE_ECUDA, "cudaStreamCreate failed: %s", cudaGetErrorString(e));
+    }
+    h->stream = h->own_stream;
+    int rc = h->bal.ensure(sizeof(double) * cfg->n_routed);
+    if (rc == 0) rc = cudaMemset(h->bal.p, 0, sizeof(double) * cfg->n_routed) == cudaSuccess ? 0 : GTMOE_ECUDA;
+    if (rc != 0) {
+        gtmoe_destroy(h);
+        return rc;
+    }
+    *out = h;
+    return 0;
+}
+
+static int upload(DevBuf &dst, const void *src, size_t bytes, cudaStream_t st) {
+    GT_CHECK(dst.ensure(bytes));
+    if (bytes) GT_CUDA(cudaMemcpyAsync(dst.p, src, bytes, cudaMemcpyDefault, st));
+    return 0;
+}
+
+static int to_host(std::vector<char> &buf, const void *src, size_t bytes) {
+    buf.resize(bytes);
+    if (bytes) GT_CUDA(cudaMemcpy(buf.data(), src, bytes, cudaMemcpyDefault));
+    return 0;
+}
+
+// Decodes RowsSnapshot arrays to float64 exactly as Rows.Row does
+// (lowprecision/rows.go:87-119).
+static void decode_rows_host(int precision, int rows, int width, const void *values, const float *scales,
+                             double *out) {
+    int blocks = scale_blocks(width);
+    for (int r = 0; r < rows; r++)
+        for (int i = 0; i < width; i++) {
+            double v;
+            size_t o = (size_t)r * width + i;
+            switch (precision) {
+            case GTMOE_FLOAT64: v = ((const double *)values)[o]; break;
+            case GTMOE_FLOAT32: v = (double)((const float *)values)[o]; break;
+            case GTMOE_INT8: v = (double)((const int8_t *)values)[o] * (double)scales[(size_t)r * blocks + i / 16]; break;
+            default: {
+                uint8_t b = ((const uint8_t *)values)[(size_t)r * fp4_row_bytes(width) + i / 2];
+                int c = (i & 1) ? (b >> 4) : (b & 15);
+                static const double mag[8] = {0, 0.5, 1, 1.5, 2, 3, 4, 6};
+                double m = mag[c & 7] * (double)scales[(size_t)r * blocks + i / 16];
+                v = (c & 8) ? -m : m;
+            }
+            }
+            out[o] = v;
+        }
+}
+
+static int all_layers_set(const gtmoe_handle *h) {
+    for (size_t i = 0; i < h->layers.size(); i++)
+        if (!h->layers[i].set) {
+            int S = h->cfg.n_shared;
+            int e = (int)(i / 3);
+            const char *which = (i % 3 == 0) ? "gate" : (i % 3 == 1) ? "up" : "down";
+            if (e < S) return fail(GTMOE_ENOTREADY, "shared expert %d %s layer is not set", e, which);
+            return fail(GTMOE_ENOTREADY, "routed expert %d %s layer is not set", e - S + h->e_begin, which);
+        }
+    if (!h->cfg.hash_routing && !h->router_set) return fail(GTMOE_ENOTREADY, "router weights are not set");
+    return 0;
+}
+
+static int refresh_table(gtmoe_handle *h) {
+    if (!h->table_dirty) return 0;
+    int n = h->cfg.n_shared + h->e_local;
+    std::vector<ExpertLayers> t(n);
+    for (int e = 0; e < n; e++)
+        for (int w = 0; w < 3; w++) {
+            LayerDev &L = h->layers[3 * e + w];
+            t[e].w[w] = L.w.p;
+            t[e].s[w] = L.s.as<float>();
+            t[e].b32[w] = L.has_bias ? L.b32.as<float>() : nullptr;
+            t[e].b64[w] = L.has_bias ? L.b64.as<double>() : nullptr;
+        }
+    GT_CHECK(h->table.ensure(sizeof(ExpertLayers) * n));
+    GT_CUDA(cudaMemcpy(h->table.p, t.data(), sizeof(ExpertLayers) * n, cudaMemcpyHostToDevice));
+    GT_CHECK(tc_prepare(h, h->tc));
+    h->table_dirty = 0;
+    return 0;
+}
+
+// Single-GPU forward on device-resident x (x_dev) producing device out.
+int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, const int64_t *ids_dev,
+                   const void *res_dev, void *out_dev, int out_dtype) {
+    const gtmoe_config &c = h->cfg;
+    const int E = c.n_routed, k = c.experts_per_token, S = c.n_shared, d = c.d_model, hd = c.hidden;
+    cudaStream_t st = h->stream;
+    const bool use_tc = tc_supported(h, T);
+    const int compute = c.weight_precision == GTMOE_FLOAT64 ? GTMOE_DTYPE_F64
+                        : use_tc                            ? GTMOE_DTYPE_BF16
+                                                            : GTMOE_DTYPE_F32;
+    const size_t cs = dtype_size(compute);
+    const int64_t TK = T * k;
+    const int64_t rows_x = (S > 0 ? T : 0) + TK;
+    const int64_t rows_h = (int64_t)S * T + TK;
+    const int n_chunks = (int)((T + kDispatchChunk - 1) / kDispatchChunk);
+
+    GT_CHECK(h->logits.ensure(sizeof(double) * (size_t)T * E));
+    GT_CHECK(h->chosen.ensure(sizeof(int32_t) * (size_t)TK));
+    GT_CHECK(h->gates64.ensure(sizeof(double) * (size_t)TK));
+    GT_CHECK(h->gates32.ensure(sizeof(float) * (size_t)TK));
+    GT_CHECK(h->counts.ensure(sizeof(int32_t) * (size_t)(n_chunks > 0 ? n_chunks : 1) * E));
+    GT_CHECK(h->load.ensure(sizeof(int64_t) * E));
+    GT_CHECK(h->offsets.ensure(sizeof(int64_t) * (E + 1)));
+    GT_CHECK(h->perm.ensure(sizeof(int32_t) * (size_t)TK));
+    GT_CHECK(h->slot_row.ensure(sizeof(int64_t) * (size_t)TK));
+    GT_CHECK(h->groups.ensure(sizeof(Group) * (S + E)));
+    GT_CHECK(h->tile_prefix.ensure(sizeof(int64_t) * (S + E + 1)));
+    GT_CHECK(h->xp.ensure(cs * (size_t)rows_x * d));
+    GT_CHECK(h->hp.ensure(cs * (size_t)rows_h * hd));
+    GT_CHECK(h->yp.ensure(cs * (size_t)rows_h * d));
+    GT_CHECK(h->fixups.ensure(sizeof(int)));
+    GT_CHECK(refresh_table(h));
+
+    RouterArgs ra;
+    ra.hash = c.hash_routing;
+    ra.x = x_dev;
+    ra.x_dtype = x_dtype;
+    ra.T = T;
+    ra.E = E;
+    ra.k = k;
+    ra.d = d;
+    ra.token_ids = ids_dev;
+    ra.w32 = h->wr32.as<float>();
+    ra.w64 = h->wr64.as<double>();
+    ra.bias = h->br.as<double>();
+    ra.balance = h->bal.as<double>();
+    ra.thresh_scale = 32.0 * ldexp(1.0, -24) * h->wmax;
+    ra.logits = h->logits.as<double>();
+    ra.chosen = h->chosen.as<int32_t>();
+    ra.gates64 = h->gates64.as<double>();
+    ra.gates32 = h->gates32.as<float>();
+    ra.n_fixups = h->fixups.as<int>();
+    GT_CHECK(h->phase_begin(0));
+    GT_CUDA(cudaMemsetAsync(h->fixups.p, 0, sizeof(int), st));
+    GT_CHECK(launch_router(ra, st));
+    GT_CHECK(h->phase_end(0));
+
+    DispatchArgs da;
+    da.T = T;
+    da.E = E;
+    da.k = k;
+    da.S = S;
+    da.chosen = ra.chosen;
+    da.chunk_counts = h->counts.as<int32_t>();
+    da.load = h->load.as<int64_t>();
+    da.offsets = h->offsets.as<int64_t>();
+    da.perm = h->perm.as<int32_t>();
+    da.slot_row = h->slot_row.as<int64_t>();
+    da.groups = h->groups.as<Group>();
+    da.tile_prefix = h->tile_prefix.as<int64_t>();
+    da.bm = use_tc ? kTcBM : kSimtBM;
+    GT_CHECK(h->phase_begin(1));
+    GT_CHECK(launch_dispatch(da, st));
+    GT_CHECK(h->phase_end(1));
+
+    GT_CHECK(h->phase_begin(2));
+    GT_CHECK(launch_gather(x_dev, x_dtype, T, d, da.perm, TK, S > 0 ? T : 0, S > 0, h->xp.p, compute, st));
+    GT_CHECK(h->phase_end(2));
+
+    if (use_tc) {
+        TcArgs ta;
+        ta.n_groups = S + E;
+        ta.groups = da.groups;
+        ta.tile_prefix = da.tile_prefix;
+        ta.rows_x = rows_x;
+        ta.rows_h = rows_h;
+        ta.xp = h->xp.p;
+        ta.hp = h->hp.p;
+        ta.yp = h->yp.p;
+        GT_CHECK(launch_grouped_tc(h, h->tc, ta, st));  // records phases 3 and 4
+    } else {
+        GroupedArgs ga;
+        ga.precision = c.weight_precision;
+        ga.compute = compute;
+        ga.n_groups = S + E;
+        ga.groups = da.groups;
+        ga.tile_prefix = da.tile_prefix;
+        ga.experts = h->table.as<ExpertLayers>();
+        ga.d = d;
+        ga.h = hd;
+        ga.clamped = c.clamped;
+        ga.clamp_limit = c.clamp_limit;
+        ga.xp = h->xp.p;
+        ga.hp = h->hp.p;
+        ga.yp = h->yp.p;
+        GT_CHECK(h->phase_begin(3));
+        if (T > 0) GT_CHECK(launch_grouped_simt(ga, 1, st));
+        GT_CHECK(h->phase_end(3));
+        GT_CHECK(h->phase_begin(4));
+        if (T > 0) GT_CHECK(launch_grouped_simt(ga, 2, st));
+        GT_CHECK(h->phase_end(4));
+    }
+
+    CombineArgs ca;
+    ca.T = T;
+    ca.d = d;
+    ca.k = k;
+    ca.S = S;
+    ca.y = h->yp.p;
+    ca.y_dtype = compute;
+    ca.shared_row0 = 0;
+    ca.routed_row0 = (int64_t)S * T;
+    ca.slot_row = da.slot_row;
+    ca.gates32 = ra.gates32;
+    ca.gates64 = ra.gates64;
+    ca.residual = res_dev;
+    ca.out = out_dev;
+    ca.out_dtype = out_dtype;
+    GT_CHECK(h->phase_begin(5));
+    GT_CHECK(launch_combine(ca, st));
+    GT_CHECK(h->phase_end(5));
+    if (h->timing) h->tev_used++;
+    h->last_T = T;
+    h->have_load = 1;
+    return 0;
+}
+
+}  // namespace gtmoe
+
+extern "C" {
+
+int gtmoe_version(void) { return GTMOE_VERSION; }
+
+const char *gtmoe_last_error(void) { return g_error; }
+
+int gtmoe_create(const gtmoe_config *cfg, int device, gtmoe_t *out) {
+    g_error[0] = 0;
+    return create_handle(cfg, device, 1, 0, out);
+}
+
+void gtmoe_destroy(gtmoe_t h) {
+    if (!h) return;
+    {
+        std::lock_guard<std::mutex> lock(h->mu);
+        cudaSetDevice(h->device);
+        if (h->stream) cudaStreamSynchronize(h->stream);
+        ep_destroy(h);
+        tc_release(h->tc);
+        for (auto &L : h->layers) {
+            L.w.release();
+            L.s.release();
+            L.b32.release();
+            L.b64.release();
+        }
+        DevBuf *bufs[] = {&h->wr64, &h->wr32, &h->br, &h->bal, &h->table, &h->x_in, &h->ids, &h->logits,
+                          &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load, &h->offsets, &h->perm,
+                          &h->slot_row, &h->groups, &h->tile_prefix, &h->xp, &h->hp, &h->yp, &h->out_dev,
+                          &h->res_dev, &h->fixups};
+        for (DevBuf *b : bufs) b->release();
+        for (auto &pe : h->tev)
+            for (int i = 0; i < GTMOE_N_PHASES; i++) {
+                cudaEventDestroy(pe.start[i]);
+                cudaEventDestroy(pe.stop[i]);
+            }
+        if (h->own_stream) cudaStreamDestroy(h->own_stream);
+    }
+    delete h;
+}
+
+int gtmoe_set_stream(gtmoe_t h, void *stream) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    h->stream = stream ? (cudaStream_t)stream : h->own_stream;
+    return 0;
+}
+
+int gtmoe_set_router(gtmoe_t h, int precision, const void *values, const float *scales, const double *bias) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    GT_CUDA(cudaSetDevice(h->device));
+    const int E = h->cfg.n_routed, d = h->cfg.d_model;
+    if (precision < GTMOE_FLOAT64 || precision > GTMOE_FP4) return fail(GTMOE_EINVAL, "unknown precision %d", precision);
+    if (!values) return fail(GTMOE_EINVAL, "router values are NULL");
+    if ((precision == GTMOE_INT8 || precision == GTMOE_FP4) && !scales)
+        return fail(GTMOE_EINVAL, "compressed router needs scales");
+    std::vector<char> hv, hs, hb;
+    GT_CHECK(to_host(hv, values, precision_bytes(precision, E, d)));
+    if (scales) GT_CHECK(to_host(hs, scales, sizeof(float) * (size_t)E * scale_blocks(d)));
+    std::vector<double> w64((size_t)E * d);
+    decode_rows_host(precision, E, d, hv.data(), (const float *)hs.data(), w64.data());
+    std::vector<float> w32(w64.size());
+    double wmax = 0;
+    for (int e = 0; e < E; e++) {
+        double ss = 0;
+        for (int i = 0; i < d; i++) {
+            double v = w64[(size_t)e * d + i];
+            ss += v * v;
+            w32[(size_t)e * d + i] = (float)v;
+        }
+        wmax = fmax(wmax, sqrt(ss));
+    }
+    std::vector<double> b(E, 0.0);
+    if (bias) {
+        GT_CHECK(to_host(hb, bias, sizeof(double) * E));
+        memcpy(b.data(), hb.data(), sizeof(double) * E);
+    }
+    GT_CHECK(upload(h->wr64, w64.data(), sizeof(double) * w64.size(), h->stream));
+    GT_CHECK(upload(h->wr32, w32.data(), sizeof(float) * w32.size(), h->stream));
+    GT_CHECK(upload(h->br, b.data(), sizeof(double) * E, h->stream));
+    GT_CUDA(cudaStreamSynchronize(h->stream));
+    h->wmax = wmax * (1 + 1e-6);
+    h->router_set = 1;
+    return 0;
+}
+
+int gtmoe_set_balance(gtmoe_t h, const double *balance) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    if (!balance) return fail(GTMOE_EINVAL, "balance is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    GT_CUDA(cudaSetDevice(h->device));
+    std::vector<char> hb;
+    GT_CHECK(to_host(hb, balance, sizeof(double) * h->cfg.n_routed));
+    memcpy(h->h_bal.data(), hb.data(), sizeof(double) * h->cfg.n_routed);
+    GT_CHECK(upload(h->bal, h->h_bal.data(), sizeof(double) * h->cfg.n_routed, h->stream));
+    GT_CUDA(cudaStreamSynchronize(h->stream));
+    return 0;
+}
+
+int gtmoe_get_balance(gtmoe_t h, double *balance) {
+    if (!h || !balance) return fail(GTMOE_EINVAL, "handle or balance is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    GT_CUDA(cudaSetDevice(h->device));
+    GT_CUDA(cudaMemcpy(balance, h->h_bal.data(), sizeof(double) * h->cfg.n_routed, cudaMemcpyDefault));
+    return 0;
+}
+
+int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, int precision, const void *values,
+                           const float *scales, int rows, int width, const double *bias) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    GT_CUDA(cudaSetDevice(h->device));
+    const gtmoe_config &c = h->cfg;
+    if (kind == GTMOE_SHARED) {
+        if (index < 0 || index >= c.n_shared)
+            return fail(GTMOE_EINVAL, "shared expert %d does not exist (%d shared)", index, c.n_shared);
+    } else if (kind == GTMOE_ROUTED) {
+        if (index < 0 || index >= c.n_routed)
+            return fail(GTMOE_EINVAL, "routed expert %d does not exist (%d routed)", index, c.n_routed);
+        if (index < h->e_begin || index >= h->e_begin + h->e_local)
+            return fail(GTMOE_EINVAL, "routed expert %d is not owned by rank %d (owns %d..%d)", index, h->rank,
+                        h->e_begin, h->e_begin + h->e_local - 1);
+    } else {
+        return fail(GTMOE_EINVAL, "kind must be GTMOE_SHARED or GTMOE_ROUTED, got %d", kind);
+    }
+    if (which < GTMOE_GATE || which > GTMOE_DOWN) return fail(GTMOE_EINVAL, "which must be gate, up or down");
+    if (precision != c.weight_precision)
+        return fail(GTMOE_EINVAL, "layer precision %d differs from the handle's weight precision %d", precision,
+                    c.weight_precision);
+    int want_rows = which == GTMOE_DOWN ? c.d_model : c.hidden;
+    int want_width = which == GTMOE_DOWN ? c.hidden : c.d_model;
+    if (rows != want_rows || width != want_width)
+        return fail(GTMOE_EINVAL, "layer: got %dx%d compressed weights but it holds %dx%d", rows, width, want_rows,
+                    want_width);
+    if (!values) return fail(GTMOE_EINVAL, "values are NULL");
+    if ((precision == GTMOE_INT8 || precision == GTMOE_FP4) && !scales)
+        return fail(GTMOE_EINVAL, "Int8/FP4 layers need scales");
+    LayerDev &L = h->layers[layer_index(h, kind, index, which)];
+    GT_CHECK(upload(L.w, values, precision_bytes(precision, rows, width), h->stream));
+    if (precision == GTMOE_INT8 || precision == GTMOE_FP4)
+        GT_CHECK(upload(L.s, scales, sizeof(float) * (size_t)rows * scale_blocks(width), h->stream));
+    L.has_bias = 0;
+    if (bias) {
+        std::vector<char> hb;
+        GT_CHECK(to_host(hb, bias, sizeof(double) * rows));
+        std::vector<float> b32(rows);
+        const double *b = (const double *)hb.data();
+        int nonzero = 0;
+        for (int i = 0; i < rows; i++) {
+            b32[i] = (float)b[i];
+            nonzero |= b[i] != 0;
+        }
+        if (nonzero) {
+            GT_CHECK(upload(L.b64, b, sizeof(double) * rows, h->stream));
+            GT_CHECK(upload(L.b32, b32.data(), sizeof(float) * rows, h->stream));
+            L.has_bias = 1;
+        }
+    }
+    GT_CUDA(cudaStreamSynchronize(h->stream));
+    L.precision = precision;
+    L.rows = rows;
+    L.width = width;
+    L.set = 1;
+    h->table_dirty = 1;
+    return 0;
+}
+
+int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
+                  void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    GT_CUDA(cudaSetDevice(h->device));
+    const gtmoe_config &c = h->cfg;
+    if (T < 0) return fail(GTMOE_EINVAL, "mixture of experts: negative number of rows %lld", (long long)T);
+    if (T > 0 && (!x || !out)) return fail(GTMOE_EINVAL, "mixture of experts: x and out must be given");
+    if (x_dtype < GTMOE_DTYPE_F64 || x_dtype > GTMOE_DTYPE_BF16 || out_dtype < GTMOE_DTYPE_F64 ||
+        out_dtype > GTMOE_DTYPE_BF16)
+        return fail(GTMOE_EINVAL, "unknown dtype");
+    if (c.hash_routing && T > 0 && !token_ids)
+        return fail(GTMOE_EINVAL, "mixture of experts: hash routing needs one token ID per row, got none for %lld rows",
+                    (long long)T);
+    GT_CHECK(all_layers_set(h));
+    if (h->n_ranks > 1)
+        return ep_forward(h, x, x_dtype, T, token_ids, residual, out, out_dtype, chosen, gates, perm, load);
+
+    cudaStream_t st = h->stream;
+    const int d = c.d_model, k = c.experts_per_token, E = c.n_routed;
+    const size_t xbytes = dtype_size(x_dtype) * (size_t)T * d;
+    const size_t obytes = dtype_size(out_dtype) * (size_t)T * d;
+
+    const void *x_dev = x;
+    if (T > 0 && !is_device_ptr(x)) {
+        GT_CHECK(upload(h->x_in, x, xbytes, st));
+        x_dev = h->x_in.p;
+    }
+    const int64_t *ids_dev = nullptr;
+    if (c.hash_routing && T > 0) {
+        std::vector<char> hid;
+        GT_CHECK(to_host(hid, token_ids, sizeof(int64_t) * T));
+        const int64_t *ids = (const int64_t *)hid.data();
+        for (int64_t t = 0; t < T; t++)
+            if (ids[t] < 0)
+                return fail(GTMOE_EINVAL, "mixture of experts: token ID %lld at row %lld is negative",
+                            (long long)ids[t], (long long)t);
+        GT_CHECK(upload(h->ids, hid.data(), sizeof(int64_t) * T, st));
+        ids_dev = h->ids.as<int64_t>();
+    }
+    const void *res_dev = residual;
+    if (residual && T > 0 && !is_device_ptr(residual)) {
+        GT_CHECK(upload(h->res_dev, residual, obytes, st));
+        res_dev = h->res_dev.p;
+    }
+    void *out_dev = out;
+    const bool out_host = T > 0 && !is_device_ptr(out);
+    if (out_host) {
+        GT_CHECK(h->out_dev.ensure(obytes));
+        out_dev = h->out_dev.p;
+    }
+    GT_CHECK(forward_device(h, x_dev, x_dtype, T, ids_dev, res_dev, out_dev, out_dtype));
+
+    bool sync = out_host;
+    const int64_t TK = T * k;
+    if (out_host) GT_CUDA(cudaMemcpyAsync(out, out_dev, obytes, cudaMemcpyDeviceToHost, st));
+    if (chosen && TK) {
+        GT_CUDA(cudaMemcpyAsync(chosen, h->chosen.p, sizeof(int32_t) * TK, cudaMemcpyDefault, st));
+        sync |= !is_device_ptr(chosen);
+    }
+    if (gates && TK) {
+        GT_CUDA(cudaMemcpyAsync(gates, h->gates64.p, sizeof(double) * TK, cudaMemcpyDefault, st));
+        sync |= !is_device_ptr(gates);
+    }
+    if (perm && TK) {
+        GT_CUDA(cudaMemcpyAsync(perm, h->perm.p, sizeof(int32_t) * TK, cudaMemcpyDefault, st));
+        sync |= !is_device_ptr(perm);
+    }
+    if (load) {
+        GT_CUDA(cudaMemcpyAsync(load, h->load.p, sizeof(int64_t) * E, cudaMemcpyDefault, st));
+        sync |= !is_device_ptr(load);
+    }
+    if (sync) GT_CUDA(cudaStreamSynchronize(st));
+    return 0;
+}
+
+int gtmoe_last_expert_load(gtmoe_t h, int64_t *load) {
+    if (!h || !load) return fail(GTMOE_EINVAL, "handle or load is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    if (!h->have_load) return fail(GTMOE_ENOTREADY, "LastExpertLoad before the first Forward");
+    GT_CUDA(cudaSetDevice(h->device));
+    int n = h->n_ranks > 1 ? h->e_local : h->cfg.n_routed;
+    GT_CUDA(cudaMemcpyAsync(load, h->load.p, sizeof(int64_t) * n, cudaMemcpyDefault, h->stream));
+    GT_CUDA(cudaStreamSynchronize(h->stream));
+    return 0;
+}
+
+int gtmoe_update_balance(gtmoe_t h, double rate) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    if (!h->have_load || h->cfg.hash_routing) return 0;
+    GT_CUDA(cudaSetDevice(h->device));
+    const int E = h->cfg.n_routed;
+    std::vector<int64_t> load(E);
+    GT_CHECK(ep_global_load(h, load.data()));
+    int64_t total = 0;
+    for (int e = 0; e < E; e++) total += load[e];
+    double average = (double)total / (double)E;
+    for (int e = 0; e < E; e++) {
+        if ((double)load[e] < average) h->h_bal[e] += rate;
+        if ((double)load[e] > average) h->h_bal[e] -= rate;
+    }
+    GT_CHECK(upload(h->bal, h->h_bal.data(), sizeof(double) * E, h->stream));
+    GT_CUDA(cudaStreamSynchronize(h->stream));
+    return 0;
+}
+
+int gtmoe_set_timing(gtmoe_t h, int enable) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    h->timing = enable != 0;
+    h->tev_used = 0;
+    h->launches_at_read = launches_so_far();
+    return 0;
+}
+
+int gtmoe_read_timing(gtmoe_t h, double *ms, int n_phases, int64_t *calls, int64_t *kernel_launches) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    GT_CUDA(cudaSetDevice(h->device));
+    GT_CUDA(cudaStreamSynchronize(h->stream));
+    for (int p = 0; p < n_phases && p < GTMOE_N_PHASES; p++) {
+        double total = 0;
+        for (size_t i = 0; i < h->tev_used; i++) {
+            float t = 0;
+            cudaError_t e = cudaEventElapsedTime(&t, h->tev[i].start[p], h->tev[i].stop[p]);
+            if (e == cudaSuccess) total += t;
+            else cudaGetLastError();  // phase not recorded in this call
+        }
+        if (ms) ms[p] += total;
+    }
+    if (calls) *calls = (int64_t)h->tev_used;
+    int64_t now = launches_so_far();
+    if (kernel_launches) *kernel_launches = now - h->launches_at_read;
+    h->launches_at_read = now;
+    h->tev_used = 0;
+    return 0;
+}
+
+int gtmoe_quantize_rows(int precision, const double *values, int64_t rows, int width, void *codes, float *scales) {
+    if (precision < GTMOE_FLOAT64 || precision > GTMOE_FP4) return fail(GTMOE_EINVAL, "unknown precision %d", precision);
+    if (width <= 0 || rows < 0) return fail(GTMOE_EINVAL, "NewRows: width must be at least 1, got %d", width);
+    if (rows == 0) return 0;
+    if (!values || !codes || ((precision == GTMOE_INT8 || precision == GTMOE_FP4) && !scales))
+        return fail(GTMOE_EINVAL, "NULL pointer");
+    int dev = 0;
+    GT_CUDA(cudaGetDevice(&dev));
+    GT_CHECK(open_device(dev));
+    const size_t vbytes = sizeof(double) * (size_t)rows * width;
+    const size_t cbytes = precision_bytes(precision, rows, width);
+    const size_t sbytes = sizeof(float) * (size_t)rows * scale_blocks(width);
+    DevBuf dv, dc, ds;
+    const double *v = values;
+    void *cd = codes;
+    float *sd = scales;
+    int rc = 0;
+    if (!is_device_ptr(values)) {
+        if ((rc = upload(dv, values, vbytes, 0))) goto done;
+        v = dv.as<double>();
+    }
+    if (!is_device_ptr(codes)) {
+        if ((rc = dc.ensure(cbytes))) goto done;
+        cd = dc.p;
+    }
+    if (scales && !is_device_ptr(scales)) {
+        if ((rc = ds.ensure(sbytes))) goto done;
+        sd = ds.as<float>();
+    }
+    if ((rc = launch_quantize_rows(precision, v, rows, width, cd, sd, 0))) goto done;
+    if (cd != codes && cudaMemcpy(codes, cd, cbytes, cudaMemcpyDeviceToHost) != cudaSuccess) rc = GTMOE_ECUDA;
+    if (!rc && scales && sd != scales && (precision == GTMOE_INT8 || precision == GTMOE_FP4) &&
+        cudaMemcpy(scales, sd, sbytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = GTMOE_ECUDA;
+    if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = fail(GTMOE_ECUDA, "quantiser failed");
+done:
+    dv.release();
+    dc.release();
+    ds.release();
+    return rc;
+}
+
+int gtmoe_fill_normal(void *dev, int dtype, int64_t n, uint64_t seed, uint64_t stream, int64_t offset,
+                      double stddev) {
+    if (n < 0 || (n > 0 && !dev)) return fail(GTMOE_EINVAL, "bad arguments");
+    if (n > 0 && !is_device_ptr(dev)) return fail(GTMOE_EINVAL, "gtmoe_fill_normal writes device memory only");
+    GT_CHECK(launch_fill_normal(dev, dtype, n, seed, stream, offset, stddev, 0));
+    GT_CUDA(cudaDeviceSynchronize());
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,185 @@
+// dispatch.cu -- expert-sorted token permutation (rowsForExpert,
+// mixtureofexperts.go:175-180), per-expert load (:188-190), the group table
+// of the grouped GEMMs, and the row gather (gatherRows, :114-120).
+//
+// rowsForExpert lists, for each expert, the tokens that chose it in
+// ascending token order.  The scatter is therefore stable: (token, slot)
+// pairs are ranked in token-major order, chunk by chunk, and within a chunk
+// by warp match over 32 consecutive pairs; a token never lists an expert
+// twice, so token-major pair order is token order per expert.  No atomics
+// decide a position.
+#include "common.cuh"
+#include "internal.h"
+
+namespace gtmoe {
+
+__global__ void dispatch_count_kernel(const int32_t *__restrict__ chosen, int64_t T, int E, int k,
+                                      int32_t *__restrict__ counts) {
+    extern __shared__ int32_t c_smem[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) c_smem[e] = 0;
+    __syncthreads();
+    int64_t t0 = (int64_t)blockIdx.x * kDispatchChunk;
+    int64_t t1 = min(T, t0 + kDispatchChunk);
+    for (int64_t p = t0 * k + threadIdx.x; p < t1 * k; p += blockDim.x) atomicAdd(&c_smem[chosen[p]], 1);
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) counts[(int64_t)blockIdx.x * E + e] = c_smem[e];
+}
+
+__global__ void dispatch_scan_kernel(int32_t *__restrict__ counts, int n_chunks, int64_t T, int E, int S, int bm,
+                                     int64_t *__restrict__ load, int64_t *__restrict__ offsets, Group *__restrict__ groups,
+                                     int64_t *__restrict__ tile_prefix) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int32_t run = 0;
+        for (int c = 0; c < n_chunks; c++) {
+            int32_t v = counts[(int64_t)c * E + e];
+            counts[(int64_t)c * E + e] = run;
+            run += v;
+        }
+        load[e] = run;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int64_t xbase = S > 0 ? T : 0;
+        int64_t off = 0, tiles = 0;
+        for (int s = 0; s < S; s++) {
+            Group g;
+            g.x_row0 = 0;
+            g.h_row0 = (int64_t)s * T;
+            g.m = T;
+            g.expert = s;
+            g.pad = 0;
+            groups[s] = g;
+            tile_prefix[s] = tiles;
+            tiles += (T + bm - 1) / bm;
+        }
+        for (int e = 0; e < E; e++) {
+            offsets[e] = off;
+            Group g;
+            g.x_row0 = xbase + off;
+            g.h_row0 = (int64_t)S * T + off;
+            g.m = load[e];
+            g.expert = S + e;
+            g.pad = 0;
+            groups[S + e] = g;
+            tile_prefix[S + e] = tiles;
+            tiles += (load[e] + bm - 1) / bm;
+            off += load[e];
+        }
+        offsets[E] = off;
+        tile_prefix[S + E] = tiles;
+    }
+}
+
+__global__ void dispatch_scatter_kernel(const int32_t *__restrict__ chosen, const int32_t *__restrict__ counts,
+                                        const int64_t *__restrict__ offsets, int64_t T, int E, int k,
+                                        int32_t *__restrict__ perm, int64_t *__restrict__ slot_row) {
+    extern __shared__ int64_t base[];
+    const int lane = threadIdx.x;
+    for (int e = lane; e < E; e += 32) base[e] = offsets[e] + counts[(int64_t)blockIdx.x * E + e];
+    __syncwarp();
+    int64_t t0 = (int64_t)blockIdx.x * kDispatchChunk;
+    int64_t t1 = min(T, t0 + kDispatchChunk);
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int64_t p0 = t0 * k; p0 < t1 * k; p0 += 32) {
+        int64_t p = p0 + lane;
+        bool valid = p < t1 * k;
+        int e = valid ? chosen[p] : -1;
+        uint32_t peers = __match_any_sync(0xffffffffu, e);
+        int rank = __popc(peers & lt);
+        int64_t pos = 0;
+        if (valid) pos = base[e] + rank;
+        __syncwarp();
+        if (valid) {
+            perm[pos] = (int32_t)(p / k);
+            slot_row[p] = pos;
+            if (rank == 0) base[e] += __popc(peers);
+        }
+        __syncwarp();
+    }
+}
+
+int launch_dispatch(const DispatchArgs &a, cudaStream_t st) {
+    int n_chunks = (int)((a.T + kDispatchChunk - 1) / kDispatchChunk);
+    if (a.T > 0) {
+        dispatch_count_kernel<<<n_chunks, 256, a.E * sizeof(int32_t), st>>>(a.chosen, a.T, a.E, a.k, a.chunk_counts);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+    }
+    dispatch_scan_kernel<<<1, 1024, 0, st>>>(a.chunk_counts, n_chunks, a.T, a.E, a.S, a.bm, a.load, a.offsets,
+                                             a.groups, a.tile_prefix);
+    GT_CUDA(cudaGetLastError());
+    note_launches(1);
+    if (a.T > 0) {
+        dispatch_scatter_kernel<<<n_chunks, 32, a.E * sizeof(int64_t), st>>>(a.chosen, a.chunk_counts, a.offsets,
+                                                                             a.T, a.E, a.k, a.perm, a.slot_row);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+    }
+    return 0;
+}
+
+template <typename OUT>
+__global__ void gather_kernel(const void *__restrict__ x, int x_dtype, int64_t T, int d,
+                              const int32_t *__restrict__ perm, int64_t n_routed, int64_t xbase, int copy_shared,
+                              OUT *__restrict__ xp) {
+    int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    int64_t n_shared_rows = copy_shared ? T : 0;
+    if (w >= n_shared_rows + n_routed) return;
+    int64_t src, dst;
+    if (w < n_shared_rows) {
+        src = w;
+        dst = w;
+    } else {
+        int64_t r = w - n_shared_rows;
+        src = perm[r];
+        dst = xbase + r;
+    }
+    for (int i = lane; i < d; i += 32)
+        xp[dst * d + i] = from_double<OUT>(load_as_double(x, x_dtype, src * d + i));
+}
+
+// Same-type bf16 rows: 16-byte vector copies.
+__global__ void gather_bf16_vec_kernel(const uint4 *__restrict__ x, int64_t T, int vec_per_row,
+                                       const int32_t *__restrict__ perm, int64_t n_routed, int64_t xbase,
+                                       int copy_shared, uint4 *__restrict__ xp) {
+    int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    int64_t n_shared_rows = copy_shared ? T : 0;
+    if (w >= n_shared_rows + n_routed) return;
+    int64_t src, dst;
+    if (w < n_shared_rows) {
+        src = w;
+        dst = w;
+    } else {
+        int64_t r = w - n_shared_rows;
+        src = perm[r];
+        dst = xbase + r;
+    }
+    for (int i = lane; i < vec_per_row; i += 32) xp[dst * vec_per_row + i] = x[src * vec_per_row + i];
+}
+
+int launch_gather(const void *x, int x_dtype, int64_t T, int d, const int32_t *perm, int64_t n_routed_rows,
+                  int64_t xbase, int copy_shared, void *xp, int xp_dtype, cudaStream_t st) {
+    int64_t rows = (copy_shared ? T : 0) + n_routed_rows;
+    if (rows == 0) return 0;
+    unsigned blocks = (unsigned)((rows * 32 + 255) / 256);
+    if (x_dtype == GTMOE_DTYPE_BF16 && xp_dtype == GTMOE_DTYPE_BF16 && d % 8 == 0) {
+        gather_bf16_vec_kernel<<<blocks, 256, 0, st>>>((const uint4 *)x, T, d / 8, perm, n_routed_rows, xbase,
+                                                       copy_shared, (uint4 *)xp);
+    } else if (xp_dtype == GTMOE_DTYPE_F64) {
+        gather_kernel<double><<<blocks, 256, 0, st>>>(x, x_dtype, T, d, perm, n_routed_rows, xbase, copy_shared,
+                                                      (double *)xp);
+    } else if (xp_dtype == GTMOE_DTYPE_F32) {
+        gather_kernel<float><<<blocks, 256, 0, st>>>(x, x_dtype, T, d, perm, n_routed_rows, xbase, copy_shared,
+                                                     (float *)xp);
+    } else {
+        gather_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(x, x_dtype, T, d, perm, n_routed_rows, xbase,
+                                                             copy_shared, (__nv_bfloat16 *)xp);
+    }
+    GT_CUDA(cudaGetLastError());
+    note_launches(1);
+    return 0;
+}
+
+}  // namespace gtmoe

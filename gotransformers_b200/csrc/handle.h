@@ -1,0 +1,113 @@
+// handle.h -- the state behind a gtmoe_t (shared by api.cu, tc.cu, ep.cu).
+#pragma once
+
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace gtmoe {
+
+// Grow-only device buffer.
+struct DevBuf {
+    void *p = nullptr;
+    size_t n = 0;
+    int ensure(size_t bytes) {
+        if (bytes <= n) return 0;
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+        size_t want = bytes < 256 ? 256 : bytes;
+        cudaError_t e = cudaMalloc(&p, want);
+        if (e != cudaSuccess) {
+            p = nullptr;
+            cudaGetLastError();
+            return fail(GTMOE_ENOMEM, "cudaMalloc of %zu bytes failed: %s", want, cudaGetErrorString(e));
+        }
+        n = want;
+        return 0;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    template <typename T>
+    T *as() const {
+        return (T *)p;
+    }
+};
+
+struct LayerDev {
+    int set = 0;
+    int precision = 0, rows = 0, width = 0;
+    DevBuf w, s, b32, b64;
+    int has_bias = 0;
+};
+
+}  // namespace gtmoe
+
+#include "tc.h"
+
+struct gtmoe_handle {
+    using DevBuf = gtmoe::DevBuf;
+    using LayerDev = gtmoe::LayerDev;
+    gtmoe_config cfg;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    cudaStream_t own_stream = nullptr;
+    std::mutex mu;
+
+    // expert parallelism
+    int n_ranks = 1, rank = 0;
+    int e_begin = 0, e_local = 0;
+    void *ep = nullptr;  // EpState (ep.cu)
+
+    // router
+    int router_set = 0;
+    DevBuf wr64, wr32, br, bal;
+    std::vector<double> h_bal;
+    double wmax = 0;
+
+    std::vector<LayerDev> layers;  // (S + e_local) * 3
+    DevBuf table;
+    int table_dirty = 1;
+    gtmoe::TcWeights tc;  // tensor-core layouts (tc.h)
+
+    // per-call workspace
+    DevBuf x_in, ids, logits, chosen, gates64, gates32, counts, load, offsets, perm, slot_row, groups, tile_prefix, xp,
+        hp, yp, out_dev, res_dev, fixups;
+    int have_load = 0;
+    int64_t last_T = 0;
+    int last_fixups = 0;
+
+    // per-phase timing (gtmoe_set_timing / gtmoe_read_timing)
+    struct PhaseEvents {
+        cudaEvent_t start[GTMOE_N_PHASES];
+        cudaEvent_t stop[GTMOE_N_PHASES];
+    };
+    int timing = 0;
+    std::vector<PhaseEvents> tev;
+    size_t tev_used = 0;
+    int64_t launches_at_read = 0;
+    int phase_begin(int p);
+    int phase_end(int p);
+};
+
+
+namespace gtmoe {
+int layer_index(const gtmoe_handle *h, int kind, int index, int which);
+int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, const int64_t *ids_dev,
+                   const void *res_dev, void *out_dev, int out_dtype);
+int create_handle(const gtmoe_config *cfg, int device, int n_ranks, int rank, gtmoe_t *out);
+
+// expert parallelism (ep.cu)
+void ep_destroy(gtmoe_handle *h);
+int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
+               void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load);
+int ep_global_load(gtmoe_handle *h, int64_t *load);
+
+// kernel launches made by the library (all handles)
+int64_t launches_so_far();
+}  // namespace gtmoe

@@ -1,0 +1,105 @@
+// internal.h -- launchers shared between the .cu files of libgtmoe.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace gtmoe {
+
+// Counts kernel launches made by the library (gtmoe_read_timing).
+void note_launches(int n);
+
+// Limits of this build (checked by gtmoe_create).
+constexpr int kMaxRoutedExperts = 1024;
+constexpr int kMaxTopK = 32;
+
+struct RouterArgs {
+    int hash;
+    const void *x;
+    int x_dtype;
+    int64_t T;
+    int E, k, d;
+    const int64_t *token_ids;   // hash routing (device)
+    const float *w32;           // E x d
+    const double *w64;          // E x d
+    const double *bias;         // E
+    const double *balance;      // E
+    double thresh_scale;        // 32 * 2^-24 * max_e ||w_e||
+    double *logits;             // T x E scratch
+    int32_t *chosen;            // T x k
+    double *gates64;            // T x k
+    float *gates32;             // T x k
+    int *n_fixups;              // counter of tokens re-selected in float64
+};
+int launch_router(const RouterArgs &a, cudaStream_t st);
+
+// Dispatch: builds the token-ascending permutation of (token, slot) pairs by
+// expert (rowsForExpert, mixtureofexperts.go:175-180) and the group table.
+constexpr int kDispatchChunk = 256;
+struct DispatchArgs {
+    int64_t T;
+    int E, k, S;
+    const int32_t *chosen;     // T x k
+    int32_t *chunk_counts;     // n_chunks x E scratch
+    int64_t *load;             // E
+    int64_t *offsets;          // E + 1
+    int32_t *perm;             // T*k : token of each routed row
+    int64_t *slot_row;         // T*k : routed row of (token, slot)
+    Group *groups;             // S + E
+    int64_t *tile_prefix;      // S + E + 1 : prefix of m-tiles per group
+    int bm;                    // m-tile height for the prefix
+};
+int launch_dispatch(const DispatchArgs &a, cudaStream_t st);
+
+// Gathers activation rows into the expert-sorted buffer, converting dtype.
+// Rows [0, T) are x itself when there are shared experts; routed row r is
+// x[perm[r]] at row xbase + r.
+int launch_gather(const void *x, int x_dtype, int64_t T, int d, const int32_t *perm, int64_t n_routed_rows,
+                  int64_t xbase, int copy_shared, void *xp, int xp_dtype, cudaStream_t st);
+
+// Grouped SwiGLU on SIMT cores, any precision and shape.
+struct GroupedArgs {
+    int precision;             // weight precision
+    int compute;               // GTMOE_DTYPE_F32 or GTMOE_DTYPE_F64
+    int n_groups;
+    const Group *groups;
+    const int64_t *tile_prefix;
+    const ExpertLayers *experts;
+    int d, h;
+    int clamped;
+    double clamp_limit;
+    const void *xp;            // rows x d   (compute dtype)
+    void *hp;                  // rows x h   (compute dtype)
+    void *yp;                  // rows x d   (compute dtype)
+};
+constexpr int kSimtBM = 64;
+// which: 1 = gate/up + SwiGLU into hp, 2 = down into yp
+int launch_grouped_simt(const GroupedArgs &a, int which, cudaStream_t st);
+
+// Combine (mixtureofexperts.go:182-205): out = residual + sum_s shared_s +
+// sum_j gate_j * y[slot_row], in the reference's order.
+struct CombineArgs {
+    int64_t T;
+    int d, k, S;
+    const void *y;             // rows x d, y_dtype
+    int y_dtype;
+    int64_t shared_row0;       // row of shared expert 0 (rows s*T + t)
+    int64_t routed_row0;       // row of routed row 0
+    const int64_t *slot_row;   // T x k
+    const float *gates32;      // T x k
+    const double *gates64;     // T x k
+    const void *residual;      // NULL or T x d in out_dtype
+    void *out;
+    int out_dtype;
+};
+int launch_combine(const CombineArgs &a, cudaStream_t st);
+
+// Quantiser (lowprecision/rows.go:38-79) and the benchmark input generator.
+int launch_quantize_rows(int precision, const double *values, int64_t rows, int width, void *codes, float *scales,
+                         cudaStream_t st);
+int launch_fill_normal(void *dev, int dtype, int64_t n, uint64_t seed, uint64_t stream, int64_t offset, double stddev,
+                       cudaStream_t st);
+
+}  // namespace gtmoe

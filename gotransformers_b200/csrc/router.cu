@@ -1,0 +1,280 @@
+// router.cu -- router logits, sqrt-softplus affinities, top-k selection and
+// gates (mixtureofexperts.go:80-82, :98-112, :154-172), and hash routing
+// (:88-96, :142-152).
+//
+// Selection must reproduce the reference's float64 choice exactly.  The
+// logits are first computed from float32 operands (float32 products summed
+// per 16-element block, block sums accumulated in float64).  For token t the
+// error of every logit is below eps_t = 32 * 2^-24 * ||x_t|| * max_e ||w_e||
+// (Cauchy-Schwarz bounds sum |x_i w_i|), and |d affinity / d logit| < 0.5, so a
+// score moves by less than 0.5 * eps_t.  If the gap between the k-th and the
+// (k+1)-th score exceeds 2 * 0.5 * eps_t the chosen set is the reference's;
+// otherwise the warp recomputes that token's logits in float64 in the
+// reference's summation order, with separately rounded multiplies and adds
+// (one sequential sum per expert, as vectormath.DotProduct, vector.go:67-74),
+// and selects again.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace gtmoe {
+
+constexpr int kRouterTile = 64;
+constexpr int kRouterK = 16;
+
+template <int XDT>
+__device__ __forceinline__ float load_x_f32(const void *x, int64_t i) {
+    if (XDT == GTMOE_DTYPE_F64) return (float)((const double *)x)[i];
+    if (XDT == GTMOE_DTYPE_F32) return ((const float *)x)[i];
+    return __bfloat162float(((const __nv_bfloat16 *)x)[i]);
+}
+
+// logits[t, e] = sum_i x[t, i] * w[e, i]   (no bias; added in float64 later)
+template <int XDT>
+__global__ void __launch_bounds__(256) router_logits_kernel(const void *__restrict__ x, const float *__restrict__ w,
+                                                            int64_t T, int E, int d, double *__restrict__ logits) {
+    __shared__ float xs[kRouterK][kRouterTile + 4];
+    __shared__ float ws[kRouterK][kRouterTile + 4];
+    const int64_t t0 = (int64_t)blockIdx.x * kRouterTile;
+    const int e0 = blockIdx.y * kRouterTile;
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    double acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+
+    for (int k0 = 0; k0 < d; k0 += kRouterK) {
+        for (int i = threadIdx.x; i < kRouterTile * kRouterK; i += blockDim.x) {
+            int r = i / kRouterK, c = i % kRouterK;
+            int64_t t = t0 + r;
+            int kk = k0 + c;
+            xs[c][r] = (t < T && kk < d) ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
+            int e = e0 + r;
+            ws[c][r] = (e < E && kk < d) ? w[(int64_t)e * d + kk] : 0.f;
+        }
+        __syncthreads();
+        float part[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) part[i][j] = 0.f;
+#pragma unroll
+        for (int c = 0; c < kRouterK; c++) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) a[i] = xs[c][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) b[j] = ws[c][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) part[i][j] = fmaf(a[i], b[j], part[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] += (double)part[i][j];
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int64_t t = t0 + ty * 4 + i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int e = e0 + tx * 4 + j;
+            if (e < E) logits[t * E + e] = acc[i][j];
+        }
+    }
+}
+
+// activationfunction/moreactivationfunctions.go:8-16, mixtureofexperts.go:80-82
+__device__ __forceinline__ double affinity_d(double logit) {
+    double sp;
+    if (logit > 20) sp = logit;
+    else if (logit < -20) sp = exp(logit);
+    else sp = log1p(exp(logit));
+    return sqrt(sp);
+}
+
+constexpr int kMaxPerLane = kMaxRoutedExperts / 32;
+
+// Picks `count` experts by descending score, ties to the lower index (the
+// first k of sort.SliceStable, mixtureofexperts.go:106-109).
+__device__ __forceinline__ void warp_top(const double (&score)[kMaxPerLane], const double (&aff)[kMaxPerLane], int E,
+                                         int count, int *pick, double *pick_score, double *pick_aff) {
+    const int lane = threadIdx.x & 31;
+    uint32_t taken = 0;
+    for (int i = 0; i < count; i++) {
+        double best = 0;
+        int best_e = 0x7fffffff;
+        double best_a = 0;
+#pragma unroll
+        for (int j = 0; j < kMaxPerLane; j++) {
+            int e = lane + 32 * j;
+            if (e >= E || (taken >> j) & 1u) continue;
+            if (best_e == 0x7fffffff || score[j] > best) {
+                best = score[j];
+                best_e = e;
+                best_a = aff[j];
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            double ob = __shfl_xor_sync(0xffffffffu, best, off);
+            int oe = __shfl_xor_sync(0xffffffffu, best_e, off);
+            double oa = __shfl_xor_sync(0xffffffffu, best_a, off);
+            bool better = oe != 0x7fffffff && (best_e == 0x7fffffff || ob > best || (ob == best && oe < best_e));
+            if (better) {
+                best = ob;
+                best_e = oe;
+                best_a = oa;
+            }
+        }
+        pick[i] = best_e;
+        pick_score[i] = best;
+        pick_aff[i] = best_a;
+        if ((best_e & 31) == lane) taken |= 1u << (best_e >> 5);
+    }
+}
+
+template <int XDT>
+__global__ void __launch_bounds__(256)
+    router_select_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
+                         const double *__restrict__ balance, int64_t T, int E, int k, const void *__restrict__ x, int d,
+                         const double *__restrict__ w64, double thresh_scale, int32_t *__restrict__ chosen,
+                         double *__restrict__ gates64, float *__restrict__ gates32, int *__restrict__ n_fixups) {
+    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (t >= T) return;
+
+    double score[kMaxPerLane], aff[kMaxPerLane];
+#pragma unroll
+    for (int j = 0; j < kMaxPerLane; j++) {
+        int e = lane + 32 * j;
+        score[j] = 0;
+        aff[j] = 0;
+        if (e < E) {
+            double l = logits[t * E + e] + bias[e];  // perceptron/layer.go:150-153
+            aff[j] = affinity_d(l);
+            score[j] = aff[j] + balance[e];  // mixtureofexperts.go:103-105
+        }
+    }
+    int pick[kMaxTopK + 1];
+    double pscore[kMaxTopK + 1], paff[kMaxTopK + 1];
+    const int count = k < E ? k + 1 : k;
+    warp_top(score, aff, E, count, pick, pscore, paff);
+
+    if (k < E) {
+        double ss = 0;
+        for (int i = lane; i < d; i += 32) {
+            double v = load_as_double(x, XDT, t * d + i);
+            ss += v * v;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        double thresh = thresh_scale * sqrt(ss);
+        if (!(pscore[k - 1] - pscore[k] > thresh)) {
+            // float64 logits in the reference's order
+#pragma unroll
+            for (int j = 0; j < kMaxPerLane; j++) {
+                int e = lane + 32 * j;
+                if (e < E) {
+                    const double *wr = w64 + (int64_t)e * d;
+                    double s = 0;
+                    for (int i = 0; i < d; i++) s = __dadd_rn(s, __dmul_rn(load_as_double(x, XDT, t * d + i), wr[i]));
+                    s = __dadd_rn(s, bias[e]);
+                    aff[j] = affinity_d(s);
+                    score[j] = aff[j] + balance[e];
+                }
+            }
+            warp_top(score, aff, E, k, pick, pscore, paff);
+            if (lane == 0) atomicAdd(n_fixups, 1);
+        }
+    }
+    // sort.Ints(chosen) (mixtureofexperts.go:110)
+    for (int i = 1; i < k; i++) {
+        int v = pick[i];
+        double a = paff[i];
+        int j = i - 1;
+        while (j >= 0 && pick[j] > v) {
+            pick[j + 1] = pick[j];
+            paff[j + 1] = paff[j];
+            j--;
+        }
+        pick[j + 1] = v;
+        paff[j + 1] = a;
+    }
+    // gates (mixtureofexperts.go:162-169)
+    double total = 0;
+    for (int i = 0; i < k; i++) total += paff[i];
+    if (lane < k) {
+        int i = lane;
+        // select without dynamic register indexing of pick/paff
+        int e = pick[0];
+        double a = paff[0];
+        for (int q = 1; q < k; q++)
+            if (q == i) {
+                e = pick[q];
+                a = paff[q];
+            }
+        double g = a / total;
+        chosen[t * k + i] = e;
+        gates64[t * k + i] = g;
+        gates32[t * k + i] = (float)g;
+    }
+}
+
+// hashedExperts (mixtureofexperts.go:88-96); gates 1/k (:148-151)
+__global__ void hash_route_kernel(const int64_t *__restrict__ ids, int64_t T, int E, int k, int32_t *__restrict__ chosen,
+                                  double *__restrict__ gates64, float *__restrict__ gates32) {
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    uint64_t first = ((uint64_t)ids[t] * 2654435761ull + 12345ull) % (uint64_t)E;
+    double g = 1.0 / (double)k;
+    for (int i = 0; i < k; i++) {
+        chosen[t * k + i] = (int32_t)((first + (uint64_t)i) % (uint64_t)E);
+        gates64[t * k + i] = g;
+        gates32[t * k + i] = (float)g;
+    }
+}
+
+int launch_router(const RouterArgs &a, cudaStream_t st) {
+    if (a.T == 0) return 0;
+    if (a.hash) {
+        hash_route_kernel<<<(unsigned)((a.T + 255) / 256), 256, 0, st>>>(a.token_ids, a.T, a.E, a.k, a.chosen,
+                                                                         a.gates64, a.gates32);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+        return 0;
+    }
+    dim3 grid((unsigned)((a.T + kRouterTile - 1) / kRouterTile), (unsigned)((a.E + kRouterTile - 1) / kRouterTile));
+    unsigned sel_blocks = (unsigned)((a.T * 32 + 255) / 256);
+    switch (a.x_dtype) {
+    case GTMOE_DTYPE_F64:
+        router_logits_kernel<GTMOE_DTYPE_F64><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);
+        router_select_kernel<GTMOE_DTYPE_F64><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E,
+                                                                          a.k, a.x, a.d, a.w64, a.thresh_scale,
+                                                                          a.chosen, a.gates64, a.gates32, a.n_fixups);
+        break;
+    case GTMOE_DTYPE_F32:
+        router_logits_kernel<GTMOE_DTYPE_F32><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);
+        router_select_kernel<GTMOE_DTYPE_F32><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E,
+                                                                          a.k, a.x, a.d, a.w64, a.thresh_scale,
+                                                                          a.chosen, a.gates64, a.gates32, a.n_fixups);
+        break;
+    default:
+        router_logits_kernel<GTMOE_DTYPE_BF16><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);
+        router_select_kernel<GTMOE_DTYPE_BF16><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E,
+                                                                           a.k, a.x, a.d, a.w64, a.thresh_scale,
+                                                                           a.chosen, a.gates64, a.gates32, a.n_fixups);
+        break;
+    }
+    GT_CUDA(cudaGetLastError());
+    note_launches(2);
+    return 0;
+}
+
+}  // namespace gtmoe

@@ -1,0 +1,34 @@
+// tc.h -- grouped SwiGLU expert products on the tcgen05 tensor cores.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+struct gtmoe_handle;
+
+namespace gtmoe {
+
+constexpr int kTcBM = 128;  // rows (tokens) per tile
+
+struct TcWeights {
+    int ready = 0;
+};
+
+struct TcArgs {
+    int n_groups;
+    const Group *groups;
+    const int64_t *tile_prefix;
+    int64_t rows_x, rows_h;
+    void *xp;  // rows_x x d bf16
+    void *hp;  // rows_h x h bf16
+    void *yp;  // rows_h x d bf16
+};
+
+bool tc_supported(const gtmoe_handle *h, int64_t T);
+int tc_prepare(gtmoe_handle *h, TcWeights &w);
+int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &a, cudaStream_t st);
+void tc_release(TcWeights &w);
+
+}  // namespace gtmoe

@@ -149,3 +149,68 @@ def zipf_router_bias(E: int, k: int, s: float, seed: int, samples: int = 4096, i
         hi = np.where(up, hi, bias)
         bias = 0.5 * (lo + hi)
     return bias
+
+
+def load_config_on_gpu(cfg: MoEConfig, moe, keep_host: bool = False, device: int = 0):
+    """Generates cfg's weights on the GPU (gtmoe_fill_normal + the GPU
+    quantiser, gtmoe_quantize_rows) and sets them on `moe` (a
+    moe.MixtureOfExperts, possibly one expert-parallel rank: only the routed
+    experts it owns are generated).  With keep_host, also returns the host
+    copies {("router",): (w, bias)} | {(e, which): (codes, scales)} for a CPU
+    checker."""
+    import torch
+
+    from . import moe as M
+
+    dev = torch.device("cuda", device)
+    host = {}
+    E, S, d, h = cfg.n_routed, cfg.n_shared, cfg.d, cfg.h
+    rb = zipf_router_bias(E, cfg.k, cfg.zipf_s, cfg.weight_seed) if cfg.zipf_s else np.zeros(E)
+    if not cfg.hash_routing:
+        wr = torch.empty((E, d), dtype=torch.float64, device=dev)
+        M.fill_normal(wr, cfg.weight_seed, STREAM_ROUTER, stddev=1.0 / np.sqrt(d))
+        wr_h = wr.cpu().numpy()
+        moe.set_router(wr_h, rb)
+        if keep_host:
+            host[("router",)] = (wr_h, rb)
+    e_local = E // moe.ep_ranks
+    owned = list(range(S)) + [S + moe.ep_rank * e_local + i for i in range(e_local)]
+    buf = torch.empty(max(h * d, d * h), dtype=torch.float64, device=dev)
+    blocks = lambda w: (w + 15) // 16
+    for e in owned:
+        kind, idx = (M.SHARED, e) if e < S else (M.ROUTED, e - S)
+        for which, (rows, width) in enumerate([(h, d), (h, d), (d, h)]):
+            vals = buf[: rows * width].view(rows, width)
+            M.fill_normal(vals, cfg.weight_seed, expert_stream(e, which), stddev=1.0 / np.sqrt(width))
+            if cfg.precision == M.FLOAT64:
+                codes = vals.clone().reshape(-1)
+                scales = None
+            elif cfg.precision == M.FLOAT32:
+                codes = torch.empty(rows * width, dtype=torch.float32, device=dev)
+                scales = None
+            elif cfg.precision == M.INT8:
+                codes = torch.empty(rows * width, dtype=torch.int8, device=dev)
+                scales = torch.empty(rows * blocks(width), dtype=torch.float32, device=dev)
+            else:
+                codes = torch.empty(rows * ((width + 1) // 2), dtype=torch.uint8, device=dev)
+                scales = torch.empty(rows * blocks(width), dtype=torch.float32, device=dev)
+            M.quantize_rows(cfg.precision, vals, codes, scales)
+            r = M.Rows(cfg.precision, rows, width, codes, scales)
+            moe.set_expert_layer(kind, idx, which, r, None)
+            if keep_host:
+                host[(e, which)] = (codes.cpu().numpy(), None if scales is None else scales.cpu().numpy())
+    del buf
+    return host
+
+
+def make_x_on_gpu(cfg: MoEConfig, T: int | None = None, offset_rows: int = 0, device: int = 0):
+    """Activations of cfg on the GPU: bf16 when cfg.x_bf16, else float64."""
+    import torch
+
+    from . import moe as M
+
+    T = cfg.T if T is None else T
+    dt = torch.bfloat16 if cfg.x_bf16 else torch.float64
+    x = torch.empty((T, cfg.d), dtype=dt, device=torch.device("cuda", device))
+    M.fill_normal(x, cfg.act_seed, STREAM_X, offset=offset_rows * cfg.d)
+    return x

@@ -30,6 +30,12 @@
 extern "C" {
 #endif
 
+#if defined(__GNUC__)
+#define GTMOE_API __attribute__((visibility("default")))
+#else
+#define GTMOE_API
+#endif
+
 #define GTMOE_VERSION 100
 
 /* lowprecision.Precision (lowprecision/lowprecision.go:9-16). */
@@ -79,15 +85,15 @@ typedef struct gtmoe_config {
 typedef struct gtmoe_handle *gtmoe_t;
 
 /* GTMOE_VERSION of the loaded library. */
-int gtmoe_version(void);
+GTMOE_API int gtmoe_version(void);
 
 /* Message for the last failed call on this thread ("" if none). */
-const char *gtmoe_last_error(void);
+GTMOE_API const char *gtmoe_last_error(void);
 
 /* buildMixtureOfExperts (mixtureofexperts.go:47-70): validates the same
  * arguments and creates a handle on CUDA device `device`.  Weights start
  * unset; Forward fails with GTMOE_ENOTREADY until every layer is set. */
-int gtmoe_create(const gtmoe_config *cfg, int device, gtmoe_t *out);
+GTMOE_API int gtmoe_create(const gtmoe_config *cfg, int device, gtmoe_t *out);
 
 /* Expert-parallel variant: this process is rank `rank` of `n_ranks`, one per
  * GPU.  Routed experts are owned contiguously by index, E/n_ranks per rank
@@ -95,16 +101,16 @@ int gtmoe_create(const gtmoe_config *cfg, int device, gtmoe_t *out);
  * nccl_id is the 128-byte ncclUniqueId from gtmoe_ep_unique_id() on rank 0,
  * distributed by the caller.  No counterpart in the reference (it has no
  * multi-GPU MoE); Forward keeps the reference's per-token semantics. */
-int gtmoe_ep_unique_id(void *nccl_id_128);
-int gtmoe_create_ep(const gtmoe_config *cfg, int device, int n_ranks, int rank, const void *nccl_id_128,
+GTMOE_API int gtmoe_ep_unique_id(void *nccl_id_128);
+GTMOE_API int gtmoe_create_ep(const gtmoe_config *cfg, int device, int n_ranks, int rank, const void *nccl_id_128,
                     gtmoe_t *out);
 
 /* Frees every device allocation of the handle.  NULL is ignored. */
-void gtmoe_destroy(gtmoe_t h);
+GTMOE_API void gtmoe_destroy(gtmoe_t h);
 
 /* Runs the handle's work on `stream` (a cudaStream_t; NULL = the handle's
  * own stream). */
-int gtmoe_set_stream(gtmoe_t h, void *stream);
+GTMOE_API int gtmoe_set_stream(gtmoe_t h, void *stream);
 
 /* RouterLayer weights and biases (perceptron.Layer d -> E, Linear;
  * mixtureofexperts.go:60; Layer.SetWeights/SetBiases layer.go:234-254).
@@ -112,11 +118,11 @@ int gtmoe_set_stream(gtmoe_t h, void *stream);
  * a compressed router (transformer/memory.go:25-34 compresses it too) takes
  * the RowsSnapshot arrays as in gtmoe_set_expert_layer.  bias = double[E] or
  * NULL for zeros. */
-int gtmoe_set_router(gtmoe_t h, int precision, const void *values, const float *scales, const double *bias);
+GTMOE_API int gtmoe_set_router(gtmoe_t h, int precision, const void *values, const float *scales, const double *bias);
 
 /* MixtureOfExperts.BalanceBiases (mixtureofexperts.go:21), double[E]. */
-int gtmoe_set_balance(gtmoe_t h, const double *balance);
-int gtmoe_get_balance(gtmoe_t h, double *balance);
+GTMOE_API int gtmoe_set_balance(gtmoe_t h, const double *balance);
+GTMOE_API int gtmoe_get_balance(gtmoe_t h, double *balance);
 
 /* One perceptron.Layer of one expert, as lowprecision.Rows.Snapshot()
  * returns it (lowprecision/rows.go:148-170; Layer.SetCompressedWeights
@@ -129,7 +135,7 @@ int gtmoe_get_balance(gtmoe_t h, double *balance);
  * gate/up are hidden x d_model, down is d_model x hidden (outputs x inputs,
  * row-major, layer.go:34).  bias = double[rows] or NULL for zeros.
  * precision must equal cfg.weight_precision. */
-int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, int precision, const void *values,
+GTMOE_API int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, int precision, const void *values,
                            const float *scales, int rows, int width, const double *bias);
 
 /* MixtureOfExperts.Forward (mixtureofexperts.go:122-216).
@@ -148,28 +154,43 @@ int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, int precis
  * load cover the experts this rank owns.
  * With host output pointers the call returns after the results are there;
  * with device pointers it is asynchronous on the handle's stream. */
-int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
+GTMOE_API int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
                   void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load);
 
 /* MixtureOfExperts.LastExpertLoad (mixtureofexperts.go:287-291), int64[E]
  * (this rank's experts under expert parallelism).  GTMOE_ENOTREADY before
  * the first Forward. */
-int gtmoe_last_expert_load(gtmoe_t h, int64_t *load);
+GTMOE_API int gtmoe_last_expert_load(gtmoe_t h, int64_t *load);
 
 /* MixtureOfExperts.UpdateBalance (mixtureofexperts.go:293-310) from the last
  * Forward's load.  No-op with hash routing or before the first Forward. */
-int gtmoe_update_balance(gtmoe_t h, double rate);
+GTMOE_API int gtmoe_update_balance(gtmoe_t h, double rate);
+
+/* Per-phase device timing, the counterpart of the reference's
+ * gpu.Recorder.MeasureTime (gpu/compute.go:653-693).  While enabled, each
+ * Forward records CUDA events on its stream between its phases:
+ *   0 router, 1 dispatch, 2 gather, 3 expert gate/up, 4 expert down,
+ *   5 combine, 6 expert-parallel send, 7 expert-parallel return.
+ * gtmoe_read_timing waits for the stream, adds the milliseconds of each phase
+ * over all Forward calls since the last read into ms[0..n_phases-1], stores
+ * the number of calls and of kernels the library launched in them, and
+ * resets the record. */
+#define GTMOE_N_PHASES 8
+GTMOE_API int gtmoe_set_timing(gtmoe_t h, int enable);
+GTMOE_API int gtmoe_read_timing(gtmoe_t h, double *ms, int n_phases, int64_t *calls, int64_t *kernel_launches);
 
 /* lowprecision.RowsFromMatrix (lowprecision/rows.go:276-283, Rows.Append
  * rows.go:38-79) on the GPU: quantises rows x width float64 values into the
  * RowsSnapshot arrays described above.  Bit-identical to the reference
  * quantiser.  Any mix of host and device pointers. */
-int gtmoe_quantize_rows(int precision, const double *values, int64_t rows, int width, void *codes, float *scales);
+GTMOE_API int gtmoe_quantize_rows(int precision, const double *values, int64_t rows, int width, void *codes, float *scales);
 
 /* Benchmark input generator, no counterpart in the reference: fills n values
- * of dtype on device memory `dev` with stddev * N(0,1) samples, value i
- * derived only from (seed, i) by SplitMix64 + Box-Muller. */
-int gtmoe_fill_normal(void *dev, int dtype, int64_t n, uint64_t seed, double stddev);
+ * of dtype on device memory `dev` with stddev * N(0,1) samples; value j is
+ * sample offset+j of stream (seed, stream), derived only from those numbers
+ * by SplitMix64 + Box-Muller (the definition in synthetic.py). */
+GTMOE_API int gtmoe_fill_normal(void *dev, int dtype, int64_t n, uint64_t seed, uint64_t stream, int64_t offset,
+                      double stddev);
 
 #ifdef __cplusplus
 }

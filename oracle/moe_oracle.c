@@ -397,6 +397,39 @@ void gto_routed_experts(const double *aff, const double *balance, int E, int k, 
     }
 }
 
+/* The routing half of Forward (mixtureofexperts.go:137-173): chosen experts
+ * and gates for every token, optionally the router logits. */
+int gto_moe_route(const gto_moe *m, int T, const double *x, const int64_t *token_ids, int32_t *chosen,
+                  double *gates, double *logits_out) {
+    int E = m->n_routed, k = m->k;
+    if (E < 1 || k < 1 || k > E || m->n_shared < 0) return -2;
+    if (m->hash_routing && !token_ids && T > 0) return -3;
+    if (m->hash_routing) {
+        for (int t = 0; t < T; t++) {
+            if (token_ids[t] < 0) return -4;
+            gto_hashed_experts(token_ids[t], E, k, chosen + (size_t)t * k);
+            for (int i = 0; i < k; i++) gates[(size_t)t * k + i] = 1 / (double)k;
+        }
+        return 0;
+    }
+    double *logits = (double *)malloc(sizeof(double) * (size_t)(T > 0 ? T : 1) * E);
+    double *aff = (double *)malloc(sizeof(double) * (size_t)E);
+    gto_layer_forward(&m->router, GTO_ACT_LINEAR, 0, T, x, logits);
+    for (int t = 0; t < T; t++) {
+        const double *lt = logits + (size_t)t * E;
+        for (int e = 0; e < E; e++) aff[e] = gto_affinity(lt[e]);
+        int32_t *c = chosen + (size_t)t * k;
+        gto_routed_experts(aff, m->balance, E, k, c);
+        double total = 0.0;
+        for (int i = 0; i < k; i++) total += aff[c[i]];
+        for (int i = 0; i < k; i++) gates[(size_t)t * k + i] = aff[c[i]] / total;
+    }
+    if (logits_out) memcpy(logits_out, logits, sizeof(double) * (size_t)T * E);
+    free(aff);
+    free(logits);
+    return 0;
+}
+
 /* MixtureOfExperts.Forward (mixtureofexperts.go:122-216).
  *   x: T x d;  token_ids: T (needed for hash routing, else may be NULL)
  *   out: T x d (the MoE output, no residual)
@@ -413,28 +446,11 @@ int gto_moe_forward(const gto_moe *m, int T, const double *x, const int64_t *tok
     if (m->hash_routing && !token_ids && T > 0) return -3;
     int32_t *chosen = (int32_t *)malloc(sizeof(int32_t) * (size_t)(T > 0 ? T : 1) * k);
     double *gates = (double *)malloc(sizeof(double) * (size_t)(T > 0 ? T : 1) * k);
-    if (m->hash_routing) {
-        for (int t = 0; t < T; t++) {
-            if (token_ids[t] < 0) { free(chosen); free(gates); return -4; }
-            gto_hashed_experts(token_ids[t], E, k, chosen + (size_t)t * k);
-            for (int i = 0; i < k; i++) gates[(size_t)t * k + i] = 1 / (double)k;
-        }
-    } else {
-        double *logits = (double *)malloc(sizeof(double) * (size_t)(T > 0 ? T : 1) * E);
-        double *aff = (double *)malloc(sizeof(double) * (size_t)E);
-        gto_layer_forward(&m->router, GTO_ACT_LINEAR, 0, T, x, logits);
-        for (int t = 0; t < T; t++) {
-            const double *lt = logits + (size_t)t * E;
-            for (int e = 0; e < E; e++) aff[e] = gto_affinity(lt[e]);
-            int32_t *c = chosen + (size_t)t * k;
-            gto_routed_experts(aff, m->balance, E, k, c);
-            double total = 0.0;
-            for (int i = 0; i < k; i++) total += aff[c[i]];
-            for (int i = 0; i < k; i++) gates[(size_t)t * k + i] = aff[c[i]] / total;
-        }
-        if (logits_out) memcpy(logits_out, logits, sizeof(double) * (size_t)T * E);
-        free(aff);
-        free(logits);
+    int rc = gto_moe_route(m, T, x, token_ids, chosen, gates, logits_out);
+    if (rc != 0) {
+        free(chosen);
+        free(gates);
+        return rc;
     }
 
     /* rowsForExpert (:175-180): token-ascending per expert */

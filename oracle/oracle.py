@@ -87,6 +87,8 @@ def lib():
             L.gto_gated_forward.argtypes = [ctypes.POINTER(_CLayer)] * 3 + [i, d, i, vp, vp]
             L.gto_moe_forward.argtypes = [ctypes.POINTER(_CMoE), i, vp, vp, vp, vp, vp, vp, vp, vp]
             L.gto_moe_forward.restype = i
+            L.gto_moe_route.argtypes = [ctypes.POINTER(_CMoE), i, vp, vp, vp, vp, vp]
+            L.gto_moe_route.restype = i
             L.gto_update_balance.argtypes = [vp, vp, i, d]
             L.gto_set_threads.argtypes = [i]
             L.gto_softplus.argtypes = [d]
@@ -263,6 +265,23 @@ def moe_forward(spec: MoESpec, x: np.ndarray, token_ids=None, threads: int = 1) 
     if rc != 0:
         raise ValueError(f"gto_moe_forward rejected its arguments ({rc})")
     return dict(out=out, chosen=chosen, gates=gates, perm=perm, load=load, logits=logits)
+
+
+def moe_route(spec: MoESpec, x: np.ndarray, token_ids=None, threads: int = 1) -> dict:
+    """Routing half of Forward (mixtureofexperts.go:137-173) for every token."""
+    x = np.ascontiguousarray(x, np.float64)
+    T, k = x.shape[0], spec.k
+    chosen = np.empty((T, k), np.int32)
+    gates = np.empty((T, k), np.float64)
+    ids = None if token_ids is None else np.ascontiguousarray(token_ids, np.int64)
+    m = spec._c()
+    L = lib()
+    L.gto_set_threads(threads)
+    rc = L.gto_moe_route(ctypes.byref(m), T, _ptr(x), _ptr(ids), _ptr(chosen), _ptr(gates), None)
+    L.gto_set_threads(1)
+    if rc != 0:
+        raise ValueError(f"gto_moe_route rejected its arguments ({rc})")
+    return dict(chosen=chosen, gates=gates)
 
 
 def update_balance(balance: np.ndarray, load: np.ndarray, rate: float) -> None:
