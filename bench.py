@@ -222,7 +222,10 @@ def main():
     host = synthetic.load_config_on_gpu(cfg, moe, keep_host=want_cpu, device=local_rank)
     x = synthetic.make_x_on_gpu(cfg, T=T_local, offset_rows=rank * T_local, device=local_rank)
     out = torch.empty((T_local, cfg.d), dtype=torch.bfloat16, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    # a dedicated stream: torch's default (legacy) stream has handle 0, which
+    # the C ABI reads as "the handle's own stream"
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     moe.set_stream(stream.cuda_stream)
 
     def barrier():
@@ -285,7 +288,6 @@ def main():
 
     peaks = measured_peaks()
     # dominant kernel: the grouped gate/up GEMM (2/3 of the expert FLOPs)
-    rows_local = T_local * (cfg.k + cfg.n_shared) if mode != "ep" else None
     gate_up_flops = T_local * (cfg.k + cfg.n_shared) * 4.0 * cfg.d * cfg.h
     down_flops = T_local * (cfg.k + cfg.n_shared) * 2.0 * cfg.d * cfg.h
     kern = max((("expert_gate_up", gate_up_flops), ("expert_down", down_flops)),

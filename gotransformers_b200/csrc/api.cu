@@ -613,7 +613,10 @@ int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_
         GT_CUDA(cudaMemcpyAsync(load, h->load.p, sizeof(int64_t) * E, cudaMemcpyDefault, st));
         sync |= !is_device_ptr(load);
     }
-    if (sync) GT_CUDA(cudaStreamSynchronize(st));
+    if (sync) {
+        GT_CUDA(cudaStreamSynchronize(st));
+        GT_CHECK(tc_check_error(h->tc));
+    }
     return 0;
 }
 
@@ -662,6 +665,7 @@ int gtmoe_read_timing(gtmoe_t h, double *ms, int n_phases, int64_t *calls, int64
     std::lock_guard<std::mutex> lock(h->mu);
     GT_CUDA(cudaSetDevice(h->device));
     GT_CUDA(cudaStreamSynchronize(h->stream));
+    GT_CHECK(tc_check_error(h->tc));
     for (int p = 0; p < n_phases && p < GTMOE_N_PHASES; p++) {
         double total = 0;
         for (size_t i = 0; i < h->tev_used; i++) {

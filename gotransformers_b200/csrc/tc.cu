@@ -1,13 +1,619 @@
-// tc.cu -- tcgen05 grouped SwiGLU (placeholder until the kernel lands).
+// tc.cu -- grouped SwiGLU expert products on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), for Int8 and FP4 expert weights.
+//
+// Per expert (GatedFeedForward.Forward, feedforward/gatedfeedforward.go:49-57):
+//   kernel 1 (GATED):  H = act_g(X Wg^T + bg) * act_u(X Wu^T + bu)  -> bf16
+//   kernel 2 (DOWN):   Y = H Wd^T + bd                               -> bf16
+// X / H rows of every expert are contiguous (the dispatch's expert-sorted
+// buffer).  Tiles are 128 rows x 256 columns; for kernel 1 the 256 columns are
+// 128 gate features and the same 128 up features, so each epilogue thread holds
+// both operands of its SwiGLU products in registers.
+//
+// The Int8/FP4 weights stay compressed in HBM exactly as lowprecision.Rows
+// stores them (codes row-major, one float32 scale per 16 values of a row,
+// lowprecision/rows.go:38-79).  Dequantisation warps read them (L2-resident:
+// every weight tile is reused by all m-tiles of its expert), multiply code by
+// scale in float32 and round once to bf16 straight into the shared-memory
+// operand in the UMMA canonical K-major SWIZZLE_128B layout (Rows.Row
+// semantics, rows.go:87-119).  Activations arrive by TMA in the same layout.
+// One elected thread issues tcgen05.mma kind::f16 (bf16 x bf16 -> f32 in
+// TMEM); four epilogue warps read TMEM with tcgen05.ld.
+//
+// Persistent kernel, one CTA per SM, warp roles:
+//   warp 0      TMA producer of the activation tile
+//   warp 1      TMEM allocator and MMA issuer
+//   warps 2-5   epilogue (TMEM -> bias, SwiGLU -> bf16 -> global)
+//   warps 6-13  dequantisation of the weight tile
+// 4-stage shared-memory ring (48 KB per stage), 2 TMEM accumulators of 256
+// columns (the epilogue of one tile overlaps the main loop of the next).
+//
+// Every mbarrier wait is bounded (kWaitLimitNs of %globaltimer).  On expiry
+// the kernel records an error code in *err, raises a CTA-wide abort flag so
+// every role leaves its loop, lets in-flight copies land, frees TMEM and
+// returns; the host reports GTMOE_ETIMEOUT.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <stdlib.h>
+
 #include "handle.h"
 
 namespace gtmoe {
 
-bool tc_supported(const gtmoe_handle *, int64_t) { return false; }
-int tc_prepare(gtmoe_handle *, TcWeights &) { return 0; }
-int launch_grouped_tc(gtmoe_handle *, TcWeights &, const TcArgs &, cudaStream_t) {
-    return fail(GTMOE_EINVAL, "tensor-core path not available");
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kBK = 64;                 // K elements per stage (128 bytes of bf16)
+constexpr int kBM = kTcBM;              // 128 rows
+constexpr int kBN = 256;                // columns per tile
+constexpr int kATileBytes = kBM * kBK * 2;  // 16 KB
+constexpr int kBTileBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kNumDequantWarps = 8;
+constexpr int kNumThreads = (6 + kNumDequantWarps) * 32;  // 448
+constexpr int kTmemCols = 512;
+constexpr int kSmemBytes = kStages * (kATileBytes + kBTileBytes) + 1024 /*align*/ + 256 /*barriers*/;
+
+// instruction descriptor: D f32, A bf16, B bf16, both K-major, N=256, M=128
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+struct TcKernelArgs {
+    const Group *groups;
+    const int64_t *tile_prefix;
+    const ExpertLayers *experts;
+    int n_groups;
+    int K;          // reduction length (d for GATED, h for DOWN)
+    int n_out;      // output features (h for GATED, d for DOWN)
+    int clamped;
+    float clamp_limit;
+    __nv_bfloat16 *out;  // hp (GATED) or yp (DOWN)
+    int *err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
-void tc_release(TcWeights &) {}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t tx) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(tx) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; false when it gave up (timeout or another role aborted).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err,
+                                          int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        for (int i = 0; i < 32; i++)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicCAS(err, 0, code);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address
+    d |= (uint64_t)1 << 16;                    // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset: 8 rows x 128 B
+    d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// Work unit u -> (group, n-tile, m-tile); m-tiles innermost so that
+// neighbouring CTAs share one weight tile in L2.
+struct Unit {
+    int g;
+    int nt;
+    int64_t mt;
+};
+__device__ __forceinline__ Unit decode_unit(int64_t u, const int64_t *__restrict__ prefix, int n_groups, int n_tiles) {
+    int lo = 0, hi = n_groups - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (__ldg(prefix + mid) * n_tiles <= u) lo = mid;
+        else hi = mid - 1;
+    }
+    Unit w;
+    w.g = lo;
+    const int64_t mt_g = __ldg(prefix + lo + 1) - __ldg(prefix + lo);
+    const int64_t r = u - __ldg(prefix + lo) * n_tiles;
+    w.nt = (int)(r / mt_g);
+    w.mt = r % mt_g;
+    return w;
+}
+
+// Raw compressed weights of one dequantisation step for one thread: 4 items
+// of (row, 16-value block).
+template <int PREC>
+struct Raw {
+    uint4 c[4];  // Int8: 16 codes; FP4: .x/.y hold 16 codes
+    float s[4];
+};
+
+template <int PREC, bool GATED>
+__device__ __forceinline__ void load_raw(Raw<PREC> &raw, const ExpertLayers &L, int n0, int kb, int K, int tid) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int item = tid + i * (kNumDequantWarps * 32);
+        const int r = item >> 2;    // 0..255 row of the B tile
+        const int b = item & 3;     // 16-value block within the 64-wide k-step
+        int which, row;
+        if (GATED) {
+            which = r < 128 ? 0 : 1;
+            row = n0 + (r & 127);
+        } else {
+            which = 2;
+            row = n0 + r;
+        }
+        const int k = kb * kBK + b * 16;
+        const float *sp = L.s[which] + (int64_t)row * (K / 16) + (k >> 4);
+        raw.s[i] = __ldg(sp);
+        if (PREC == GTMOE_INT8) {
+            const int8_t *cp = (const int8_t *)L.w[which] + (int64_t)row * K + k;
+            raw.c[i] = __ldg((const uint4 *)cp);
+        } else {
+            const uint8_t *cp = (const uint8_t *)L.w[which] + (int64_t)row * (K / 2) + (k >> 1);
+            uint2 v = __ldg((const uint2 *)cp);
+            raw.c[i] = make_uint4(v.x, v.y, 0, 0);
+        }
+    }
+}
+
+template <int PREC>
+__device__ __forceinline__ void store_dequant(const Raw<PREC> &raw, uint8_t *btile, int tid) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int item = tid + i * (kNumDequantWarps * 32);
+        const int r = item >> 2;
+        const int b = item & 3;
+        const float s = raw.s[i];
+        uint32_t w[8];
+        if (PREC == GTMOE_INT8) {
+            const uint32_t in[4] = {raw.c[i].x, raw.c[i].y, raw.c[i].z, raw.c[i].w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const uint32_t v = in[q];
+                const float f0 = (float)(int8_t)(v & 0xff) * s;
+                const float f1 = (float)(int8_t)((v >> 8) & 0xff) * s;
+                const float f2 = (float)(int8_t)((v >> 16) & 0xff) * s;
+                const float f3 = (float)(int8_t)(v >> 24) * s;
+                w[2 * q] = pack_bf16(f0, f1);
+                w[2 * q + 1] = pack_bf16(f2, f3);
+            }
+        } else {
+            const uint32_t in[2] = {raw.c[i].x, raw.c[i].y};
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                const uint32_t v = in[q];
+#pragma unroll
+                for (int bb = 0; bb < 4; bb++) {
+                    const uint32_t byte = (v >> (8 * bb)) & 0xff;
+                    // low nibble = even element (lowprecision/rows.go:68-74)
+                    w[4 * q + bb] = pack_bf16(fp4_value(byte & 15u) * s, fp4_value(byte >> 4) * s);
+                }
+            }
+        }
+        // 16 values = 2 chunks of 16 B: logical chunks 2b, 2b+1 of row r,
+        // placed at chunk ^ (r & 7) (SWIZZLE_128B)
+        uint8_t *row = btile + r * 128;
+        const int c0 = (2 * b) ^ (r & 7), c1 = (2 * b + 1) ^ (r & 7);
+        *reinterpret_cast<uint4 *>(row + c0 * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(row + c1 * 16) = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+}
+
+template <int PREC, bool GATED>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    grouped_tc_kernel(const __grid_constant__ CUtensorMap amap, const TcKernelArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *a_tiles = smem;
+    uint8_t *b_tiles = smem + kStages * kATileBytes;
+    uint64_t *bars = (uint64_t *)(smem + kStages * (kATileBytes + kBTileBytes));
+    uint64_t *full_a = bars;                 // [kStages]
+    uint64_t *full_b = bars + kStages;       // [kStages]
+    uint64_t *empty = bars + 2 * kStages;    // [kStages]
+    uint64_t *tmem_full = bars + 3 * kStages;   // [2]
+    uint64_t *tmem_empty = bars + 3 * kStages + 2;  // [2]
+    uint32_t *tmem_slot = (uint32_t *)(bars + 3 * kStages + 4);
+    volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n_tiles = GATED ? a.n_out / 128 : a.n_out / kBN;  // GATED: 128 gate + 128 up features per tile
+    const int64_t total = __ldg(a.tile_prefix + a.n_groups) * n_tiles;
+    const int KB = a.K / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full_a[s], 1);
+            mbar_init(&full_b[s], kNumDequantWarps);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tmem_full[b], 1);
+            mbar_init(&tmem_empty[b], 4);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer of the activation tiles
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&amap) : "memory");
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+                const Unit w = decode_unit(u, a.tile_prefix, a.n_groups, n_tiles);
+                const Group grp = a.groups[w.g];
+                const int row0 = (int)((GATED ? grp.x_row0 : grp.h_row0) + w.mt * kBM);
+                for (int kb = 0; kb < KB; kb++) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err, 1)) break;
+                    mbar_arrive_expect_tx(&full_a[stage], kATileBytes);
+                    tma_load_2d(a_tiles + stage * kATileBytes, &amap, kb * kBK, row0, &full_a[stage]);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (*abort_flag) {
+                // let copies already issued land before the CTA can exit
+                const uint64_t t0 = global_timer_ns();
+                while (global_timer_ns() - t0 < 1000000ull) {
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+                if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, a.err, 2)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kBN);
+                bool ok = true;
+                for (int kb = 0; kb < KB; kb++) {
+                    if (!mbar_wait(&full_a[stage], phase, abort_flag, a.err, 3) ||
+                        !mbar_wait(&full_b[stage], phase, abort_flag, a.err, 4)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t adesc = sw128_desc(smem_u32(a_tiles + stage * kATileBytes));
+                    const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + stage * kBTileBytes));
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)
+                        umma_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), (kb | k) != 0);
+                    umma_commit(&empty[stage]);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tmem_full[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+        }
+    } else if (warp < 6) {
+        // ---------------- epilogue: TMEM -> registers -> global
+        const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+        const int row_in_tile = quad * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+            const Unit w = decode_unit(u, a.tile_prefix, a.n_groups, n_tiles);
+            const Group grp = a.groups[w.g];
+            const ExpertLayers L = a.experts[grp.expert];
+            if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, a.err, 5)) break;
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * kBN);
+            const int64_t m_left = grp.m - w.mt * kBM;
+            const bool valid = row_in_tile < m_left;
+            __nv_bfloat16 *dst = a.out + (grp.h_row0 + w.mt * kBM + row_in_tile) * (int64_t)a.n_out;
+            if (GATED) {
+                const int f0 = w.nt * 128;
+                const float *bg = L.b32[0];
+                const float *bu = L.b32[1];
+#pragma unroll 1
+                for (int c = 0; c < 128; c += 16) {
+                    uint32_t g[16], up[16];
+                    tmem_ld16(t_row + c, g);
+                    tmem_ld16(t_row + 128 + c, up);
+                    tmem_ld_wait();
+                    uint32_t o[8];
+#pragma unroll
+                    for (int j = 0; j < 16; j += 2) {
+                        float hv[2];
+#pragma unroll
+                        for (int q = 0; q < 2; q++) {
+                            float gv = __uint_as_float(g[j + q]) + (bg ? __ldg(bg + f0 + c + j + q) : 0.f);
+                            float uv = __uint_as_float(up[j + q]) + (bu ? __ldg(bu + f0 + c + j + q) : 0.f);
+                            hv[q] = gate_act<float>(gv, a.clamped, a.clamp_limit) *
+                                    up_act<float>(uv, a.clamped, a.clamp_limit);
+                        }
+                        o[j / 2] = pack_bf16(hv[0], hv[1]);
+                    }
+                    if (valid) {
+                        uint4 *p = reinterpret_cast<uint4 *>(dst + f0 + c);
+                        p[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                        p[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                    }
+                }
+            } else {
+                const int f0 = w.nt * kBN;
+                const float *bd = L.b32[2];
+#pragma unroll 1
+                for (int c = 0; c < kBN; c += 16) {
+                    uint32_t y[16];
+                    tmem_ld16(t_row + c, y);
+                    tmem_ld_wait();
+                    uint32_t o[8];
+#pragma unroll
+                    for (int j = 0; j < 16; j += 2) {
+                        float y0 = __uint_as_float(y[j]) + (bd ? __ldg(bd + f0 + c + j) : 0.f);
+                        float y1 = __uint_as_float(y[j + 1]) + (bd ? __ldg(bd + f0 + c + j + 1) : 0.f);
+                        o[j / 2] = pack_bf16(y0, y1);
+                    }
+                    if (valid) {
+                        uint4 *p = reinterpret_cast<uint4 *>(dst + f0 + c);
+                        p[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                        p[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    } else {
+        // ---------------- dequantisation of the weight tiles
+        const int tid = threadIdx.x - 6 * 32;
+        int stage = 0;
+        uint32_t phase = 0;
+        int64_t u = blockIdx.x;
+        int kb = 0;
+        Raw<PREC> cur, nxt;
+        ExpertLayers L{};
+        int n0 = 0;
+        auto setup_unit = [&](int64_t uu, ExpertLayers &LL, int &nn0) {
+            const Unit w = decode_unit(uu, a.tile_prefix, a.n_groups, n_tiles);
+            const Group grp = a.groups[w.g];
+            LL = a.experts[grp.expert];
+            nn0 = GATED ? w.nt * 128 : w.nt * kBN;
+        };
+        if (u < total) {
+            setup_unit(u, L, n0);
+            load_raw<PREC, GATED>(cur, L, n0, 0, a.K, tid);
+        }
+        while (u < total && !*abort_flag) {
+            // prefetch the next step's raw weights
+            int64_t un = u;
+            int kbn = kb + 1;
+            ExpertLayers Ln = L;
+            int n0n = n0;
+            if (kbn == KB) {
+                kbn = 0;
+                un = u + gridDim.x;
+                if (un < total) setup_unit(un, Ln, n0n);
+            }
+            if (un < total) load_raw<PREC, GATED>(nxt, Ln, n0n, kbn, a.K, tid);
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err, 6)) break;
+            store_dequant<PREC>(cur, b_tiles + stage * kBTileBytes, tid);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_b[stage]);
+            if (++stage == kStages) {
+                stage = 0;
+                phase ^= 1;
+            }
+            u = un;
+            kb = kbn;
+            L = Ln;
+            n0 = n0n;
+            cur = nxt;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+int make_act_map(CUtensorMap *map, const void *base, int64_t rows, int K) {
+    auto enc = get_encode();
+    if (!enc) return fail(GTMOE_ECUDA, "cuTensorMapEncodeTiled is not available");
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(rows > 0 ? rows : 1)};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GTMOE_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
+template <int PREC, bool GATED>
+int launch_one(const CUtensorMap &map, const TcKernelArgs &ka, int sms, cudaStream_t st) {
+    auto kern = grouped_tc_kernel<PREC, GATED>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        attr_set = true;
+    }
+    kern<<<sms, kNumThreads, kSmemBytes, st>>>(map, ka);
+    GT_CUDA(cudaGetLastError());
+    note_launches(1);
+    return 0;
+}
+
+}  // namespace
+
+bool tc_supported(const gtmoe_handle *h, int64_t T) {
+    const gtmoe_config &c = h->cfg;
+    if (c.weight_precision != GTMOE_INT8 && c.weight_precision != GTMOE_FP4) return false;
+    if (c.d_model % kBN != 0 || c.hidden % 128 != 0) return false;
+    if (T <= 0) return false;
+    if (getenv("GTMOE_DISABLE_TC")) return false;
+    return true;
+}
+
+int tc_prepare(gtmoe_handle *h, TcWeights &w) {
+    if (!w.err) {
+        GT_CUDA(cudaMalloc(&w.err, sizeof(int)));
+        GT_CUDA(cudaMemset(w.err, 0, sizeof(int)));
+    }
+    int dev = 0;
+    GT_CUDA(cudaGetDevice(&dev));
+    GT_CUDA(cudaDeviceGetAttribute(&w.sms, cudaDevAttrMultiProcessorCount, dev));
+    w.ready = 1;
+    (void)h;
+    return 0;
+}
+
+int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, cudaStream_t st) {
+    const gtmoe_config &c = h->cfg;
+    CUtensorMap xmap, hmap;
+    GT_CHECK(make_act_map(&xmap, ta.xp, ta.rows_x, c.d_model));
+    GT_CHECK(make_act_map(&hmap, ta.hp, ta.rows_h, c.hidden));
+    TcKernelArgs ka;
+    ka.groups = ta.groups;
+    ka.tile_prefix = ta.tile_prefix;
+    ka.experts = h->table.as<ExpertLayers>();
+    ka.n_groups = ta.n_groups;
+    ka.clamped = c.clamped;
+    ka.clamp_limit = (float)c.clamp_limit;
+    ka.err = w.err;
+    const int prec = c.weight_precision;
+
+    GT_CHECK(h->phase_begin(3));
+    ka.K = c.d_model;
+    ka.n_out = c.hidden;
+    ka.out = (__nv_bfloat16 *)ta.hp;
+    if (prec == GTMOE_INT8) GT_CHECK((launch_one<GTMOE_INT8, true>(xmap, ka, w.sms, st)));
+    else GT_CHECK((launch_one<GTMOE_FP4, true>(xmap, ka, w.sms, st)));
+    GT_CHECK(h->phase_end(3));
+
+    GT_CHECK(h->phase_begin(4));
+    ka.K = c.hidden;
+    ka.n_out = c.d_model;
+    ka.out = (__nv_bfloat16 *)ta.yp;
+    if (prec == GTMOE_INT8) GT_CHECK((launch_one<GTMOE_INT8, false>(hmap, ka, w.sms, st)));
+    else GT_CHECK((launch_one<GTMOE_FP4, false>(hmap, ka, w.sms, st)));
+    GT_CHECK(h->phase_end(4));
+    return 0;
+}
+
+int tc_check_error(TcWeights &w) {
+    if (!w.err) return 0;
+    int v = 0;
+    GT_CUDA(cudaMemcpy(&v, w.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v != 0) {
+        cudaMemset(w.err, 0, sizeof(int));
+        return fail(GTMOE_ETIMEOUT, "tensor-core expert kernel gave up waiting (barrier %d); results are invalid", v);
+    }
+    return 0;
+}
+
+void tc_release(TcWeights &w) {
+    if (w.err) cudaFree(w.err);
+    w.err = nullptr;
+}
 
 }  // namespace gtmoe

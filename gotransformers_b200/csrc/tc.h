@@ -14,6 +14,8 @@ constexpr int kTcBM = 128;  // rows (tokens) per tile
 
 struct TcWeights {
     int ready = 0;
+    int sms = 148;
+    int *err = nullptr;  // device flag: nonzero when a bounded wait expired
 };
 
 struct TcArgs {
@@ -30,5 +32,7 @@ bool tc_supported(const gtmoe_handle *h, int64_t T);
 int tc_prepare(gtmoe_handle *h, TcWeights &w);
 int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &a, cudaStream_t st);
 void tc_release(TcWeights &w);
+// GTMOE_ETIMEOUT (and clears the flag) if a kernel recorded an expired wait.
+int tc_check_error(TcWeights &w);
 
 }  // namespace gtmoe

@@ -28,8 +28,11 @@ CASES = {
     "one expert": dict(T=5, d=16, h=16, n_shared=0, n_routed=1, k=1, precision=O.FLOAT32),
     "one token": dict(T=1, d=64, h=64, n_shared=1, n_routed=16, k=4, precision=O.INT8),
     "many experts": dict(T=300, d=64, h=64, n_shared=1, n_routed=96, k=8, precision=O.FP4),
-    "tc shapes int8": dict(T=700, d=256, h=192, n_shared=1, n_routed=8, k=2, precision=O.INT8),
-    "tc shapes fp4": dict(T=513, d=128, h=256, n_shared=0, n_routed=6, k=3, precision=O.FP4, x_bf16=True),
+    "tc shapes int8": dict(T=700, d=256, h=384, n_shared=1, n_routed=8, k=2, precision=O.INT8),
+    "tc shapes fp4": dict(T=513, d=512, h=256, n_shared=0, n_routed=6, k=3, precision=O.FP4, x_bf16=True),
+    "tc bias clamped": dict(T=300, d=256, h=128, n_shared=1, n_routed=5, k=2, precision=O.FP4, layer_bias=0.3,
+                            clamped=True, clamp_limit=0.7),
+    "tc one token": dict(T=1, d=256, h=256, n_shared=1, n_routed=16, k=4, precision=O.INT8),
     "f32 biases": dict(T=40, d=64, h=48, n_shared=1, n_routed=5, k=2, precision=O.FLOAT32, layer_bias=0.2),
     "compressed router": dict(T=50, d=64, h=32, n_shared=0, n_routed=8, k=2, precision=O.INT8,
                               router_precision=O.INT8),
@@ -131,6 +134,22 @@ def test_one_row_matches_many_rows_bitwise():
             one = m.forward(x[t : t + 1], ids[t : t + 1])
             assert np.array_equal(one[0], many[t])
         m.close()
+
+
+@pytest.mark.parametrize("prec", [O.INT8, O.FP4])
+def test_tensor_core_path_matches_simt_path(prec, monkeypatch):
+    """The tcgen05 kernels (bf16 operands) against the SIMT kernels (float32)
+    on identical weights: same routing, outputs within the bf16 tolerance."""
+    spec, x, ids = make_case(T=1000, d=512, h=384, n_shared=1, n_routed=12, k=3, precision=prec, seed=4,
+                             x_bf16=True, layer_bias=0.05)
+    m = gpu_moe(spec)
+    tc = m.forward(x, ids)
+    monkeypatch.setenv("GTMOE_DISABLE_TC", "1")
+    simt = m.forward(x, ids)
+    assert rel_l2(tc, simt) <= 1e-2
+    ref = O.moe_forward(spec, x, ids, threads=8)["out"]
+    assert rel_l2(tc, ref) <= TOL[prec]
+    m.close()
 
 
 def test_empty_batch():
