@@ -305,7 +305,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     da.slot_row = h->slot_row.as<int64_t>();
     da.groups = h->groups.as<Group>();
     da.tile_prefix = h->tile_prefix.as<int64_t>();
-    da.bm = use_tc ? kTcBM : kSimtBM;
+    da.bm = use_tc ? tc_tile_rows(h->tc) : kSimtBM;
     GT_CHECK(h->phase_begin(1));
     GT_CHECK(launch_dispatch(da, st));
     GT_CHECK(h->phase_end(1));

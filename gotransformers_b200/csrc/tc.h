@@ -10,11 +10,10 @@ struct gtmoe_handle;
 
 namespace gtmoe {
 
-constexpr int kTcBM = 128;  // rows (tokens) per tile
-
 struct TcWeights {
     int ready = 0;
     int sms = 148;
+    int mh = 2, bn = 128, bm = 256;  // tile: mh x 128 rows, bn columns
     int *err = nullptr;  // device flag: nonzero when a bounded wait expired
 };
 
@@ -29,6 +28,7 @@ struct TcArgs {
 };
 
 bool tc_supported(const gtmoe_handle *h, int64_t T);
+int tc_tile_rows(TcWeights &w);  // m-tile height of the current shape
 int tc_prepare(gtmoe_handle *h, TcWeights &w);
 int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &a, cudaStream_t st);
 void tc_release(TcWeights &w);
