@@ -203,6 +203,21 @@ static void decode_rows_host(int precision, int rows, int width, const void *val
         }
 }
 
+// bf16 round-to-nearest-even of a float, and back.
+static uint16_t bf16_bits(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);  // NaN
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+static double bf16_value(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return (double)f;
+}
+
 static int all_layers_set(const gtmoe_handle *h) {
     for (size_t i = 0; i < h->layers.size(); i++)
         if (!h->layers[i].set) {
@@ -281,7 +296,12 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     ra.w64 = h->wr64.as<double>();
     ra.bias = h->br.as<double>();
     ra.balance = h->bal.as<double>();
-    ra.thresh_scale = 32.0 * ldexp(1.0, -24) * h->wmax;
+    ra.use_tc = !c.hash_routing && h->wr3.p && router_tc_usable(x_dev, x_dtype, T, d);
+    ra.thresh_scale = (ra.use_tc ? kRouterTcErr : kRouterSimtErr) * h->wmax;
+    ra.w3 = h->wr3.p;
+    ra.e_pad = h->e_pad;
+    ra.err = h->tc.err;
+    ra.sms = h->tc.sms;
     ra.logits = h->logits.as<double>();
     ra.chosen = h->chosen.as<int32_t>();
     ra.gates64 = h->gates64.as<double>();
@@ -399,7 +419,7 @@ void gtmoe_destroy(gtmoe_t h) {
             L.b32.release();
             L.b64.release();
         }
-        DevBuf *bufs[] = {&h->wr64, &h->wr32, &h->br, &h->bal, &h->table, &h->x_in, &h->ids, &h->logits,
+        DevBuf *bufs[] = {&h->wr64, &h->wr32, &h->wr3, &h->br, &h->bal, &h->table, &h->x_in, &h->ids, &h->logits,
                           &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load, &h->offsets, &h->perm,
                           &h->slot_row, &h->groups, &h->tile_prefix, &h->xp, &h->hp, &h->yp, &h->out_dev,
                           &h->res_dev, &h->fixups};
@@ -451,6 +471,21 @@ int gtmoe_set_router(gtmoe_t h, int precision, const void *values, const float *
         GT_CHECK(to_host(hb, bias, sizeof(double) * E));
         memcpy(b.data(), hb.data(), sizeof(double) * E);
     }
+    // bf16 split w = hi + mid + lo (+ residual below 2^-24 |w|) for the
+    // tensor-core router, rows padded with zeros to a multiple of 128
+    const int e_pad = (E + 127) / 128 * 128;
+    std::vector<uint16_t> w3((size_t)3 * e_pad * d, 0);
+    for (int e = 0; e < E; e++)
+        for (int i = 0; i < d; i++) {
+            double r = w64[(size_t)e * d + i];
+            for (int t = 0; t < 3; t++) {
+                uint16_t b = bf16_bits((float)r);
+                w3[((size_t)t * e_pad + e) * d + i] = b;
+                r -= bf16_value(b);
+            }
+        }
+    GT_CHECK(upload(h->wr3, w3.data(), sizeof(uint16_t) * w3.size(), h->stream));
+    h->e_pad = e_pad;
     GT_CHECK(upload(h->wr64, w64.data(), sizeof(double) * w64.size(), h->stream));
     GT_CHECK(upload(h->wr32, w32.data(), sizeof(float) * w32.size(), h->stream));
     GT_CHECK(upload(h->br, b.data(), sizeof(double) * E, h->stream));

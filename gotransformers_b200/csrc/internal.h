@@ -26,7 +26,12 @@ struct RouterArgs {
     const double *w64;          // E x d
     const double *bias;         // E
     const double *balance;      // E
-    double thresh_scale;        // 32 * 2^-24 * max_e ||w_e||
+    double thresh_scale;        // score margin per unit ||x_t||: 2 * 0.5 * (logit error bound) / ||x_t||
+    int use_tc;                 // logits on the tensor cores (router_tc.cu)
+    const void *w3;             // 3 x E_pad x d bf16 split of w64 (tensor-core path)
+    int e_pad;
+    int *err;                   // bounded-wait error flag
+    int sms;
     double *logits;             // T x E scratch
     int32_t *chosen;            // T x k
     double *gates64;            // T x k
@@ -34,6 +39,12 @@ struct RouterArgs {
     int *n_fixups;              // counter of tokens re-selected in float64
 };
 int launch_router(const RouterArgs &a, cudaStream_t st);
+bool router_tc_usable(const void *x, int x_dtype, int64_t T, int d);
+int launch_router_logits_tc(const void *x, int64_t T, int d, int E, int E_pad, const void *w3, double *logits,
+                            int *err, int sms, cudaStream_t st);
+// Logit error bounds (relative to ||x_t|| * max_e ||w_e||) of the two paths.
+constexpr double kRouterSimtErr = 32.0 / 16777216.0;  // 32 * 2^-24
+constexpr double kRouterTcErr = 70.0 / 8388608.0;     // 70 * 2^-23
 
 // Dispatch: builds the token-ascending permutation of (token, slot) pairs by
 // expert (rowsForExpert, mixtureofexperts.go:175-180) and the group table.

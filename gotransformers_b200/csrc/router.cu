@@ -3,12 +3,14 @@
 // (:88-96, :142-152).
 //
 // Selection must reproduce the reference's float64 choice exactly.  The
-// logits are first computed from float32 operands (float32 products summed
-// per 16-element block, block sums accumulated in float64).  For token t the
-// error of every logit is below eps_t = 32 * 2^-24 * ||x_t|| * max_e ||w_e||
-// (Cauchy-Schwarz bounds sum |x_i w_i|), and |d affinity / d logit| < 0.5, so a
-// score moves by less than 0.5 * eps_t.  If the gap between the k-th and the
-// (k+1)-th score exceeds 2 * 0.5 * eps_t the chosen set is the reference's;
+// logits are first computed either here from float32 operands (float32
+// products summed per 16-element block, block sums accumulated in float64;
+// error below eps_t = 32 * 2^-24 * ||x_t|| * max_e ||w_e||, Cauchy-Schwarz
+// bounding sum |x_i w_i|) or, for bf16 activations, on the tensor cores
+// (router_tc.cu; eps_t = 70 * 2^-23 * ||x_t|| * max_e ||w_e||).  As
+// |d affinity / d logit| < 0.5, a score moves by less than 0.5 * eps_t.  If
+// the gap between the k-th and the (k+1)-th score exceeds 2 * 0.5 * eps_t the
+// chosen set is the reference's;
 // otherwise the warp recomputes that token's logits in float64 in the
 // reference's summation order, with separately rounded multiplies and adds
 // (one sequential sum per expert, as vectormath.DotProduct, vector.go:67-74),
@@ -252,6 +254,15 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
     }
     dim3 grid((unsigned)((a.T + kRouterTile - 1) / kRouterTile), (unsigned)((a.E + kRouterTile - 1) / kRouterTile));
     unsigned sel_blocks = (unsigned)((a.T * 32 + 255) / 256);
+    if (a.use_tc) {
+        GT_CHECK(launch_router_logits_tc(a.x, a.T, a.d, a.E, a.e_pad, a.w3, a.logits, a.err, a.sms, st));
+        router_select_kernel<GTMOE_DTYPE_BF16><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E,
+                                                                           a.k, a.x, a.d, a.w64, a.thresh_scale,
+                                                                           a.chosen, a.gates64, a.gates32, a.n_fixups);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+        return 0;
+    }
     switch (a.x_dtype) {
     case GTMOE_DTYPE_F64:
         router_logits_kernel<GTMOE_DTYPE_F64><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);

@@ -3,6 +3,8 @@
 Expert indices, the token permutation and the per-expert load must match the
 oracle exactly; gates to 1e-6 relative; the output within the north star's
 rel-L2 bound (1e-5 Float32/Float64, 2e-2 Int8/FP4)."""
+import os
+
 import numpy as np
 import pytest
 
@@ -97,6 +99,25 @@ def test_exact_ties_go_to_the_lower_index():
     m = gpu_moe(spec)
     out = m.forward(x, ids)
     check_against_oracle(spec, x, ids, out, m)
+    m.close()
+
+
+@pytest.mark.parametrize("E", [10, 200])
+def test_tensor_core_router_exact_with_ties(E):
+    """bf16 activations with T >= 256 take the tensor-core router; duplicated
+    router rows tie exactly and must still resolve to the lower index."""
+    spec, x, ids = make_case(T=777, d=256, h=128, n_shared=0, n_routed=E, k=3, precision=O.INT8, seed=12,
+                             x_bf16=True)
+    w = O.decode_rows(spec.router)
+    w[4] = w[2]
+    w[E - 1] = w[0]
+    spec.router = O.Layer(O.FLOAT64, E, 256, w.reshape(-1).copy(), None, np.zeros(E))
+    m = gpu_moe(spec)
+    import torch
+
+    out = m.forward(torch.from_numpy(x).to(torch.bfloat16).cuda(), ids, out_dtype=_lib.DTYPE_F32)
+    torch.cuda.synchronize()
+    check_against_oracle(spec, x, ids, out.cpu().numpy(), m)
     m.close()
 
 
@@ -244,14 +265,22 @@ def test_config_c1_full():
     m.close()
 
 
-@pytest.mark.parametrize("name", ["c2", "c4_1", "c4_8", "c4_64"])
+@pytest.mark.parametrize("name", ["c2", "c3", "c4_1", "c4_8", "c4_64", "c5"])
 def test_config_sampled(name):
     """Full-size configs: routing of every token against the oracle's router;
     the output on a seeded token sample (row independence,
     mixtureofexperts_test.go:83-100)."""
+    import torch
+
     spec, x, ids, m = config_case(name)
-    out = m.forward(x, ids)
-    r = O.moe_route(spec, x, ids, threads=8)
+    cfg = synthetic.CONFIGS[name]
+    if cfg.x_bf16:  # bf16 activations stay bf16 on the device (tensor-core router)
+        xd = torch.from_numpy(x).to(torch.bfloat16).cuda()
+        torch.cuda.synchronize()
+        out = m.forward(xd, ids, out_dtype=_lib.DTYPE_F32).cpu().numpy()
+    else:
+        out = m.forward(x, ids)
+    r = O.moe_route(spec, x, ids, threads=os.cpu_count() or 8)
     assert np.array_equal(m.last_chosen_experts, r["chosen"])
     np.testing.assert_allclose(m.last_gates, r["gates"], rtol=1e-6)
     load = np.bincount(r["chosen"].reshape(-1), minlength=spec.n_routed)
@@ -260,6 +289,6 @@ def test_config_sampled(name):
     assert np.array_equal(m.last_rows_for_expert, perm)
     rng = np.random.default_rng(0)
     sample = np.sort(rng.choice(x.shape[0], size=min(64, x.shape[0]), replace=False))
-    ref = O.moe_forward(spec, x[sample], ids[sample], threads=8)["out"]
+    ref = O.moe_forward(spec, x[sample], ids[sample], threads=os.cpu_count() or 8)["out"]
     assert rel_l2(out[sample], ref) <= TOL[spec.experts[0][0].precision]
     m.close()
