@@ -281,6 +281,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     GT_CHECK(h->hp.ensure(cs * (size_t)rows_h * hd));
     GT_CHECK(h->yp.ensure(cs * (size_t)rows_h * d));
     GT_CHECK(h->fixups.ensure(sizeof(int)));
+    GT_CHECK(h->flagged.ensure(sizeof(int) * (size_t)(T > 0 ? T : 1)));
     GT_CHECK(refresh_table(h));
 
     RouterArgs ra;
@@ -307,8 +308,8 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     ra.gates64 = h->gates64.as<double>();
     ra.gates32 = h->gates32.as<float>();
     ra.n_fixups = h->fixups.as<int>();
+    ra.flagged = h->flagged.as<int>();
     GT_CHECK(h->phase_begin(0));
-    GT_CUDA(cudaMemsetAsync(h->fixups.p, 0, sizeof(int), st));
     GT_CHECK(launch_router(ra, st));
     GT_CHECK(h->phase_end(0));
 
@@ -422,7 +423,7 @@ void gtmoe_destroy(gtmoe_t h) {
         DevBuf *bufs[] = {&h->wr64, &h->wr32, &h->wr3, &h->br, &h->bal, &h->table, &h->x_in, &h->ids, &h->logits,
                           &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load, &h->offsets, &h->perm,
                           &h->slot_row, &h->groups, &h->tile_prefix, &h->xp, &h->hp, &h->yp, &h->out_dev,
-                          &h->res_dev, &h->fixups};
+                          &h->res_dev, &h->fixups, &h->flagged};
         for (DevBuf *b : bufs) b->release();
         for (auto &pe : h->tev)
             for (int i = 0; i < GTMOE_N_PHASES; i++) {

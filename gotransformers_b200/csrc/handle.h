@@ -78,7 +78,7 @@ struct gtmoe_handle {
 
     // per-call workspace
     DevBuf x_in, ids, logits, chosen, gates64, gates32, counts, load, offsets, perm, slot_row, groups, tile_prefix, xp,
-        hp, yp, out_dev, res_dev, fixups;
+        hp, yp, out_dev, res_dev, fixups, flagged;
     int have_load = 0;
     int64_t last_T = 0;
     int last_fixups = 0;

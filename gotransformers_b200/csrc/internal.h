@@ -37,6 +37,7 @@ struct RouterArgs {
     double *gates64;            // T x k
     float *gates32;             // T x k
     int *n_fixups;              // counter of tokens re-selected in float64
+    int *flagged;               // T: tokens whose choice the fix-up kernel settles
 };
 int launch_router(const RouterArgs &a, cudaStream_t st);
 bool router_tc_usable(const void *x, int x_dtype, int64_t T, int d);

@@ -101,20 +101,19 @@ __device__ __forceinline__ double affinity_d(double logit) {
     return sqrt(sp);
 }
 
-constexpr int kMaxPerLane = kMaxRoutedExperts / 32;
-
-// Picks `count` experts by descending score, ties to the lower index (the
-// first k of sort.SliceStable, mixtureofexperts.go:106-109).
-__device__ __forceinline__ void warp_top(const double (&score)[kMaxPerLane], const double (&aff)[kMaxPerLane], int E,
-                                         int count, int *pick, double *pick_score, double *pick_aff) {
+// Picks `count` experts by descending score among those not masked, ties to
+// the lower index (the first k of sort.SliceStable, mixtureofexperts.go:106-109).
+template <int MAXJ>
+__device__ __forceinline__ void warp_top(const double (&score)[MAXJ], const double (&aff)[MAXJ], uint32_t masked,
+                                         int E, int count, int *pick, double *pick_score, double *pick_aff) {
     const int lane = threadIdx.x & 31;
-    uint32_t taken = 0;
+    uint32_t taken = masked;
     for (int i = 0; i < count; i++) {
         double best = 0;
         int best_e = 0x7fffffff;
         double best_a = 0;
 #pragma unroll
-        for (int j = 0; j < kMaxPerLane; j++) {
+        for (int j = 0; j < MAXJ; j++) {
             int e = lane + 32 * j;
             if (e >= E || (taken >> j) & 1u) continue;
             if (best_e == 0x7fffffff || score[j] > best) {
@@ -138,23 +137,17 @@ __device__ __forceinline__ void warp_top(const double (&score)[kMaxPerLane], con
         pick[i] = best_e;
         pick_score[i] = best;
         pick_aff[i] = best_a;
-        if ((best_e & 31) == lane) taken |= 1u << (best_e >> 5);
+        if (best_e != 0x7fffffff && (best_e & 31) == lane) taken |= 1u << (best_e >> 5);
     }
 }
 
-template <int XDT>
-__global__ void __launch_bounds__(256)
-    router_select_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
-                         const double *__restrict__ balance, int64_t T, int E, int k, const void *__restrict__ x, int d,
-                         const double *__restrict__ w64, double thresh_scale, int32_t *__restrict__ chosen,
-                         double *__restrict__ gates64, float *__restrict__ gates32, int *__restrict__ n_fixups) {
-    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+template <int XDT, int MAXJ>
+__device__ __forceinline__ void load_scores(const double *__restrict__ logits, const double *__restrict__ bias,
+                                            const double *__restrict__ balance, int64_t t, int E, double (&score)[MAXJ],
+                                            double (&aff)[MAXJ]) {
     const int lane = threadIdx.x & 31;
-    if (t >= T) return;
-
-    double score[kMaxPerLane], aff[kMaxPerLane];
 #pragma unroll
-    for (int j = 0; j < kMaxPerLane; j++) {
+    for (int j = 0; j < MAXJ; j++) {
         int e = lane + 32 * j;
         score[j] = 0;
         aff[j] = 0;
@@ -164,39 +157,25 @@ __global__ void __launch_bounds__(256)
             score[j] = aff[j] + balance[e];  // mixtureofexperts.go:103-105
         }
     }
-    int pick[kMaxTopK + 1];
-    double pscore[kMaxTopK + 1], paff[kMaxTopK + 1];
-    const int count = k < E ? k + 1 : k;
-    warp_top(score, aff, E, count, pick, pscore, paff);
+}
 
-    if (k < E) {
-        double ss = 0;
-        for (int i = lane; i < d; i += 32) {
-            double v = load_as_double(x, XDT, t * d + i);
-            ss += v * v;
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        double thresh = thresh_scale * sqrt(ss);
-        if (!(pscore[k - 1] - pscore[k] > thresh)) {
-            // float64 logits in the reference's order
-#pragma unroll
-            for (int j = 0; j < kMaxPerLane; j++) {
-                int e = lane + 32 * j;
-                if (e < E) {
-                    const double *wr = w64 + (int64_t)e * d;
-                    double s = 0;
-                    for (int i = 0; i < d; i++) s = __dadd_rn(s, __dmul_rn(load_as_double(x, XDT, t * d + i), wr[i]));
-                    s = __dadd_rn(s, bias[e]);
-                    aff[j] = affinity_d(s);
-                    score[j] = aff[j] + balance[e];
-                }
-            }
-            warp_top(score, aff, E, k, pick, pscore, paff);
-            if (lane == 0) atomicAdd(n_fixups, 1);
-        }
+template <int XDT>
+__device__ __forceinline__ double warp_x_norm(const void *__restrict__ x, int64_t t, int d) {
+    const int lane = threadIdx.x & 31;
+    double ss = 0;
+    for (int i = lane; i < d; i += 32) {
+        double v = load_as_double(x, XDT, t * d + i);
+        ss += v * v;
     }
-    // sort.Ints(chosen) (mixtureofexperts.go:110)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    return sqrt(ss);
+}
+
+// sort.Ints(chosen) (mixtureofexperts.go:110) and the gates (:162-169).
+__device__ __forceinline__ void write_choice(int64_t t, int k, int *pick, double *paff, int32_t *__restrict__ chosen,
+                                             double *__restrict__ gates64, float *__restrict__ gates32) {
+    const int lane = threadIdx.x & 31;
     for (int i = 1; i < k; i++) {
         int v = pick[i];
         double a = paff[i];
@@ -209,23 +188,118 @@ __global__ void __launch_bounds__(256)
         pick[j + 1] = v;
         paff[j + 1] = a;
     }
-    // gates (mixtureofexperts.go:162-169)
     double total = 0;
     for (int i = 0; i < k; i++) total += paff[i];
     if (lane < k) {
-        int i = lane;
-        // select without dynamic register indexing of pick/paff
         int e = pick[0];
         double a = paff[0];
         for (int q = 1; q < k; q++)
-            if (q == i) {
+            if (q == lane) {
                 e = pick[q];
                 a = paff[q];
             }
         double g = a / total;
-        chosen[t * k + i] = e;
-        gates64[t * k + i] = g;
-        gates32[t * k + i] = (float)g;
+        chosen[t * k + lane] = e;
+        gates64[t * k + lane] = g;
+        gates32[t * k + lane] = (float)g;
+    }
+}
+
+// One warp per token: scores from the fast logits, top-(k+1), and either the
+// final choice or, when the k-th and (k+1)-th scores are within the error
+// margin, the token's index on the fix-up list.
+template <int XDT, int MAXJ>
+__global__ void __launch_bounds__(256)
+    router_select_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
+                         const double *__restrict__ balance, int64_t T, int E, int k, const void *__restrict__ x, int d,
+                         double thresh_scale, int32_t *__restrict__ chosen, double *__restrict__ gates64,
+                         float *__restrict__ gates32, int *__restrict__ flagged, int *__restrict__ n_flagged) {
+    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (t >= T) return;
+    double score[MAXJ], aff[MAXJ];
+    load_scores<XDT, MAXJ>(logits, bias, balance, t, E, score, aff);
+    int pick[kMaxTopK + 1];
+    double pscore[kMaxTopK + 1], paff[kMaxTopK + 1];
+    const int count = k < E ? k + 1 : k;
+    warp_top<MAXJ>(score, aff, 0u, E, count, pick, pscore, paff);
+    if (k < E) {
+        const double thresh = thresh_scale * warp_x_norm<XDT>(x, t, d);
+        if (!(pscore[k - 1] - pscore[k] > thresh)) {
+            if (lane == 0) flagged[atomicAdd(n_flagged, 1)] = (int)t;
+            return;
+        }
+    }
+    write_choice(t, k, pick, paff, chosen, gates64, gates32);
+}
+
+// One warp per flagged token.  With fast scores s^ within eps of the exact
+// ones (thresh = 2 eps), L = s^_(k) and U = s^_(k+1): an expert with
+// s^ > U + thresh is certainly chosen (only the other computed top-k experts
+// can beat it), one with s^ < L - thresh certainly not (the k computed top-k
+// experts beat it).  Only the experts in between get float64 logits, in the
+// reference's order with separately rounded products and sums (one sequential
+// sum, vectormath.DotProduct, vector.go:67-74), and fill the remaining places
+// by exact score, ties to the lower index.
+template <int XDT, int MAXJ>
+__global__ void __launch_bounds__(256)
+    router_fixup_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
+                        const double *__restrict__ balance, int E, int k, const void *__restrict__ x, int d,
+                        const double *__restrict__ w64, double thresh_scale, int32_t *__restrict__ chosen,
+                        double *__restrict__ gates64, float *__restrict__ gates32, const int *__restrict__ flagged,
+                        const int *__restrict__ n_flagged) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    const int n = *n_flagged;
+    for (int wi = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); wi < n; wi += warps) {
+        const int64_t t = flagged[wi];
+        double score[MAXJ], aff[MAXJ];
+        load_scores<XDT, MAXJ>(logits, bias, balance, t, E, score, aff);
+        int pick[kMaxTopK + 1];
+        double pscore[kMaxTopK + 1], paff[kMaxTopK + 1];
+        warp_top<MAXJ>(score, aff, 0u, E, k + 1, pick, pscore, paff);
+        const double thresh = thresh_scale * warp_x_norm<XDT>(x, t, d);
+        const double L = pscore[k - 1], U = pscore[k];
+        uint32_t sure = 0, unsure = 0;
+#pragma unroll
+        for (int j = 0; j < MAXJ; j++) {
+            const int e = lane + 32 * j;
+            if (e >= E) continue;
+            if (score[j] > U + thresh) sure |= 1u << j;
+            else if (!(score[j] < L - thresh)) unsure |= 1u << j;
+        }
+#pragma unroll
+        for (int j = 0; j < MAXJ; j++) {
+            if (!((unsure >> j) & 1u)) continue;
+            const int e = lane + 32 * j;
+            const double *wr = w64 + (int64_t)e * d;
+            double s = 0;
+            for (int i = 0; i < d; i++) s = __dadd_rn(s, __dmul_rn(load_as_double(x, XDT, t * d + i), wr[i]));
+            s = __dadd_rn(s, bias[e]);
+            aff[j] = affinity_d(s);
+            score[j] = aff[j] + balance[e];
+        }
+        int n_sure = 0;
+#pragma unroll
+        for (int j = 0; j < MAXJ; j++) n_sure += __popc(__ballot_sync(0xffffffffu, (sure >> j) & 1u));
+        // the sure experts first (any order), then the best unsure ones
+        int npick = 0;
+#pragma unroll
+        for (int j = 0; j < MAXJ; j++) {
+            uint32_t bal = __ballot_sync(0xffffffffu, (sure >> j) & 1u);
+            while (bal) {
+                const int src = __ffs(bal) - 1;
+                bal &= bal - 1;
+                const double a = __shfl_sync(0xffffffffu, aff[j], src);
+                if (npick < kMaxTopK) {
+                    pick[npick] = src + 32 * j;
+                    paff[npick] = a;
+                }
+                npick++;
+            }
+        }
+        warp_top<MAXJ>(score, aff, ~unsure, E, k - n_sure, pick + n_sure, pscore, paff + n_sure);
+        write_choice(t, k, pick, paff, chosen, gates64, gates32);
     }
 }
 
@@ -243,6 +317,37 @@ __global__ void hash_route_kernel(const int64_t *__restrict__ ids, int64_t T, in
     }
 }
 
+template <int XDT, int MAXJ>
+static int launch_select(const RouterArgs &a, cudaStream_t st) {
+    unsigned sel_blocks = (unsigned)((a.T * 32 + 255) / 256);
+    GT_CUDA(cudaMemsetAsync(a.n_fixups, 0, sizeof(int), st));
+    router_select_kernel<XDT, MAXJ><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d,
+                                                                a.thresh_scale, a.chosen, a.gates64, a.gates32,
+                                                                a.flagged, a.n_fixups);
+    GT_CUDA(cudaGetLastError());
+    if (a.k < a.E) {
+        int64_t want = (a.T * 32 + 255) / 256;
+        unsigned fix_blocks = (unsigned)(want < (int64_t)a.sms * 8 ? want : (int64_t)a.sms * 8);
+        router_fixup_kernel<XDT, MAXJ><<<fix_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.E, a.k, a.x, a.d,
+                                                                   a.w64, a.thresh_scale, a.chosen, a.gates64,
+                                                                   a.gates32, a.flagged, a.n_fixups);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+    }
+    note_launches(1);
+    return 0;
+}
+
+template <int XDT>
+static int launch_select_e(const RouterArgs &a, cudaStream_t st) {
+    if (a.E <= 32) return launch_select<XDT, 1>(a, st);
+    if (a.E <= 64) return launch_select<XDT, 2>(a, st);
+    if (a.E <= 128) return launch_select<XDT, 4>(a, st);
+    if (a.E <= 256) return launch_select<XDT, 8>(a, st);
+    if (a.E <= 512) return launch_select<XDT, 16>(a, st);
+    return launch_select<XDT, 32>(a, st);
+}
+
 int launch_router(const RouterArgs &a, cudaStream_t st) {
     if (a.T == 0) return 0;
     if (a.hash) {
@@ -252,40 +357,23 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
         note_launches(1);
         return 0;
     }
-    dim3 grid((unsigned)((a.T + kRouterTile - 1) / kRouterTile), (unsigned)((a.E + kRouterTile - 1) / kRouterTile));
-    unsigned sel_blocks = (unsigned)((a.T * 32 + 255) / 256);
     if (a.use_tc) {
         GT_CHECK(launch_router_logits_tc(a.x, a.T, a.d, a.E, a.e_pad, a.w3, a.logits, a.err, a.sms, st));
-        router_select_kernel<GTMOE_DTYPE_BF16><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E,
-                                                                           a.k, a.x, a.d, a.w64, a.thresh_scale,
-                                                                           a.chosen, a.gates64, a.gates32, a.n_fixups);
+    } else {
+        dim3 grid((unsigned)((a.T + kRouterTile - 1) / kRouterTile),
+                  (unsigned)((a.E + kRouterTile - 1) / kRouterTile));
+        if (a.x_dtype == GTMOE_DTYPE_F64)
+            router_logits_kernel<GTMOE_DTYPE_F64><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);
+        else if (a.x_dtype == GTMOE_DTYPE_F32)
+            router_logits_kernel<GTMOE_DTYPE_F32><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);
+        else
+            router_logits_kernel<GTMOE_DTYPE_BF16><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);
         GT_CUDA(cudaGetLastError());
         note_launches(1);
-        return 0;
     }
-    switch (a.x_dtype) {
-    case GTMOE_DTYPE_F64:
-        router_logits_kernel<GTMOE_DTYPE_F64><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);
-        router_select_kernel<GTMOE_DTYPE_F64><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E,
-                                                                          a.k, a.x, a.d, a.w64, a.thresh_scale,
-                                                                          a.chosen, a.gates64, a.gates32, a.n_fixups);
-        break;
-    case GTMOE_DTYPE_F32:
-        router_logits_kernel<GTMOE_DTYPE_F32><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);
-        router_select_kernel<GTMOE_DTYPE_F32><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E,
-                                                                          a.k, a.x, a.d, a.w64, a.thresh_scale,
-                                                                          a.chosen, a.gates64, a.gates32, a.n_fixups);
-        break;
-    default:
-        router_logits_kernel<GTMOE_DTYPE_BF16><<<grid, 256, 0, st>>>(a.x, a.w32, a.T, a.E, a.d, a.logits);
-        router_select_kernel<GTMOE_DTYPE_BF16><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E,
-                                                                           a.k, a.x, a.d, a.w64, a.thresh_scale,
-                                                                           a.chosen, a.gates64, a.gates32, a.n_fixups);
-        break;
-    }
-    GT_CUDA(cudaGetLastError());
-    note_launches(2);
-    return 0;
+    if (a.x_dtype == GTMOE_DTYPE_F64) return launch_select_e<GTMOE_DTYPE_F64>(a, st);
+    if (a.x_dtype == GTMOE_DTYPE_F32) return launch_select_e<GTMOE_DTYPE_F32>(a, st);
+    return launch_select_e<GTMOE_DTYPE_BF16>(a, st);
 }
 
 }  // namespace gtmoe
