@@ -242,6 +242,7 @@ static int refresh_table(gtmoe_handle *h) {
             t[e].s[w] = L.s.as<float>();
             t[e].b32[w] = L.has_bias ? L.b32.as<float>() : nullptr;
             t[e].b64[w] = L.has_bias ? L.b64.as<double>() : nullptr;
+            t[e].tiled[w] = L.tiled.as<uint8_t>();
         }
     GT_CHECK(h->table.ensure(sizeof(ExpertLayers) * n));
     GT_CUDA(cudaMemcpy(h->table.p, t.data(), sizeof(ExpertLayers) * n, cudaMemcpyHostToDevice));
@@ -415,6 +416,7 @@ void gtmoe_destroy(gtmoe_t h) {
         ep_destroy(h);
         tc_release(h->tc);
         for (auto &L : h->layers) {
+            L.tiled.release();
             L.w.release();
             L.s.release();
             L.b32.release();
@@ -568,10 +570,11 @@ int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, int precis
             L.has_bias = 1;
         }
     }
-    GT_CUDA(cudaStreamSynchronize(h->stream));
     L.precision = precision;
     L.rows = rows;
     L.width = width;
+    GT_CHECK(tc_relayout_layer(h, L, which));
+    GT_CUDA(cudaStreamSynchronize(h->stream));
     L.set = 1;
     h->table_dirty = 1;
     return 0;

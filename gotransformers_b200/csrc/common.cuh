@@ -96,6 +96,7 @@ struct ExpertLayers {
     const float *s[3];      // Int8/FP4 scales, rows*ceil(width/16)
     const float *b32[3];    // biases as float
     const double *b64[3];   // biases as double
+    const uint8_t *tiled[3];  // Int8/FP4 codes+scales re-laid in tile chunks (tensor-core path) or NULL
 };
 
 // One group of rows that run through one expert (shared or routed).

@@ -43,6 +43,7 @@ struct LayerDev {
     int set = 0;
     int precision = 0, rows = 0, width = 0;
     DevBuf w, s, b32, b64;
+    DevBuf tiled;  // tile-chunk layout of w + s for the tensor-core kernels (tc.cu)
     int has_bias = 0;
 };
 

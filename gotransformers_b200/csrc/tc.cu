@@ -5,34 +5,36 @@
 //   kernel 1 (GATED):  H = act_g(X Wg^T + bg) * act_u(X Wu^T + bu)  -> bf16
 //   kernel 2 (DOWN):   Y = H Wd^T + bd                               -> bf16
 // X / H rows of every expert are contiguous (the dispatch's expert-sorted
-// buffer).  Tiles are 128 rows x 256 columns; for kernel 1 the 256 columns are
-// 128 gate features and the same 128 up features, so each epilogue thread holds
-// both operands of its SwiGLU products in registers.
+// buffer).  A tile is 256 rows x 128 columns computed by two M=128 UMMAs that
+// share one weight tile, so every dequantised weight feeds 256 rows of MMA
+// work.  For kernel 1 the 128 columns are 64 gate features and the same 64
+// up features, so each epilogue thread holds both operands of its SwiGLU
+// products in registers.
 //
-// The Int8/FP4 weights stay compressed in HBM exactly as lowprecision.Rows
-// stores them (codes row-major, one float32 scale per 16 values of a row,
-// lowprecision/rows.go:38-79).  Dequantisation warps read them (L2-resident:
-// every weight tile is reused by all m-tiles of its expert), multiply code by
-// scale in float32 and round once to bf16 straight into the shared-memory
-// operand in the UMMA canonical K-major SWIZZLE_128B layout (Rows.Row
-// semantics, rows.go:87-119).  Activations arrive by TMA in the same layout.
-// One elected thread issues tcgen05.mma kind::f16 (bf16 x bf16 -> f32 in
-// TMEM); four epilogue warps read TMEM with tcgen05.ld.
+// The Int8/FP4 weights stay compressed in HBM: the bytes of the
+// lowprecision.Rows snapshot (codes, one float32 scale per 16 values of a
+// row; lowprecision/rows.go:38-79) are only permuted at set time into chunks
+// of (row tile, 64-wide k-block), codes then scales, so that one bulk async
+// copy moves the raw weights of one pipeline stage into shared memory.
+// Dequantisation warps turn them into bf16(code * scale) (Rows.Row semantics,
+// rows.go:87-119) straight in the UMMA canonical K-major SWIZZLE_128B layout;
+// activations arrive by TMA in the same layout.  One elected thread issues
+// tcgen05.mma kind::f16 (bf16 x bf16 -> f32 in TMEM); four epilogue warps read
+// TMEM with tcgen05.ld.
 //
 // Persistent kernel, one CTA per SM, warp roles:
-//   warp 0      TMA producer of the activation tile
+//   warp 0      TMA / bulk-copy producer (activation tile + raw weight chunks)
 //   warp 1      TMEM allocator and MMA issuer
 //   warps 2-5   epilogue (TMEM -> bias, SwiGLU -> bf16 -> global)
 //   warps 6-13  dequantisation of the weight tile
-// 4-stage shared-memory ring (48 KB per stage), 2 TMEM accumulators of 256
+// A ring of shared-memory stages (activations 32 KB, bf16 weights 16 KB, raw
+// weights 6 KB FP4 / 10 KB Int8 each) and two TMEM accumulators of 256
 // columns (the epilogue of one tile overlaps the main loop of the next).
 //
 // Every mbarrier wait is bounded (kWaitLimitNs of %globaltimer).  On expiry
 // the kernel records an error code in *err, raises a CTA-wide abort flag so
 // every role leaves its loop, lets in-flight copies land, frees TMEM and
 // returns; the host reports GTMOE_ETIMEOUT.
-#include <cuda.h>
-#include <cudaTypedefs.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -43,26 +45,29 @@ namespace gtmoe {
 
 namespace {
 
-constexpr int kStages = 4;
-constexpr int kBK = 64;                 // K elements per stage (128 bytes of bf16)
+constexpr int kBK = 64;         // K elements per stage (128 bytes of bf16)
+constexpr int kBM = 256;        // rows per tile: two M=128 UMMAs
+constexpr int kBN = 128;        // columns per tile
+constexpr int kGateRows = kBN / 2;  // gate (and up) features per kernel-1 tile
 constexpr int kNumDequantWarps = 8;
 constexpr int kDequantThreads = kNumDequantWarps * 32;
 constexpr int kNumThreads = (6 + kNumDequantWarps) * 32;  // 448
 constexpr int kTmemCols = 512;
+constexpr int kATileBytes = kBM * kBK * 2;  // 32 KB
+constexpr int kBTileBytes = kBN * kBK * 2;  // 16 KB
+constexpr int kItems = kBN * 4 / kDequantThreads;  // (row, 16-value block) items per dequant thread
+// instruction descriptor: D f32, A bf16, B bf16, both K-major, N=128, M=128
+constexpr uint32_t kIdesc =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
-// Tile shape: MH halves of 128 rows (one UMMA of M=128 each, sharing the
-// weight tile) x BN columns; two accumulators of MH*BN columns fit TMEM.
-template <int MH, int BN>
-struct Shape {
-    static_assert(MH * BN * 2 <= kTmemCols, "accumulators exceed TMEM");
-    static constexpr int kBM = 128 * MH;
-    static constexpr int kATileBytes = kBM * kBK * 2;
-    static constexpr int kBTileBytes = BN * kBK * 2;
-    static constexpr int kSmemBytes = kStages * (kATileBytes + kBTileBytes) + 1024 /*align*/ + 256 /*barriers*/;
-    static constexpr int kItems = BN * 4 / kDequantThreads;  // (row, 16-value block) items per dequant thread
-    // instruction descriptor: D f32, A bf16, B bf16, both K-major, N=BN, M=128
-    static constexpr uint32_t kIdesc =
-        (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// Raw chunk geometry: code bytes per row per k-block, chunk bytes.
+template <int PREC>
+struct Raw {
+    static constexpr int kCodeBytes = PREC == GTMOE_INT8 ? 64 : 32;
+    static constexpr int kRowBytes = kCodeBytes + 16;  // codes + 4 float scales
+    static constexpr int kStageBytes = kBN * kRowBytes;  // both chunks of kernel 1, or one of kernel 2
+    static constexpr int kStages = PREC == GTMOE_INT8 ? 3 : 4;
+    static constexpr int kSmemBytes = kStages * (kATileBytes + kBTileBytes + kStageBytes) + 1024 + 256;
 };
 
 struct TcKernelArgs {
@@ -77,6 +82,14 @@ struct TcKernelArgs {
     __nv_bfloat16 *out;  // hp (GATED) or yp (DOWN)
     int *err;
 };
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
 
 // Work unit u -> (group, n-tile, m-tile); m-tiles innermost so that
 // neighbouring CTAs share one weight tile in L2.
@@ -158,57 +171,34 @@ __device__ __forceinline__ void int8_decode4(uint32_t w, float s, uint32_t *o) {
     o[1] = pack_bf16(f2 * s, f3 * s);
 }
 
-// Raw compressed weights of one dequantisation step for one thread: kItems
-// items of (row, 16-value block).
-template <int NI>
-struct Raw {
-    uint4 c[NI];  // Int8: 16 codes; FP4: .x/.y hold 16 codes
-    float s[NI];
-};
-
-template <int PREC, bool GATED, int BN, int NI>
-__device__ __forceinline__ void load_raw(Raw<NI> &raw, const ExpertLayers &L, int n0, int kb, int K, int tid) {
+// Dequantises one stage: item (r, b) = 16 values of B-tile row r, k-block
+// quarter b.  The raw stage holds, for kernel 1, the gate chunk (rows 0..63)
+// then the up chunk (rows 64..127); for kernel 2 one chunk of 128 rows; each
+// chunk is codes [rows][kCodeBytes] then scales [rows][4].
+template <int PREC, bool GATED>
+__device__ __forceinline__ void dequant_stage(const uint8_t *raw, uint8_t *btile, int tid) {
+    using R = Raw<PREC>;
+    constexpr int CR = GATED ? kGateRows : kBN;  // rows per chunk
 #pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int item = tid + i * kDequantThreads;
-        const int r = item >> 2;    // row of the B tile
-        const int b = item & 3;     // 16-value block within the 64-wide k-step
-        int which, row;
-        if (GATED) {
-            which = r < BN / 2 ? 0 : 1;
-            row = n0 + (r & (BN / 2 - 1));
-        } else {
-            which = 2;
-            row = n0 + r;
-        }
-        const int k = kb * kBK + b * 16;
-        raw.s[i] = __ldg(L.s[which] + (int64_t)row * (K / 16) + (k >> 4));
-        if (PREC == GTMOE_INT8) {
-            raw.c[i] = __ldg((const uint4 *)((const int8_t *)L.w[which] + (int64_t)row * K + k));
-        } else {
-            const uint2 v = __ldg((const uint2 *)((const uint8_t *)L.w[which] + (int64_t)row * (K / 2) + (k >> 1)));
-            raw.c[i] = make_uint4(v.x, v.y, 0, 0);
-        }
-    }
-}
-
-template <int PREC, int NI>
-__device__ __forceinline__ void store_dequant(const Raw<NI> &raw, uint8_t *btile, int tid) {
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
+    for (int i = 0; i < kItems; i++) {
         const int item = tid + i * kDequantThreads;
         const int r = item >> 2;
         const int b = item & 3;
+        const int ch = r / CR, lr = r % CR;
+        const uint8_t *chunk = raw + ch * CR * R::kRowBytes;
+        const float s = *reinterpret_cast<const float *>(chunk + CR * R::kCodeBytes + lr * 16 + b * 4);
         uint32_t w[8];
         if (PREC == GTMOE_INT8) {
-            int8_decode4(raw.c[i].x, raw.s[i], w);
-            int8_decode4(raw.c[i].y, raw.s[i], w + 2);
-            int8_decode4(raw.c[i].z, raw.s[i], w + 4);
-            int8_decode4(raw.c[i].w, raw.s[i], w + 6);
+            const uint4 c = *reinterpret_cast<const uint4 *>(chunk + lr * R::kCodeBytes + b * 16);
+            int8_decode4(c.x, s, w);
+            int8_decode4(c.y, s, w + 2);
+            int8_decode4(c.z, s, w + 4);
+            int8_decode4(c.w, s, w + 6);
         } else {
-            const Fp4Tables t = fp4_tables(raw.s[i]);
-            fp4_decode8(raw.c[i].x, t, w);
-            fp4_decode8(raw.c[i].y, t, w + 4);
+            const uint2 c = *reinterpret_cast<const uint2 *>(chunk + lr * R::kCodeBytes + b * 8);
+            const Fp4Tables t = fp4_tables(s);
+            fp4_decode8(c.x, t, w);
+            fp4_decode8(c.y, t, w + 4);
         }
         // 16 values = logical 16-byte chunks 2b, 2b+1 of row r, placed at
         // chunk ^ (r & 7) (SWIZZLE_128B)
@@ -219,35 +209,37 @@ __device__ __forceinline__ void store_dequant(const Raw<NI> &raw, uint8_t *btile
     }
 }
 
-template <int PREC, bool GATED, int MH, int BN>
+template <int PREC, bool GATED>
 __global__ void __launch_bounds__(kNumThreads, 1)
     grouped_tc_kernel(const __grid_constant__ CUtensorMap amap, const TcKernelArgs a) {
-    using Sh = Shape<MH, BN>;
-    constexpr int kBM = Sh::kBM;
-    constexpr int NI = Sh::kItems;
+    using R = Raw<PREC>;
+    constexpr int S = R::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *a_tiles = smem;
-    uint8_t *b_tiles = smem + kStages * Sh::kATileBytes;
-    uint64_t *bars = (uint64_t *)(smem + kStages * (Sh::kATileBytes + Sh::kBTileBytes));
-    uint64_t *full_a = bars;                        // [kStages]
-    uint64_t *full_b = bars + kStages;              // [kStages]
-    uint64_t *empty = bars + 2 * kStages;           // [kStages]
-    uint64_t *tmem_full = bars + 3 * kStages;       // [2]
-    uint64_t *tmem_empty = bars + 3 * kStages + 2;  // [2]
-    uint32_t *tmem_slot = (uint32_t *)(bars + 3 * kStages + 4);
+    uint8_t *b_tiles = smem + S * kATileBytes;
+    uint8_t *raw_tiles = b_tiles + S * kBTileBytes;
+    uint64_t *bars = (uint64_t *)(raw_tiles + S * R::kStageBytes);
+    uint64_t *full_a = bars;                  // [S] activations landed
+    uint64_t *full_raw = bars + S;            // [S] raw weights landed
+    uint64_t *full_b = bars + 2 * S;          // [S] bf16 weights written
+    uint64_t *empty = bars + 3 * S;           // [S] MMAs of the stage done
+    uint64_t *tmem_full = bars + 4 * S;       // [2]
+    uint64_t *tmem_empty = bars + 4 * S + 2;  // [2]
+    uint32_t *tmem_slot = (uint32_t *)(bars + 4 * S + 4);
     volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // GATED: BN/2 gate + the same BN/2 up features per tile
-    const int n_tiles = GATED ? a.n_out / (BN / 2) : a.n_out / BN;
+    // kernel 1: kGateRows gate + the same up features per tile
+    const int n_tiles = GATED ? a.n_out / kGateRows : a.n_out / kBN;
     const int64_t total = __ldg(a.tile_prefix + a.n_groups) * n_tiles;
     const int KB = a.K / kBK;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; s++) {
+        for (int s = 0; s < S; s++) {
             mbar_init(&full_a[s], 1);
+            mbar_init(&full_raw[s], 1);
             mbar_init(&full_b[s], kNumDequantWarps);
             mbar_init(&empty[s], 1);
         }
@@ -269,20 +261,31 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA producer of the activation tiles
+        // ---------------- producer: activation tile (TMA) + raw weight chunks (bulk)
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&amap) : "memory");
             int stage = 0;
             uint32_t phase = 0;
+            const int chunk_rows = GATED ? kGateRows : kBN;
+            const size_t chunk_bytes = (size_t)chunk_rows * R::kRowBytes;
             for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
                 const Unit w = decode_unit(u, a.tile_prefix, a.n_groups, n_tiles);
                 const Group grp = a.groups[w.g];
+                const ExpertLayers &L = a.experts[grp.expert];
                 const int row0 = (int)((GATED ? grp.x_row0 : grp.h_row0) + w.mt * kBM);
+                // chunk (n-tile, k-block) of a layer sits at (nt * KB + kb) * chunk_bytes
+                const uint8_t *src0 = GATED ? L.tiled[0] : L.tiled[2];
+                const uint8_t *src1 = L.tiled[1];
                 for (int kb = 0; kb < KB; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err, 1)) break;
-                    mbar_arrive_expect_tx(&full_a[stage], Sh::kATileBytes);
-                    tma_load_2d(a_tiles + stage * Sh::kATileBytes, &amap, kb * kBK, row0, &full_a[stage]);
-                    if (++stage == kStages) {
+                    mbar_arrive_expect_tx(&full_a[stage], kATileBytes);
+                    tma_load_2d(a_tiles + stage * kATileBytes, &amap, kb * kBK, row0, &full_a[stage]);
+                    const size_t off = ((size_t)w.nt * KB + kb) * chunk_bytes;
+                    uint8_t *dst = raw_tiles + stage * R::kStageBytes;
+                    mbar_arrive_expect_tx(&full_raw[stage], R::kStageBytes);
+                    bulk_load(dst, src0 + off, (uint32_t)chunk_bytes, &full_raw[stage]);
+                    if (GATED) bulk_load(dst + chunk_bytes, src1 + off, (uint32_t)chunk_bytes, &full_raw[stage]);
+                    if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
                     }
@@ -303,16 +306,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
-                int halves = MH;
-                if (MH > 1) {
-                    // skip the second half when it holds no row of the group
-                    const Unit w = decode_unit(u, a.tile_prefix, a.n_groups, n_tiles);
-                    const int64_t m_left = a.groups[w.g].m - w.mt * kBM;
-                    halves = m_left > 128 ? MH : 1;
-                }
+                // skip the second half when it holds no row of the group
+                const Unit w = decode_unit(u, a.tile_prefix, a.n_groups, n_tiles);
+                const bool two = a.groups[w.g].m - w.mt * kBM > 128;
                 if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, a.err, 2)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * MH * BN);
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 2 * kBN);
                 bool ok = true;
                 for (int kb = 0; kb < KB; kb++) {
                     if (!mbar_wait(&full_a[stage], phase, abort_flag, a.err, 3) ||
@@ -321,18 +320,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t adesc = sw128_desc(smem_u32(a_tiles + stage * Sh::kATileBytes));
-                    const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + stage * Sh::kBTileBytes));
+                    const uint64_t adesc = sw128_desc(smem_u32(a_tiles + stage * kATileBytes));
+                    const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + stage * kBTileBytes));
 #pragma unroll
                     for (int k = 0; k < kBK / 16; k++) {
-                        umma_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), Sh::kIdesc,
+                        umma_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
                                   (kb | k) != 0);
-                        if (MH > 1 && halves > 1)
-                            umma_bf16(d_tmem + BN, adesc + (uint64_t)((128 * 128) >> 4) + (uint64_t)(2 * k),
-                                      bdesc + (uint64_t)(2 * k), Sh::kIdesc, (kb | k) != 0);
+                        if (two)
+                            umma_bf16(d_tmem + kBN, adesc + (uint64_t)((128 * 128) >> 4) + (uint64_t)(2 * k),
+                                      bdesc + (uint64_t)(2 * k), kIdesc, (kb | k) != 0);
                     }
                     umma_commit(&empty[stage]);
-                    if (++stage == kStages) {
+                    if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
                     }
@@ -353,28 +352,27 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
             const Unit w = decode_unit(u, a.tile_prefix, a.n_groups, n_tiles);
             const Group grp = a.groups[w.g];
-            const ExpertLayers L = a.experts[grp.expert];
+            const ExpertLayers &L = a.experts[grp.expert];
             if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, a.err, 5)) break;
             tc_fence_after();
             const int64_t m_left = grp.m - w.mt * kBM;
 #pragma unroll 1
-            for (int hh = 0; hh < MH; hh++) {
+            for (int hh = 0; hh < 2; hh++) {
                 if (hh > 0 && m_left <= 128) break;  // the MMA skipped this half
                 const int row_in_tile = hh * 128 + quad * 32 + lane;
                 const bool valid = row_in_tile < m_left;
                 const uint32_t t_row =
-                    tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * MH * BN + hh * BN);
+                    tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * 2 * kBN + hh * kBN);
                 __nv_bfloat16 *dst = a.out + (grp.h_row0 + w.mt * kBM + row_in_tile) * (int64_t)a.n_out;
                 if (GATED) {
-                    constexpr int HW = BN / 2;
-                    const int f0 = w.nt * HW;
+                    const int f0 = w.nt * kGateRows;
                     const float *bg = L.b32[0];
                     const float *bu = L.b32[1];
 #pragma unroll 1
-                    for (int c = 0; c < HW; c += 16) {
+                    for (int c = 0; c < kGateRows; c += 16) {
                         uint32_t g[16], up[16];
                         tmem_ld16(t_row + c, g);
-                        tmem_ld16(t_row + HW + c, up);
+                        tmem_ld16(t_row + kGateRows + c, up);
                         tmem_ld_wait();
                         uint32_t o[8];
 #pragma unroll
@@ -396,10 +394,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                         }
                     }
                 } else {
-                    const int f0 = w.nt * BN;
+                    const int f0 = w.nt * kBN;
                     const float *bd = L.b32[2];
 #pragma unroll 1
-                    for (int c = 0; c < BN; c += 16) {
+                    for (int c = 0; c < kBN; c += 16) {
                         uint32_t y[16];
                         tmem_ld16(t_row + c, y);
                         tmem_ld_wait();
@@ -431,47 +429,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int tid = threadIdx.x - 6 * 32;
         int stage = 0;
         uint32_t phase = 0;
-        int64_t u = blockIdx.x;
-        int kb = 0;
-        Raw<NI> cur, nxt;
-        ExpertLayers L{};
-        int n0 = 0;
-        auto setup_unit = [&](int64_t uu, ExpertLayers &LL, int &nn0) {
-            const Unit w = decode_unit(uu, a.tile_prefix, a.n_groups, n_tiles);
-            const Group grp = a.groups[w.g];
-            LL = a.experts[grp.expert];
-            nn0 = GATED ? w.nt * (BN / 2) : w.nt * BN;
-        };
-        if (u < total) {
-            setup_unit(u, L, n0);
-            load_raw<PREC, GATED, BN, NI>(cur, L, n0, 0, a.K, tid);
-        }
-        while (u < total && !*abort_flag) {
-            // prefetch the next step's raw weights
-            int64_t un = u;
-            int kbn = kb + 1;
-            ExpertLayers Ln = L;
-            int n0n = n0;
-            if (kbn == KB) {
-                kbn = 0;
-                un = u + gridDim.x;
-                if (un < total) setup_unit(un, Ln, n0n);
-            }
-            if (un < total) load_raw<PREC, GATED, BN, NI>(nxt, Ln, n0n, kbn, a.K, tid);
-            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err, 6)) break;
-            store_dequant<PREC, NI>(cur, b_tiles + stage * Sh::kBTileBytes, tid);
+        const int64_t units = blockIdx.x < total ? (total - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+        const int64_t steps = units * KB;  // stages this CTA runs
+        for (int64_t j = 0; j < steps && !*abort_flag; j++) {
+            if (!mbar_wait(&full_raw[stage], phase, abort_flag, a.err, 6)) break;
+            dequant_stage<PREC, GATED>(raw_tiles + stage * R::kStageBytes, b_tiles + stage * kBTileBytes, tid);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(&full_b[stage]);
-            if (++stage == kStages) {
+            if (++stage == S) {
                 stage = 0;
                 phase ^= 1;
             }
-            u = un;
-            kb = kbn;
-            L = Ln;
-            n0 = n0n;
-            cur = nxt;
         }
     }
 
@@ -483,79 +452,67 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
 }
 
-int make_act_map(CUtensorMap *map, const void *base, int64_t rows, int K, int box_rows) {
-    return encode_bf16_2d(map, base, K, rows, kBK, box_rows);
+// Re-lays one Int8/FP4 layer (rows x K, reference snapshot layout) into
+// chunks of (chunk_rows rows, 64-wide k-block): codes [rows][code bytes]
+// then scales [rows][4].  One thread per (row, k-block).
+__global__ void relayout_kernel(const uint8_t *__restrict__ codes, const float *__restrict__ scales, int rows, int K,
+                                int code_bytes, int chunk_rows, uint8_t *__restrict__ out) {
+    const int KB = K / kBK;
+    const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (item >= (int64_t)rows * KB) return;
+    const int row = (int)(item / KB), kb = (int)(item % KB);
+    const int nt = row / chunk_rows, lr = row % chunk_rows;
+    const int row_bytes = code_bytes + 16;
+    uint8_t *chunk = out + ((int64_t)nt * KB + kb) * chunk_rows * row_bytes;
+    const int64_t src_row = (int64_t)row * KB * code_bytes + (int64_t)kb * code_bytes;
+    for (int i = 0; i < code_bytes; i += 16)
+        *reinterpret_cast<uint4 *>(chunk + lr * code_bytes + i) = *reinterpret_cast<const uint4 *>(codes + src_row + i);
+    const float4 s = *reinterpret_cast<const float4 *>(scales + (int64_t)row * (K / 16) + kb * 4);
+    *reinterpret_cast<float4 *>(chunk + chunk_rows * code_bytes + lr * 16) = s;
 }
 
-template <int PREC, bool GATED, int MH, int BN>
+template <int PREC, bool GATED>
 int launch_one(const CUtensorMap &map, const TcKernelArgs &ka, int sms, cudaStream_t st) {
-    using Sh = Shape<MH, BN>;
-    auto kern = grouped_tc_kernel<PREC, GATED, MH, BN>;
+    auto kern = grouped_tc_kernel<PREC, GATED>;
     static bool attr_set = false;
     if (!attr_set) {
-        GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmemBytes));
+        GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Raw<PREC>::kSmemBytes));
         attr_set = true;
     }
-    kern<<<sms, kNumThreads, Sh::kSmemBytes, st>>>(map, ka);
+    kern<<<sms, kNumThreads, Raw<PREC>::kSmemBytes, st>>>(map, ka);
     GT_CUDA(cudaGetLastError());
     note_launches(1);
     return 0;
 }
 
-template <int MH, int BN>
-int launch_pair(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, TcKernelArgs ka, cudaStream_t st) {
-    const gtmoe_config &c = h->cfg;
-    CUtensorMap xmap, hmap;
-    GT_CHECK(make_act_map(&xmap, ta.xp, ta.rows_x, c.d_model, 128 * MH));
-    GT_CHECK(make_act_map(&hmap, ta.hp, ta.rows_h, c.hidden, 128 * MH));
-    const int prec = c.weight_precision;
-    GT_CHECK(h->phase_begin(3));
-    ka.K = c.d_model;
-    ka.n_out = c.hidden;
-    ka.out = (__nv_bfloat16 *)ta.hp;
-    if (prec == GTMOE_INT8) GT_CHECK((launch_one<GTMOE_INT8, true, MH, BN>(xmap, ka, w.sms, st)));
-    else GT_CHECK((launch_one<GTMOE_FP4, true, MH, BN>(xmap, ka, w.sms, st)));
-    GT_CHECK(h->phase_end(3));
-
-    GT_CHECK(h->phase_begin(4));
-    ka.K = c.hidden;
-    ka.n_out = c.d_model;
-    ka.out = (__nv_bfloat16 *)ta.yp;
-    if (prec == GTMOE_INT8) GT_CHECK((launch_one<GTMOE_INT8, false, MH, BN>(hmap, ka, w.sms, st)));
-    else GT_CHECK((launch_one<GTMOE_FP4, false, MH, BN>(hmap, ka, w.sms, st)));
-    GT_CHECK(h->phase_end(4));
-    return 0;
+bool shapes_ok(const gtmoe_config &c) {
+    // gate/up tiles hold 64 features of each, down tiles 128; K in steps of 64
+    return c.hidden % kGateRows == 0 && c.d_model % kBN == 0 && c.d_model % kBK == 0 && c.hidden % kBK == 0;
 }
 
 }  // namespace
-
-// Tile shapes: 256 rows x 128 columns (two M=128 UMMAs share each dequantised
-// weight tile: half the dequantisation per MMA) by default; GTMOE_TC_SHAPE=
-// 128x256 selects one M=128 x N=256 UMMA per k-slice.
-static void choose_shape(TcWeights &w) {
-    const char *e = getenv("GTMOE_TC_SHAPE");
-    if (e && strcmp(e, "128x256") == 0) {
-        w.mh = 1;
-        w.bn = 256;
-    } else {
-        w.mh = 2;
-        w.bn = 128;
-    }
-    w.bm = 128 * w.mh;
-}
 
 bool tc_supported(const gtmoe_handle *h, int64_t T) {
     const gtmoe_config &c = h->cfg;
     if (c.weight_precision != GTMOE_INT8 && c.weight_precision != GTMOE_FP4) return false;
     if (T <= 0) return false;
     if (getenv("GTMOE_DISABLE_TC")) return false;
-    TcWeights w;
-    choose_shape(w);
-    // gate/up tiles hold bn/2 features of each; down tiles bn features; K in
-    // steps of 64
-    if (c.hidden % (w.bn / 2) != 0 || c.d_model % w.bn != 0) return false;
-    if (c.d_model % kBK != 0 || c.hidden % kBK != 0) return false;
-    return true;
+    return shapes_ok(c);
+}
+
+int tc_relayout_layer(gtmoe_handle *h, LayerDev &L, int which) {
+    const gtmoe_config &c = h->cfg;
+    L.tiled.release();
+    if (c.weight_precision != GTMOE_INT8 && c.weight_precision != GTMOE_FP4) return 0;
+    if (!shapes_ok(c)) return 0;
+    const int code_bytes = c.weight_precision == GTMOE_INT8 ? 64 : 32;
+    const int chunk_rows = which == GTMOE_DOWN ? kBN : kGateRows;
+    const int64_t items = (int64_t)L.rows * (L.width / kBK);
+    GT_CHECK(L.tiled.ensure((size_t)items * (code_bytes + 16)));
+    relayout_kernel<<<(unsigned)((items + 255) / 256), 256, 0, h->stream>>>(
+        (const uint8_t *)L.w.p, L.s.as<float>(), L.rows, L.width, code_bytes, chunk_rows, L.tiled.as<uint8_t>());
+    GT_CUDA(cudaGetLastError());
+    return 0;
 }
 
 int tc_prepare(gtmoe_handle *h, TcWeights &w) {
@@ -566,16 +523,12 @@ int tc_prepare(gtmoe_handle *h, TcWeights &w) {
     int dev = 0;
     GT_CUDA(cudaGetDevice(&dev));
     GT_CUDA(cudaDeviceGetAttribute(&w.sms, cudaDevAttrMultiProcessorCount, dev));
-    choose_shape(w);
     w.ready = 1;
     (void)h;
     return 0;
 }
 
-int tc_tile_rows(TcWeights &w) {
-    choose_shape(w);
-    return w.bm;
-}
+int tc_tile_rows(TcWeights &) { return kBM; }
 
 int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, cudaStream_t st) {
     const gtmoe_config &c = h->cfg;
@@ -587,8 +540,27 @@ int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, cudaStrea
     ka.clamped = c.clamped;
     ka.clamp_limit = (float)c.clamp_limit;
     ka.err = w.err;
-    if (w.mh == 1) return launch_pair<1, 256>(h, w, ta, ka, st);
-    return launch_pair<2, 128>(h, w, ta, ka, st);
+    CUtensorMap xmap, hmap;
+    GT_CHECK(encode_bf16_2d(&xmap, ta.xp, c.d_model, ta.rows_x, kBK, kBM));
+    GT_CHECK(encode_bf16_2d(&hmap, ta.hp, c.hidden, ta.rows_h, kBK, kBM));
+    const int prec = c.weight_precision;
+
+    GT_CHECK(h->phase_begin(3));
+    ka.K = c.d_model;
+    ka.n_out = c.hidden;
+    ka.out = (__nv_bfloat16 *)ta.hp;
+    if (prec == GTMOE_INT8) GT_CHECK((launch_one<GTMOE_INT8, true>(xmap, ka, w.sms, st)));
+    else GT_CHECK((launch_one<GTMOE_FP4, true>(xmap, ka, w.sms, st)));
+    GT_CHECK(h->phase_end(3));
+
+    GT_CHECK(h->phase_begin(4));
+    ka.K = c.hidden;
+    ka.n_out = c.d_model;
+    ka.out = (__nv_bfloat16 *)ta.yp;
+    if (prec == GTMOE_INT8) GT_CHECK((launch_one<GTMOE_INT8, false>(hmap, ka, w.sms, st)));
+    else GT_CHECK((launch_one<GTMOE_FP4, false>(hmap, ka, w.sms, st)));
+    GT_CHECK(h->phase_end(4));
+    return 0;
 }
 
 int tc_check_error(TcWeights &w) {
@@ -597,7 +569,7 @@ int tc_check_error(TcWeights &w) {
     GT_CUDA(cudaMemcpy(&v, w.err, sizeof(int), cudaMemcpyDeviceToHost));
     if (v != 0) {
         cudaMemset(w.err, 0, sizeof(int));
-        return fail(GTMOE_ETIMEOUT, "tensor-core expert kernel gave up waiting (barrier %d); results are invalid", v);
+        return fail(GTMOE_ETIMEOUT, "tensor-core kernel gave up waiting (barrier %d); results are invalid", v);
     }
     return 0;
 }

@@ -10,10 +10,11 @@ struct gtmoe_handle;
 
 namespace gtmoe {
 
+struct LayerDev;
+
 struct TcWeights {
     int ready = 0;
     int sms = 148;
-    int mh = 2, bn = 128, bm = 256;  // tile: mh x 128 rows, bn columns
     int *err = nullptr;  // device flag: nonzero when a bounded wait expired
 };
 
@@ -28,6 +29,9 @@ struct TcArgs {
 };
 
 bool tc_supported(const gtmoe_handle *h, int64_t T);
+// Builds L.tiled (the chunk layout the tensor-core kernels stream) when the
+// handle's shapes and precision use the tensor-core path; no-op otherwise.
+int tc_relayout_layer(gtmoe_handle *h, LayerDev &L, int which);
 int tc_tile_rows(TcWeights &w);  // m-tile height of the current shape
 int tc_prepare(gtmoe_handle *h, TcWeights &w);
 int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &a, cudaStream_t st);
