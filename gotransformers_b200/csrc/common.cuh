@@ -59,6 +59,12 @@ __device__ __forceinline__ T gate_act(T x, int clamped, T limit) {
     if (clamped && x > limit) x = limit;
     return x * sigmoid_t<T>(x);
 }
+// float SiLU as x / (1 + e^-x) with the fast reciprocal (<= 2 ulp)
+template <>
+__device__ __forceinline__ float gate_act<float>(float x, int clamped, float limit) {
+    if (clamped && x > limit) x = limit;
+    return __fdividef(x, 1.f + __expf(-x));
+}
 template <typename T>
 __device__ __forceinline__ T up_act(T x, int clamped, T limit) {
     if (clamped) {

@@ -56,6 +56,7 @@ constexpr int kTmemCols = 512;
 constexpr int kATileBytes = kBM * kBK * 2;  // 32 KB
 constexpr int kBTileBytes = kBN * kBK * 2;  // 16 KB
 constexpr int kItems = kBN * 4 / kDequantThreads;  // (row, 16-value block) items per dequant thread
+constexpr int kPrefixCache = 2048;  // m-tile prefix entries cached in shared memory
 // instruction descriptor: D f32, A bf16, B bf16, both K-major, N=128, M=128
 constexpr uint32_t kIdesc =
     (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
@@ -67,7 +68,8 @@ struct Raw {
     static constexpr int kRowBytes = kCodeBytes + 16;  // codes + 4 float scales
     static constexpr int kStageBytes = kBN * kRowBytes;  // both chunks of kernel 1, or one of kernel 2
     static constexpr int kStages = PREC == GTMOE_INT8 ? 3 : 4;
-    static constexpr int kSmemBytes = kStages * (kATileBytes + kBTileBytes + kStageBytes) + 1024 + 256;
+    static constexpr int kSmemBytes =
+        kStages * (kATileBytes + kBTileBytes + kStageBytes) + 1024 + 256 + kPrefixCache * 4;
 };
 
 struct TcKernelArgs {
@@ -92,27 +94,39 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 }
 
 // Work unit u -> (group, n-tile, m-tile); m-tiles innermost so that
-// neighbouring CTAs share one weight tile in L2.
+// neighbouring CTAs share one weight tile in L2.  Each role walks its units in
+// increasing order, so the group index only moves forward: the decoder keeps
+// it and the group's record, and reads the m-tile prefix from shared memory.
 struct Unit {
     int g;
     int nt;
     int64_t mt;
 };
-__device__ __forceinline__ Unit decode_unit(int64_t u, const int64_t *__restrict__ prefix, int n_groups, int n_tiles) {
-    int lo = 0, hi = n_groups - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (__ldg(prefix + mid) * n_tiles <= u) lo = mid;
-        else hi = mid - 1;
+struct UnitDecoder {
+    const int *prefix;  // shared-memory copy (n_groups + 1 entries)
+    const Group *groups;
+    int n_groups, n_tiles;
+    int g = -1;
+    Group grp;
+    __device__ __forceinline__ bool advance(int64_t u, Unit &w) {
+        bool changed = false;
+        if (g < 0) {
+            g = 0;
+            changed = true;
+        }
+        while (g + 1 < n_groups && (int64_t)prefix[g + 1] * n_tiles <= u) {
+            g++;
+            changed = true;
+        }
+        if (changed) grp = groups[g];
+        const int64_t mt_g = prefix[g + 1] - prefix[g];
+        const int64_t r = u - (int64_t)prefix[g] * n_tiles;
+        w.g = g;
+        w.nt = (int)(r / mt_g);
+        w.mt = r % mt_g;
+        return changed;
     }
-    Unit w;
-    w.g = lo;
-    const int64_t mt_g = __ldg(prefix + lo + 1) - __ldg(prefix + lo);
-    const int64_t r = u - __ldg(prefix + lo) * n_tiles;
-    w.nt = (int)(r / mt_g);
-    w.mt = r % mt_g;
-    return w;
-}
+};
 
 // prmt with the sign-replicating selector mode (msb of a selector nibble set)
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -228,6 +242,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     uint64_t *tmem_empty = bars + 4 * S + 2;  // [2]
     uint32_t *tmem_slot = (uint32_t *)(bars + 4 * S + 4);
     volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+    volatile uint32_t *stage_two = (volatile uint32_t *)(tmem_slot + 2);  // [S] second M half in use
+    int *prefix_s = (int *)(smem + S * (kATileBytes + kBTileBytes + R::kStageBytes) + 256);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -235,6 +251,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int n_tiles = GATED ? a.n_out / kGateRows : a.n_out / kBN;
     const int64_t total = __ldg(a.tile_prefix + a.n_groups) * n_tiles;
     const int KB = a.K / kBK;
+    for (int i = threadIdx.x; i <= a.n_groups; i += blockDim.x) prefix_s[i] = (int)__ldg(a.tile_prefix + i);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
@@ -268,16 +285,22 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             uint32_t phase = 0;
             const int chunk_rows = GATED ? kGateRows : kBN;
             const size_t chunk_bytes = (size_t)chunk_rows * R::kRowBytes;
+            UnitDecoder dec{prefix_s, a.groups, a.n_groups, n_tiles};
+            const uint8_t *src0 = nullptr, *src1 = nullptr;
             for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
-                const Unit w = decode_unit(u, a.tile_prefix, a.n_groups, n_tiles);
-                const Group grp = a.groups[w.g];
-                const ExpertLayers &L = a.experts[grp.expert];
+                Unit w;
+                if (dec.advance(u, w)) {
+                    const ExpertLayers &L = a.experts[dec.grp.expert];
+                    src0 = GATED ? L.tiled[0] : L.tiled[2];
+                    src1 = L.tiled[1];
+                }
+                const Group &grp = dec.grp;
                 const int row0 = (int)((GATED ? grp.x_row0 : grp.h_row0) + w.mt * kBM);
+                const uint32_t two = grp.m - w.mt * kBM > 128;
                 // chunk (n-tile, k-block) of a layer sits at (nt * KB + kb) * chunk_bytes
-                const uint8_t *src0 = GATED ? L.tiled[0] : L.tiled[2];
-                const uint8_t *src1 = L.tiled[1];
                 for (int kb = 0; kb < KB; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err, 1)) break;
+                    stage_two[stage] = two;
                     mbar_arrive_expect_tx(&full_a[stage], kATileBytes);
                     tma_load_2d(a_tiles + stage * kATileBytes, &amap, kb * kBK, row0, &full_a[stage]);
                     const size_t off = ((size_t)w.nt * KB + kb) * chunk_bytes;
@@ -306,9 +329,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
-                // skip the second half when it holds no row of the group
-                const Unit w = decode_unit(u, a.tile_prefix, a.n_groups, n_tiles);
-                const bool two = a.groups[w.g].m - w.mt * kBM > 128;
                 if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, a.err, 2)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 2 * kBN);
@@ -320,6 +340,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                         break;
                     }
                     tc_fence_after();
+                    // skip the second half when it holds no row of the group
+                    const bool two = stage_two[stage] != 0;
                     const uint64_t adesc = sw128_desc(smem_u32(a_tiles + stage * kATileBytes));
                     const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + stage * kBTileBytes));
 #pragma unroll
@@ -349,10 +371,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
         int acc = 0;
         uint32_t acc_phase = 0;
+        UnitDecoder dec{prefix_s, a.groups, a.n_groups, n_tiles};
+        const float *b0 = nullptr, *b1 = nullptr;
         for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
-            const Unit w = decode_unit(u, a.tile_prefix, a.n_groups, n_tiles);
-            const Group grp = a.groups[w.g];
-            const ExpertLayers &L = a.experts[grp.expert];
+            Unit w;
+            if (dec.advance(u, w)) {
+                const ExpertLayers &L = a.experts[dec.grp.expert];
+                b0 = GATED ? L.b32[0] : L.b32[2];
+                b1 = L.b32[1];
+            }
+            const Group &grp = dec.grp;
             if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, a.err, 5)) break;
             tc_fence_after();
             const int64_t m_left = grp.m - w.mt * kBM;
@@ -366,8 +394,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                 __nv_bfloat16 *dst = a.out + (grp.h_row0 + w.mt * kBM + row_in_tile) * (int64_t)a.n_out;
                 if (GATED) {
                     const int f0 = w.nt * kGateRows;
-                    const float *bg = L.b32[0];
-                    const float *bu = L.b32[1];
+                    const float *bg = b0;
+                    const float *bu = b1;
 #pragma unroll 1
                     for (int c = 0; c < kGateRows; c += 16) {
                         uint32_t g[16], up[16];
@@ -395,7 +423,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                     }
                 } else {
                     const int f0 = w.nt * kBN;
-                    const float *bd = L.b32[2];
+                    const float *bd = b0;
 #pragma unroll 1
                     for (int c = 0; c < kBN; c += 16) {
                         uint32_t y[16];
@@ -486,8 +514,10 @@ int launch_one(const CUtensorMap &map, const TcKernelArgs &ka, int sms, cudaStre
 }
 
 bool shapes_ok(const gtmoe_config &c) {
-    // gate/up tiles hold 64 features of each, down tiles 128; K in steps of 64
-    return c.hidden % kGateRows == 0 && c.d_model % kBN == 0 && c.d_model % kBK == 0 && c.hidden % kBK == 0;
+    // gate/up tiles hold 64 features of each, down tiles 128; K in steps of 64;
+    // the group prefix fits the shared-memory cache
+    return c.hidden % kGateRows == 0 && c.d_model % kBN == 0 && c.d_model % kBK == 0 && c.hidden % kBK == 0 &&
+           c.n_shared + c.n_routed + 1 <= kPrefixCache;
 }
 
 }  // namespace
