@@ -43,31 +43,33 @@
 
 namespace gtmoe {
 
+
 namespace {
 
-constexpr int kBK = 64;         // K elements per stage (128 bytes of bf16)
-constexpr int kBM = 256;        // rows per tile: two M=128 UMMAs
-constexpr int kBN = 128;        // columns per tile
-constexpr int kGateRows = kBN / 2;  // gate (and up) features per kernel-1 tile
+constexpr int kBK = 64;              // K elements per stage (128 bytes of bf16)
+constexpr int kCtaRows = 128;        // token rows per CTA (UMMA M=256 over the pair)
+constexpr int kTileM = 2 * kCtaRows; // rows per cluster tile
+constexpr int kTileN = 256;          // B rows (output columns) per cluster tile, 128 per CTA
+constexpr int kChunkRows = 128;      // weight rows per raw chunk = one CTA's half of B
 constexpr int kNumDequantWarps = 8;
 constexpr int kDequantThreads = kNumDequantWarps * 32;
 constexpr int kNumThreads = (6 + kNumDequantWarps) * 32;  // 448
 constexpr int kTmemCols = 512;
-constexpr int kATileBytes = kBM * kBK * 2;  // 32 KB
-constexpr int kBTileBytes = kBN * kBK * 2;  // 16 KB
-constexpr int kItems = kBN * 4 / kDequantThreads;  // (row, 16-value block) items per dequant thread
+constexpr int kATileBytes = kCtaRows * kBK * 2;    // 16 KB per CTA
+constexpr int kBTileBytes = kChunkRows * kBK * 2;  // 16 KB per CTA
+constexpr int kItems = kChunkRows * 4 / kDequantThreads;  // (row, 16-value block) items per dequant thread
 constexpr int kPrefixCache = 2048;  // m-tile prefix entries cached in shared memory
-// instruction descriptor: D f32, A bf16, B bf16, both K-major, N=128, M=128
+// instruction descriptor: D f32, A bf16, B bf16, both K-major, N=256, M=256 (2-SM)
 constexpr uint32_t kIdesc =
-    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileN >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
 
-// Raw chunk geometry: code bytes per row per k-block, chunk bytes.
+// Raw chunk geometry: code bytes per row per k-block, stage bytes.
 template <int PREC>
 struct Raw {
     static constexpr int kCodeBytes = PREC == GTMOE_INT8 ? 64 : 32;
     static constexpr int kRowBytes = kCodeBytes + 16;  // codes + 4 float scales
-    static constexpr int kStageBytes = kBN * kRowBytes;  // both chunks of kernel 1, or one of kernel 2
-    static constexpr int kStages = PREC == GTMOE_INT8 ? 3 : 4;
+    static constexpr int kStageBytes = kChunkRows * kRowBytes;
+    static constexpr int kStages = 5;
     static constexpr int kSmemBytes =
         kStages * (kATileBytes + kBTileBytes + kStageBytes) + 1024 + 256 + kPrefixCache * 4;
 };
@@ -93,10 +95,32 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
+// Bounded wait of the 2-SM kernel: on expiry it records `code`, raises the
+// abort flag of this CTA and of its peer, and returns false.
+template <bool CLUSTER_ACQUIRE>
+__device__ __forceinline__ bool pair_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          uint32_t peer_abort, int *err, int code) {
+    auto probe = [&]() { return CLUSTER_ACQUIRE ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
+    if (probe()) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        for (int i = 0; i < 32; i++)
+            if (probe()) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicCAS(err, 0, code);
+            *abort_flag = 1;
+            asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1) : "memory");
+            return false;
+        }
+    }
+}
+
 // Work unit u -> (group, n-tile, m-tile); m-tiles innermost so that
-// neighbouring CTAs share one weight tile in L2.  Each role walks its units in
-// increasing order, so the group index only moves forward: the decoder keeps
-// it and the group's record, and reads the m-tile prefix from shared memory.
+// neighbouring clusters share one weight tile in L2.  Each role walks its
+// units in increasing order, so the group index only moves forward: the
+// decoder keeps it and the group's record, and reads the m-tile prefix from
+// shared memory.
 struct Unit {
     int g;
     int nt;
@@ -185,31 +209,27 @@ __device__ __forceinline__ void int8_decode4(uint32_t w, float s, uint32_t *o) {
     o[1] = pack_bf16(f2 * s, f3 * s);
 }
 
-// Dequantises one stage: item (r, b) = 16 values of B-tile row r, k-block
-// quarter b.  The raw stage holds, for kernel 1, the gate chunk (rows 0..63)
-// then the up chunk (rows 64..127); for kernel 2 one chunk of 128 rows; each
-// chunk is codes [rows][kCodeBytes] then scales [rows][4].
-template <int PREC, bool GATED>
+// Dequantises one stage of this CTA's 128 B rows: item (r, b) = 16 values of
+// row r, k-block quarter b.  The raw stage is one chunk: codes
+// [128][kCodeBytes] then scales [128][4].
+template <int PREC>
 __device__ __forceinline__ void dequant_stage(const uint8_t *raw, uint8_t *btile, int tid) {
     using R = Raw<PREC>;
-    constexpr int CR = GATED ? kGateRows : kBN;  // rows per chunk
 #pragma unroll
     for (int i = 0; i < kItems; i++) {
         const int item = tid + i * kDequantThreads;
         const int r = item >> 2;
         const int b = item & 3;
-        const int ch = r / CR, lr = r % CR;
-        const uint8_t *chunk = raw + ch * CR * R::kRowBytes;
-        const float s = *reinterpret_cast<const float *>(chunk + CR * R::kCodeBytes + lr * 16 + b * 4);
+        const float s = *reinterpret_cast<const float *>(raw + kChunkRows * R::kCodeBytes + r * 16 + b * 4);
         uint32_t w[8];
         if (PREC == GTMOE_INT8) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(chunk + lr * R::kCodeBytes + b * 16);
+            const uint4 c = *reinterpret_cast<const uint4 *>(raw + r * R::kCodeBytes + b * 16);
             int8_decode4(c.x, s, w);
             int8_decode4(c.y, s, w + 2);
             int8_decode4(c.z, s, w + 4);
             int8_decode4(c.w, s, w + 6);
         } else {
-            const uint2 c = *reinterpret_cast<const uint2 *>(chunk + lr * R::kCodeBytes + b * 8);
+            const uint2 c = *reinterpret_cast<const uint2 *>(raw + r * R::kCodeBytes + b * 8);
             const Fp4Tables t = fp4_tables(s);
             fp4_decode8(c.x, t, w);
             fp4_decode8(c.y, t, w + 4);
@@ -223,6 +243,13 @@ __device__ __forceinline__ void dequant_stage(const uint8_t *raw, uint8_t *btile
     }
 }
 
+// Grouped SwiGLU GEMM on a CTA pair (cluster of 2, tcgen05.mma.cta_group::2):
+// the pair computes a 256-row x 256-column tile, CTA rank r holding A rows
+// r*128..r*128+127 and B rows r*128..r*128+127 in its own shared memory and
+// D rows r*128.. in its own TMEM.  For kernel 1 the pair's B rows are 128
+// gate features (rank 0) and the same 128 up features (rank 1), so D columns
+// 0..127 / 128..255 of each TMEM lane are the gate / up values of one
+// (token, feature).  Rank 0 (the leader) issues the MMAs.
 template <int PREC, bool GATED>
 __global__ void __launch_bounds__(kNumThreads, 1)
     grouped_tc_kernel(const __grid_constant__ CUtensorMap amap, const TcKernelArgs a) {
@@ -234,21 +261,24 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     uint8_t *b_tiles = smem + S * kATileBytes;
     uint8_t *raw_tiles = b_tiles + S * kBTileBytes;
     uint64_t *bars = (uint64_t *)(raw_tiles + S * R::kStageBytes);
-    uint64_t *full_a = bars;                  // [S] activations landed
-    uint64_t *full_raw = bars + S;            // [S] raw weights landed
-    uint64_t *full_b = bars + 2 * S;          // [S] bf16 weights written
-    uint64_t *empty = bars + 3 * S;           // [S] MMAs of the stage done
-    uint64_t *tmem_full = bars + 4 * S;       // [2]
-    uint64_t *tmem_empty = bars + 4 * S + 2;  // [2]
+    uint64_t *full_a = bars;                  // [S] both activation tiles landed (leader)
+    uint64_t *full_raw = bars + S;            // [S] this CTA's raw weights landed
+    uint64_t *full_b = bars + 2 * S;          // [S] both bf16 weight halves written (leader)
+    uint64_t *empty = bars + 3 * S;           // [S] MMAs of the stage done (both CTAs)
+    uint64_t *tmem_full = bars + 4 * S;       // [2] accumulator ready (both CTAs)
+    uint64_t *tmem_empty = bars + 4 * S + 2;  // [2] both epilogues done (leader)
     uint32_t *tmem_slot = (uint32_t *)(bars + 4 * S + 4);
     volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
-    volatile uint32_t *stage_two = (volatile uint32_t *)(tmem_slot + 2);  // [S] second M half in use
     int *prefix_s = (int *)(smem + S * (kATileBytes + kBTileBytes + R::kStageBytes) + 256);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // kernel 1: kGateRows gate + the same up features per tile
-    const int n_tiles = GATED ? a.n_out / kGateRows : a.n_out / kBN;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+    const uint32_t peer_abort = mapa_shared(smem_u32((const void *)abort_flag), rank ^ 1u);
+    // kernel 1: 128 gate + the same 128 up features per tile; kernel 2: 256 features
+    const int n_tiles = GATED ? a.n_out / kChunkRows : a.n_out / kTileN;
     const int64_t total = __ldg(a.tile_prefix + a.n_groups) * n_tiles;
     const int KB = a.K / kBK;
     for (int i = threadIdx.x; i <= a.n_groups; i += blockDim.x) prefix_s[i] = (int)__ldg(a.tile_prefix + i);
@@ -257,57 +287,54 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         for (int s = 0; s < S; s++) {
             mbar_init(&full_a[s], 1);
             mbar_init(&full_raw[s], 1);
-            mbar_init(&full_b[s], kNumDequantWarps);
+            mbar_init(&full_b[s], 2 * kNumDequantWarps);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], 4);
+            mbar_init(&tmem_empty[b], 2 * 4);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTmemCols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // the peer's barriers are initialised before any remote operation
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- producer: activation tile (TMA) + raw weight chunks (bulk)
+        // ---------------- producer: activation tile (TMA, counted on the leader) + raw weight chunk (bulk)
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&amap) : "memory");
             int stage = 0;
             uint32_t phase = 0;
-            const int chunk_rows = GATED ? kGateRows : kBN;
-            const size_t chunk_bytes = (size_t)chunk_rows * R::kRowBytes;
+            constexpr uint32_t chunk_bytes = R::kStageBytes;
             UnitDecoder dec{prefix_s, a.groups, a.n_groups, n_tiles};
-            const uint8_t *src0 = nullptr, *src1 = nullptr;
-            for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+            const uint8_t *src = nullptr;
+            for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
                 Unit w;
                 if (dec.advance(u, w)) {
                     const ExpertLayers &L = a.experts[dec.grp.expert];
-                    src0 = GATED ? L.tiled[0] : L.tiled[2];
-                    src1 = L.tiled[1];
+                    src = GATED ? L.tiled[rank] : L.tiled[2];
                 }
                 const Group &grp = dec.grp;
-                const int row0 = (int)((GATED ? grp.x_row0 : grp.h_row0) + w.mt * kBM);
-                const uint32_t two = grp.m - w.mt * kBM > 128;
-                // chunk (n-tile, k-block) of a layer sits at (nt * KB + kb) * chunk_bytes
+                const int row0 = (int)((GATED ? grp.x_row0 : grp.h_row0) + w.mt * kTileM + rank * kCtaRows);
+                // chunk (t, k-block) of a layer sits at (t * KB + kb) * chunk_bytes
+                const int64_t chunk = GATED ? w.nt : 2 * w.nt + rank;
                 for (int kb = 0; kb < KB; kb++) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err, 1)) break;
-                    stage_two[stage] = two;
-                    mbar_arrive_expect_tx(&full_a[stage], kATileBytes);
-                    tma_load_2d(a_tiles + stage * kATileBytes, &amap, kb * kBK, row0, &full_a[stage]);
-                    const size_t off = ((size_t)w.nt * KB + kb) * chunk_bytes;
-                    uint8_t *dst = raw_tiles + stage * R::kStageBytes;
-                    mbar_arrive_expect_tx(&full_raw[stage], R::kStageBytes);
-                    bulk_load(dst, src0 + off, (uint32_t)chunk_bytes, &full_raw[stage]);
-                    if (GATED) bulk_load(dst + chunk_bytes, src1 + off, (uint32_t)chunk_bytes, &full_raw[stage]);
+                    if (!pair_wait<false>(&empty[stage], phase ^ 1, abort_flag, peer_abort, a.err, 1)) break;
+                    if (leader) mbar_arrive_expect_tx(&full_a[stage], 2 * kATileBytes);
+                    tma_load_2d_pair(a_tiles + stage * kATileBytes, &amap, kb * kBK, row0,
+                                     mapa_shared(smem_u32(&full_a[stage]), 0));
+                    mbar_arrive_expect_tx(&full_raw[stage], chunk_bytes);
+                    bulk_load(raw_tiles + stage * R::kStageBytes, src + ((size_t)chunk * KB + kb) * chunk_bytes,
+                              chunk_bytes, &full_raw[stage]);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
@@ -322,44 +349,38 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer
-        if (lane == 0) {
+        // ---------------- MMA issuer (leader CTA)
+        if (leader && lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
-            for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
-                if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, a.err, 2)) break;
+            for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
+                if (!pair_wait<true>(&tmem_empty[acc], acc_phase ^ 1, abort_flag, peer_abort, a.err, 2)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 2 * kBN);
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kTileN);
                 bool ok = true;
                 for (int kb = 0; kb < KB; kb++) {
-                    if (!mbar_wait(&full_a[stage], phase, abort_flag, a.err, 3) ||
-                        !mbar_wait(&full_b[stage], phase, abort_flag, a.err, 4)) {
+                    if (!pair_wait<true>(&full_a[stage], phase, abort_flag, peer_abort, a.err, 3) ||
+                        !pair_wait<true>(&full_b[stage], phase, abort_flag, peer_abort, a.err, 4)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    // skip the second half when it holds no row of the group
-                    const bool two = stage_two[stage] != 0;
                     const uint64_t adesc = sw128_desc(smem_u32(a_tiles + stage * kATileBytes));
                     const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + stage * kBTileBytes));
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; k++) {
-                        umma_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
-                                  (kb | k) != 0);
-                        if (two)
-                            umma_bf16(d_tmem + kBN, adesc + (uint64_t)((128 * 128) >> 4) + (uint64_t)(2 * k),
-                                      bdesc + (uint64_t)(2 * k), kIdesc, (kb | k) != 0);
-                    }
-                    umma_commit(&empty[stage]);
+                    for (int k = 0; k < kBK / 16; k++)
+                        umma2_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
+                                   (kb | k) != 0);
+                    umma2_commit_mc(&empty[stage], 0x3);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (!ok) break;
-                umma_commit(&tmem_full[acc]);
+                umma2_commit_mc(&tmem_full[acc], 0x3);
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1;
@@ -367,13 +388,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
         }
     } else if (warp < 6) {
-        // ---------------- epilogue: TMEM -> registers -> global
+        // ---------------- epilogue: TMEM -> registers -> global (both CTAs)
         const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+        const uint32_t tmem_empty_leader0 = mapa_shared(smem_u32(&tmem_empty[0]), 0);
         int acc = 0;
         uint32_t acc_phase = 0;
         UnitDecoder dec{prefix_s, a.groups, a.n_groups, n_tiles};
         const float *b0 = nullptr, *b1 = nullptr;
-        for (int64_t u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+        for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
             Unit w;
             if (dec.advance(u, w)) {
                 const ExpertLayers &L = a.experts[dec.grp.expert];
@@ -381,90 +403,85 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                 b1 = L.b32[1];
             }
             const Group &grp = dec.grp;
-            if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, a.err, 5)) break;
+            if (!pair_wait<false>(&tmem_full[acc], acc_phase, abort_flag, peer_abort, a.err, 5)) break;
             tc_fence_after();
-            const int64_t m_left = grp.m - w.mt * kBM;
+            const int row_in_tile = (int)rank * kCtaRows + quad * 32 + lane;
+            const bool valid = row_in_tile < grp.m - w.mt * kTileM;
+            const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * kTileN);
+            __nv_bfloat16 *dst = a.out + (grp.h_row0 + w.mt * kTileM + row_in_tile) * (int64_t)a.n_out;
+            if (GATED) {
+                const int f0 = w.nt * kChunkRows;
+                const float *bg = b0;
+                const float *bu = b1;
 #pragma unroll 1
-            for (int hh = 0; hh < 2; hh++) {
-                if (hh > 0 && m_left <= 128) break;  // the MMA skipped this half
-                const int row_in_tile = hh * 128 + quad * 32 + lane;
-                const bool valid = row_in_tile < m_left;
-                const uint32_t t_row =
-                    tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * 2 * kBN + hh * kBN);
-                __nv_bfloat16 *dst = a.out + (grp.h_row0 + w.mt * kBM + row_in_tile) * (int64_t)a.n_out;
-                if (GATED) {
-                    const int f0 = w.nt * kGateRows;
-                    const float *bg = b0;
-                    const float *bu = b1;
-#pragma unroll 1
-                    for (int c = 0; c < kGateRows; c += 16) {
-                        uint32_t g[16], up[16];
-                        tmem_ld16(t_row + c, g);
-                        tmem_ld16(t_row + kGateRows + c, up);
-                        tmem_ld_wait();
-                        uint32_t o[8];
+                for (int c = 0; c < kChunkRows; c += 16) {
+                    uint32_t g[16], up[16];
+                    tmem_ld16(t_row + c, g);
+                    tmem_ld16(t_row + kChunkRows + c, up);
+                    tmem_ld_wait();
+                    uint32_t o[8];
 #pragma unroll
-                        for (int j = 0; j < 16; j += 2) {
-                            float hv[2];
+                    for (int j = 0; j < 16; j += 2) {
+                        float hv[2];
 #pragma unroll
-                            for (int q = 0; q < 2; q++) {
-                                float gv = __uint_as_float(g[j + q]) + (bg ? __ldg(bg + f0 + c + j + q) : 0.f);
-                                float uv = __uint_as_float(up[j + q]) + (bu ? __ldg(bu + f0 + c + j + q) : 0.f);
-                                hv[q] = gate_act<float>(gv, a.clamped, a.clamp_limit) *
-                                        up_act<float>(uv, a.clamped, a.clamp_limit);
-                            }
-                            o[j / 2] = pack_bf16(hv[0], hv[1]);
+                        for (int q = 0; q < 2; q++) {
+                            float gv = __uint_as_float(g[j + q]) + (bg ? __ldg(bg + f0 + c + j + q) : 0.f);
+                            float uv = __uint_as_float(up[j + q]) + (bu ? __ldg(bu + f0 + c + j + q) : 0.f);
+                            hv[q] = gate_act<float>(gv, a.clamped, a.clamp_limit) *
+                                    up_act<float>(uv, a.clamped, a.clamp_limit);
                         }
-                        if (valid) {
-                            uint4 *p = reinterpret_cast<uint4 *>(dst + f0 + c);
-                            p[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                            p[1] = make_uint4(o[4], o[5], o[6], o[7]);
-                        }
+                        o[j / 2] = pack_bf16(hv[0], hv[1]);
                     }
-                } else {
-                    const int f0 = w.nt * kBN;
-                    const float *bd = b0;
+                    if (valid) {
+                        uint4 *p = reinterpret_cast<uint4 *>(dst + f0 + c);
+                        p[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                        p[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                    }
+                }
+            } else {
+                const int f0 = w.nt * kTileN;
+                const float *bd = b0;
 #pragma unroll 1
-                    for (int c = 0; c < kBN; c += 16) {
-                        uint32_t y[16];
-                        tmem_ld16(t_row + c, y);
-                        tmem_ld_wait();
-                        uint32_t o[8];
+                for (int c = 0; c < kTileN; c += 16) {
+                    uint32_t y[16];
+                    tmem_ld16(t_row + c, y);
+                    tmem_ld_wait();
+                    uint32_t o[8];
 #pragma unroll
-                        for (int j = 0; j < 16; j += 2) {
-                            float y0 = __uint_as_float(y[j]) + (bd ? __ldg(bd + f0 + c + j) : 0.f);
-                            float y1 = __uint_as_float(y[j + 1]) + (bd ? __ldg(bd + f0 + c + j + 1) : 0.f);
-                            o[j / 2] = pack_bf16(y0, y1);
-                        }
-                        if (valid) {
-                            uint4 *p = reinterpret_cast<uint4 *>(dst + f0 + c);
-                            p[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                            p[1] = make_uint4(o[4], o[5], o[6], o[7]);
-                        }
+                    for (int j = 0; j < 16; j += 2) {
+                        float y0 = __uint_as_float(y[j]) + (bd ? __ldg(bd + f0 + c + j) : 0.f);
+                        float y1 = __uint_as_float(y[j + 1]) + (bd ? __ldg(bd + f0 + c + j + 1) : 0.f);
+                        o[j / 2] = pack_bf16(y0, y1);
+                    }
+                    if (valid) {
+                        uint4 *p = reinterpret_cast<uint4 *>(dst + f0 + c);
+                        p[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                        p[1] = make_uint4(o[4], o[5], o[6], o[7]);
                     }
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+            if (lane == 0) mbar_arrive_remote(tmem_empty_leader0 + (uint32_t)(acc * sizeof(uint64_t)));
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
             }
         }
     } else {
-        // ---------------- dequantisation of the weight tiles
+        // ---------------- dequantisation of this CTA's half of the weight tile
         const int tid = threadIdx.x - 6 * 32;
+        const uint32_t full_b_leader0 = mapa_shared(smem_u32(&full_b[0]), 0);
         int stage = 0;
         uint32_t phase = 0;
-        const int64_t units = blockIdx.x < total ? (total - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+        const int64_t units = cluster < total ? (total - cluster + n_clusters - 1) / n_clusters : 0;
         const int64_t steps = units * KB;  // stages this CTA runs
         for (int64_t j = 0; j < steps && !*abort_flag; j++) {
-            if (!mbar_wait(&full_raw[stage], phase, abort_flag, a.err, 6)) break;
-            dequant_stage<PREC, GATED>(raw_tiles + stage * R::kStageBytes, b_tiles + stage * kBTileBytes, tid);
+            if (!pair_wait<false>(&full_raw[stage], phase, abort_flag, peer_abort, a.err, 6)) break;
+            dequant_stage<PREC>(raw_tiles + stage * R::kStageBytes, b_tiles + stage * kBTileBytes, tid);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(&full_b[stage]);
+            if (lane == 0) mbar_arrive_remote(full_b_leader0 + (uint32_t)(stage * sizeof(uint64_t)));
             if (++stage == S) {
                 stage = 0;
                 phase ^= 1;
@@ -474,9 +491,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // no CTA leaves while its peer may still signal it
     tc_fence_after();
     if (warp == 1) {
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
     }
 }
 
@@ -502,21 +520,47 @@ __global__ void relayout_kernel(const uint8_t *__restrict__ codes, const float *
 template <int PREC, bool GATED>
 int launch_one(const CUtensorMap &map, const TcKernelArgs &ka, int sms, cudaStream_t st) {
     auto kern = grouped_tc_kernel<PREC, GATED>;
-    static bool attr_set = false;
-    if (!attr_set) {
+    static int grid = 0;
+    if (!grid) {
         GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Raw<PREC>::kSmemBytes));
-        attr_set = true;
+        // one CTA pair per two SMs, as many pairs as can be resident at once
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3(2 * ((sms + 1) / 2));
+        q.blockDim = dim3(kNumThreads);
+        q.dynamicSmemBytes = Raw<PREC>::kSmemBytes;
+        cudaLaunchAttribute qa;
+        qa.id = cudaLaunchAttributeClusterDimension;
+        qa.val.clusterDim.x = 2;
+        qa.val.clusterDim.y = 1;
+        qa.val.clusterDim.z = 1;
+        q.attrs = &qa;
+        q.numAttrs = 1;
+        int clusters = 0;
+        GT_CUDA(cudaOccupancyMaxActiveClusters(&clusters, kern, &q));
+        if (clusters < 1) return fail(GTMOE_ECUDA, "no CTA pair of the tensor-core kernel fits on this device");
+        grid = 2 * (clusters < sms / 2 ? clusters : sms / 2);
     }
-    kern<<<sms, kNumThreads, Raw<PREC>::kSmemBytes, st>>>(map, ka);
-    GT_CUDA(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kNumThreads);
+    cfg.dynamicSmemBytes = Raw<PREC>::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    GT_CUDA(cudaLaunchKernelEx(&cfg, kern, map, ka));
     note_launches(1);
     return 0;
 }
 
 bool shapes_ok(const gtmoe_config &c) {
-    // gate/up tiles hold 64 features of each, down tiles 128; K in steps of 64;
-    // the group prefix fits the shared-memory cache
-    return c.hidden % kGateRows == 0 && c.d_model % kBN == 0 && c.d_model % kBK == 0 && c.hidden % kBK == 0 &&
+    // gate/up tiles hold 128 features of each, down tiles 256; K in steps of
+    // 64; the group prefix fits the shared-memory cache
+    return c.hidden % kChunkRows == 0 && c.d_model % kTileN == 0 && c.d_model % kBK == 0 && c.hidden % kBK == 0 &&
            c.n_shared + c.n_routed + 1 <= kPrefixCache;
 }
 
@@ -536,7 +580,8 @@ int tc_relayout_layer(gtmoe_handle *h, LayerDev &L, int which) {
     if (c.weight_precision != GTMOE_INT8 && c.weight_precision != GTMOE_FP4) return 0;
     if (!shapes_ok(c)) return 0;
     const int code_bytes = c.weight_precision == GTMOE_INT8 ? 64 : 32;
-    const int chunk_rows = which == GTMOE_DOWN ? kBN : kGateRows;
+    const int chunk_rows = kChunkRows;
+    (void)which;
     const int64_t items = (int64_t)L.rows * (L.width / kBK);
     GT_CHECK(L.tiled.ensure((size_t)items * (code_bytes + 16)));
     relayout_kernel<<<(unsigned)((items + 255) / 256), 256, 0, h->stream>>>(
@@ -558,7 +603,7 @@ int tc_prepare(gtmoe_handle *h, TcWeights &w) {
     return 0;
 }
 
-int tc_tile_rows(TcWeights &) { return kBM; }
+int tc_tile_rows(TcWeights &) { return kTileM; }
 
 int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, cudaStream_t st) {
     const gtmoe_config &c = h->cfg;
@@ -571,8 +616,8 @@ int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, cudaStrea
     ka.clamp_limit = (float)c.clamp_limit;
     ka.err = w.err;
     CUtensorMap xmap, hmap;
-    GT_CHECK(encode_bf16_2d(&xmap, ta.xp, c.d_model, ta.rows_x, kBK, kBM));
-    GT_CHECK(encode_bf16_2d(&hmap, ta.hp, c.hidden, ta.rows_h, kBK, kBM));
+    GT_CHECK(encode_bf16_2d(&xmap, ta.xp, c.d_model, ta.rows_x, kBK, kCtaRows));
+    GT_CHECK(encode_bf16_2d(&hmap, ta.hp, c.hidden, ta.rows_h, kBK, kCtaRows));
     const int prec = c.weight_precision;
 
     GT_CHECK(h->phase_begin(3));
@@ -603,6 +648,7 @@ int tc_check_error(TcWeights &w) {
     }
     return 0;
 }
+
 
 void tc_release(TcWeights &w) {
     if (w.err) cudaFree(w.err);
