@@ -356,13 +356,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             int acc = 0;
             uint32_t acc_phase = 0;
             for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
-                if (!pair_wait<true>(&tmem_empty[acc], acc_phase ^ 1, abort_flag, peer_abort, a.err, 2)) break;
+                if (!pair_wait<false>(&tmem_empty[acc], acc_phase ^ 1, abort_flag, peer_abort, a.err, 2)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kTileN);
                 bool ok = true;
                 for (int kb = 0; kb < KB; kb++) {
-                    if (!pair_wait<true>(&full_a[stage], phase, abort_flag, peer_abort, a.err, 3) ||
-                        !pair_wait<true>(&full_b[stage], phase, abort_flag, peer_abort, a.err, 4)) {
+                    if (!pair_wait<false>(&full_a[stage], phase, abort_flag, peer_abort, a.err, 3) ||
+                        !pair_wait<false>(&full_b[stage], phase, abort_flag, peer_abort, a.err, 4)) {
                         ok = false;
                         break;
                     }
