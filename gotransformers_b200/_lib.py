@@ -51,6 +51,7 @@ EXPORTS = [
     "gtmoe_read_timing",
     "gtmoe_quantize_rows",
     "gtmoe_fill_normal",
+    "gtmoe_route_noalloc",
 ]
 
 
@@ -112,6 +113,7 @@ def lib():
             L.gtmoe_set_timing.argtypes = [vp, i32]
             L.gtmoe_read_timing.argtypes = [vp, vp, i32, vp, vp]
             L.gtmoe_quantize_rows.argtypes = [i32, vp, i64, i32, vp, vp]
+            L.gtmoe_route_noalloc.argtypes = [vp, vp, i32, i64, vp, vp, vp]
             L.gtmoe_fill_normal.argtypes = [vp, i32, i64, ctypes.c_uint64, ctypes.c_uint64, i64, d]
             for name in EXPORTS:
                 if name not in ("gtmoe_destroy",):

@@ -179,6 +179,22 @@ GTMOE_API int gtmoe_update_balance(gtmoe_t h, double rate);
 GTMOE_API int gtmoe_set_timing(gtmoe_t h, int enable);
 GTMOE_API int gtmoe_read_timing(gtmoe_t h, double *ms, int n_phases, int64_t *calls, int64_t *kernel_launches);
 
+/* Routing only, allocating nothing.  No counterpart in the reference.  For
+ * callers that cannot allocate device memory while they run -- a
+ * token-by-token generation loop, where a cudaMalloc would synchronise the
+ * device between tokens, or a server that plans its device memory up front --
+ * this runs the router of gtmoe_forward (logits, exact top-k, gates) with its
+ * scratch in a fixed array of about 4.3 MB that the library holds on every
+ * GPU it is loaded on until exit.  Limits: T <= 65536, T * n_routed <= 262144,
+ * T * experts_per_token <= 524288; larger calls fail with GTMOE_EINVAL.  x,
+ * chosen (int32[T*k]), gates (double[T*k]) and, with hash routing, token_ids
+ * are device pointers; the results equal gtmoe_forward's chosen and gates.
+ * Asynchronous on the handle's stream.  The first call on a device looks the
+ * array up and should come before any stream capture.  Calls share the array:
+ * calls that overlap on the GPU race. */
+GTMOE_API int gtmoe_route_noalloc(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids,
+                                  int32_t *chosen, double *gates);
+
 /* lowprecision.RowsFromMatrix (lowprecision/rows.go:276-283, Rows.Append
  * rows.go:38-79) on the GPU: quantises rows x width float64 values into the
  * RowsSnapshot arrays described above.  Bit-identical to the reference
