@@ -194,12 +194,6 @@ def main():
     mode = args.mode
     if mode == "auto":
         mode = "replicas" if world == 1 else "ep"
-    if world > 1 and mode == "ep":
-        try:
-            probe_id = bytearray(128)
-            _lib.check(_lib.lib().gtmoe_ep_unique_id((__import__("ctypes").c_char * 128).from_buffer(probe_id)))
-        except _lib.GtmoeError:
-            mode = "replicas"
 
     T_total = cfg.T
     if T_total % world:

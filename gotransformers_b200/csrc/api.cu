@@ -231,7 +231,7 @@ static int all_layers_set(const gtmoe_handle *h) {
     return 0;
 }
 
-static int refresh_table(gtmoe_handle *h) {
+int refresh_table(gtmoe_handle *h) {
     if (!h->table_dirty) return 0;
     int n = h->cfg.n_shared + h->e_local;
     std::vector<ExpertLayers> t(n);
@@ -664,8 +664,7 @@ int gtmoe_last_expert_load(gtmoe_t h, int64_t *load) {
     std::lock_guard<std::mutex> lock(h->mu);
     if (!h->have_load) return fail(GTMOE_ENOTREADY, "LastExpertLoad before the first Forward");
     GT_CUDA(cudaSetDevice(h->device));
-    int n = h->n_ranks > 1 ? h->e_local : h->cfg.n_routed;
-    GT_CUDA(cudaMemcpyAsync(load, h->load.p, sizeof(int64_t) * n, cudaMemcpyDefault, h->stream));
+    GT_CUDA(cudaMemcpyAsync(load, h->load.p, sizeof(int64_t) * h->cfg.n_routed, cudaMemcpyDefault, h->stream));
     GT_CUDA(cudaStreamSynchronize(h->stream));
     return 0;
 }

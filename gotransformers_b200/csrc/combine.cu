@@ -22,6 +22,7 @@ template <typename YT, typename ACC>
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
     const int64_t t = blockIdx.x;
     const YT *__restrict__ y = (const YT *)a.y;
+    const YT *__restrict__ yr = (const YT *)(a.y_routed ? a.y_routed : a.y);
     const int d = a.d;
     for (int col = threadIdx.x; col < d; col += blockDim.x) {
         ACC acc = ACC(0);
@@ -39,8 +40,8 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
             } else {
                 g = a.gates32[t * a.k + j];
             }
-            if constexpr (sizeof(YT) == 8) v = y[row * d + col];
-            else v = (ACC)to_f<YT>(y[row * d + col]);
+            if constexpr (sizeof(YT) == 8) v = yr[row * d + col];
+            else v = (ACC)to_f<YT>(yr[row * d + col]);
             acc += g * v;
         }
         const int64_t o = t * d + col;
@@ -57,6 +58,7 @@ template <typename OT>
 __global__ void __launch_bounds__(256) combine_bf16x8_kernel(CombineArgs a) {
     const int64_t t = blockIdx.x;
     const uint4 *__restrict__ y = (const uint4 *)a.y;
+    const uint4 *__restrict__ yr = (const uint4 *)(a.y_routed ? a.y_routed : a.y);
     const int dv = a.d / 8;
     for (int v = threadIdx.x; v < dv; v += blockDim.x) {
         float acc[8];
@@ -75,7 +77,7 @@ __global__ void __launch_bounds__(256) combine_bf16x8_kernel(CombineArgs a) {
         for (int j = 0; j < a.k; j++) {
             const int64_t row = a.routed_row0 + a.slot_row[t * a.k + j];
             const float g = a.gates32[t * a.k + j];
-            const uint4 p = y[row * dv + v];
+            const uint4 p = yr[row * dv + v];
             const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&p);
 #pragma unroll
             for (int q = 0; q < 4; q++) {

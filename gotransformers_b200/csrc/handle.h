@@ -100,6 +100,7 @@ struct gtmoe_handle {
 
 namespace gtmoe {
 int layer_index(const gtmoe_handle *h, int kind, int index, int which);
+int refresh_table(gtmoe_handle *h);  // device table of expert layers (+ tensor-core set-up)
 int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, const int64_t *ids_dev,
                    const void *res_dev, void *out_dev, int out_dtype);
 int create_handle(const gtmoe_config *cfg, int device, int n_ranks, int rank, gtmoe_t *out);

@@ -96,6 +96,7 @@ struct CombineArgs {
     int64_t T;
     int d, k, S;
     const void *y;             // rows x d, y_dtype
+    const void *y_routed = nullptr;  // routed rows if not in y (expert parallelism)
     int y_dtype;
     int64_t shared_row0;       // row of shared expert 0 (rows s*T + t)
     int64_t routed_row0;       // row of routed row 0

@@ -193,8 +193,7 @@ class MixtureOfExperts:
             chosen = np.empty((T, k), np.int32)
             gates = np.empty((T, k), np.float64)
             perm = np.empty(T * k, np.int32)
-            n_load = self.cfg.n_routed // self.ep_ranks
-            load = np.empty(n_load, np.int64)
+            load = np.empty(self.cfg.n_routed, np.int64)
         check(_lib.lib().gtmoe_forward(self._h, _addr(x), xdt, T, _addr(ids), _addr(residual), _addr(out), odt_code,
                                        _addr(chosen), _addr(gates), _addr(perm), _addr(load)))
         if want_routing:
@@ -205,8 +204,7 @@ class MixtureOfExperts:
         return out
 
     def last_expert_load(self) -> np.ndarray:
-        n = self.cfg.n_routed // self.ep_ranks
-        out = np.empty(n, np.int64)
+        out = np.empty(self.cfg.n_routed, np.int64)
         check(_lib.lib().gtmoe_last_expert_load(self._h, _addr(out)))
         return out
 

@@ -150,16 +150,17 @@ GTMOE_API int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, 
  *   gates     double[T*k] lastGates
  *   perm      int32[T*k]  lastRowsForExpert concatenated, e = 0..E-1
  *   load      int64[E]    lastExpertLoad
- * In expert-parallel handles T and x are this rank's tokens, and perm and
- * load cover the experts this rank owns.
+ * In expert-parallel handles T, x, out and the optional outputs are this
+ * rank's tokens: perm lists their rows in expert order and load counts them
+ * per expert (all n_routed experts).
  * With host output pointers the call returns after the results are there;
  * with device pointers it is asynchronous on the handle's stream. */
 GTMOE_API int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
                   void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load);
 
 /* MixtureOfExperts.LastExpertLoad (mixtureofexperts.go:287-291), int64[E]
- * (this rank's experts under expert parallelism).  GTMOE_ENOTREADY before
- * the first Forward. */
+ * (this rank's tokens under expert parallelism; gtmoe_update_balance uses the
+ * sum over ranks).  GTMOE_ENOTREADY before the first Forward. */
 GTMOE_API int gtmoe_last_expert_load(gtmoe_t h, int64_t *load);
 
 /* MixtureOfExperts.UpdateBalance (mixtureofexperts.go:293-310) from the last
