@@ -190,7 +190,7 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     mode = args.mode
     if mode == "auto":
         mode = "replicas" if world == 1 else "ep"
