@@ -272,22 +272,34 @@ def main():
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
+    # expert rows this rank ran: its tokens through the shared experts plus the
+    # rows routed to the experts it owns
+    if world > 1 and mode == "ep":
+        # each rank's load counts its own tokens; the owned experts' rows come from all ranks
+        load = torch.from_numpy(moe.last_expert_load()).to(dev)
+        dist.all_reduce(load)
+        el = cfg.n_routed // world
+        my_rows = cfg.n_shared * T_local + int(load[rank * el:(rank + 1) * el].sum())
+    else:
+        my_rows = (cfg.n_shared + cfg.k) * T_local
+    per_rank = [[ms, e2e_ms, float(my_rows)] + [phases[n] for n in _lib.PHASES]]
     if world > 1:
-        t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
-        ph = torch.tensor([phases[n] for n in _lib.PHASES], dtype=torch.float64, device=dev)
-        dist.all_reduce(ph, op=dist.ReduceOp.MAX)
-        phases = {n: float(ph[i]) for i, n in enumerate(_lib.PHASES)}
+        t = torch.tensor(per_rank[0], dtype=torch.float64, device=dev)
+        allv = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allv, t)
+        per_rank = [v.tolist() for v in allv]
+        ms = max(v[0] for v in per_rank)
+        e2e_ms = max(v[1] for v in per_rank)
+        phases = {n: max(v[3 + i] for v in per_rank) for i, n in enumerate(_lib.PHASES)}
 
     peaks = measured_peaks()
-    # dominant kernel: the grouped gate/up GEMM (2/3 of the expert FLOPs)
-    gate_up_flops = T_local * (cfg.k + cfg.n_shared) * 4.0 * cfg.d * cfg.h
-    down_flops = T_local * (cfg.k + cfg.n_shared) * 2.0 * cfg.d * cfg.h
-    kern = max((("expert_gate_up", gate_up_flops), ("expert_down", down_flops)),
-               key=lambda kv: phases[kv[0]])
-    kname, kflops = kern
-    kms = phases[kname]
+    # dominant kernel: the grouped gate/up GEMM (2/3 of the expert FLOPs), on
+    # the rank where it took longest, with that rank's own rows
+    ig, idn = 3 + _lib.PHASES.index("expert_gate_up"), 3 + _lib.PHASES.index("expert_down")
+    kname, col = max((("expert_gate_up", ig), ("expert_down", idn)), key=lambda kv: phases[kv[0]])
+    slow = max(per_rank, key=lambda v: v[col])
+    kms, rows = slow[col], slow[2]
+    kflops = rows * (4.0 if kname == "expert_gate_up" else 2.0) * cfg.d * cfg.h
     achieved = kflops / (kms * 1e-3) / 1e12 if kms > 0 else 0.0
     traffic = profiled_traffic(kname, cfg.name, T_local)
     roofline = {"kernel": kname, "bound": "tensor", "achieved": round(achieved, 2),
@@ -320,12 +332,15 @@ def main():
                        "tokens": cfg.T, "d_model": cfg.d, "hidden": cfg.h, "n_routed": cfg.n_routed,
                        "n_shared": cfg.n_shared, "top_k": cfg.k,
                        "parallelism": f"{mode}{world}" if world > 1 else "single",
-                       "l2": "inputs larger than L2 (x 512 MiB, weights 4.85 GB): no flush"},
+                       "l2": l2_note(cfg)},
             "e2e": {"value": round(T_total / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(T_local * cfg.d * 2), "d2h_bytes_per_step": int(T_local * cfg.d * 2)},
             "roofline": roofline,
             "cpu_baseline": cpu_baseline,
             "phases_ms": {k: round(v, 4) for k, v in phases.items()},
+            **({"ranks": [{"ms": round(v[0], 4), "expert_rows": int(v[2]),
+                           "phases_ms": {n: round(v[3 + i], 4) for i, n in enumerate(_lib.PHASES)}}
+                          for v in per_rank]} if world > 1 else {}),
             "gpu_launches": int(launches.value),
             "clocks": clocks,
         }
@@ -334,6 +349,16 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def l2_note(cfg) -> str:
+    """Why no L2 flush is needed between steps: the step's inputs exceed L2."""
+    l2 = 126 << 20
+    xb = cfg.T * cfg.d * (2 if cfg.x_bf16 else 8)
+    code = {0: 8.0, 1: 4.0, 2: 1.0 + 4 / 16, 3: 0.5 + 4 / 16}[cfg.precision]
+    wb = (cfg.n_routed + cfg.n_shared) * 3 * cfg.d * cfg.h * code
+    verdict = "no flush" if xb + wb > l2 else "weights and activations fit in L2: not flushed (warm-L2 figure)"
+    return f"x {xb / 2**20:.0f} MiB, expert weights {wb / 1e9:.2f} GB, L2 126 MiB: {verdict}"
 
 
 def profiled_traffic(kernel: str, config: str, T_local: int):

@@ -1,4 +1,4 @@
-// ep.cu -- expert parallelism across GPUs (one process per GPU, NCCL).
+// ep.cu -- expert parallelism across GPUs (one process per GPU).
 //
 // The reference runs MixtureOfExperts.Forward in one process
 // (mixtureofexperts.go:122-216); BASELINE's config 5 shards its routed
@@ -7,24 +7,30 @@
 //   1. route this rank's tokens (router.cu) and dispatch them over all E
 //      experts (dispatch.cu): the stable permutation orders (token, slot)
 //      rows by global expert, i.e. by destination rank, token-ascending;
-//   2. gather those rows (send buffer), all-gather every rank's per-expert
-//      counts (one G x E int64 exchange, one host synchronisation: message
-//      sizes must be known on the host);
-//   3. grouped ncclSend/ncclRecv of the rows; a segment copy regroups the
-//      received rows expert-major (source-ascending inside an expert, so an
-//      expert's rows are the reference's token order over the whole batch);
+//   2. all-gather every rank's per-expert counts and token count (NCCL, one
+//      G x (E+1) int64 exchange and one host synchronisation: the host needs
+//      the sizes for the group table and the buffers);
+//   3. the push kernel copies each (token, slot) row straight into the owning
+//      GPU's GEMM input over NVLink (CUDA IPC mappings of every rank's
+//      buffers): expert-major, source-ascending inside an expert, so an
+//      expert's rows are the reference's token order over the whole batch;
 //   4. the grouped SwiGLU kernels (shared experts on this rank's tokens,
 //      owned routed experts on the received rows);
-//   5. the inverse segment copy and the reverse exchange bring every output
-//      row back to its token's rank, where combine.cu adds them in the
+//   5. the return kernel copies every output row straight into its token's
+//      rank, at the (token, slot) position, where combine.cu adds them in the
 //      reference's order.
-// Remote rows always land in local buffers before any kernel reads them.
-// NCCL is loaded at run time (dlopen), only when an expert-parallel handle is
-// created.
+// A kernel that pushed rows fences them (system scope) and then increments
+// an arrival counter on every rank, once per CTA; the receiver's wait kernel
+// spins (bounded) until all G sources' CTAs of this step have arrived.
+// Buffers are reused across steps without a race: a rank pushes step n+1 only
+// after the step n+1 count all-gather, which no rank joins before its stream
+// has finished step n.  NCCL is loaded at run time (dlopen), only when an
+// expert-parallel handle is created.
 #include <dlfcn.h>
 #include <nccl.h>
 #include <string.h>
 
+#include <string>
 #include <vector>
 
 #include "handle.h"
@@ -40,10 +46,6 @@ struct NcclApi {
     ncclResult_t (*CommDestroy)(ncclComm_t);
     const char *(*GetErrorString)(ncclResult_t);
     ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
-    ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
-    ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
-    ncclResult_t (*GroupStart)();
-    ncclResult_t (*GroupEnd)();
 };
 NcclApi g_nccl;
 std::mutex g_nccl_mu;
@@ -60,9 +62,7 @@ int load_nccl() {
     } syms[] = {
         {"ncclGetUniqueId", (void **)&g_nccl.GetUniqueId},   {"ncclCommInitRank", (void **)&g_nccl.CommInitRank},
         {"ncclCommDestroy", (void **)&g_nccl.CommDestroy},   {"ncclGetErrorString", (void **)&g_nccl.GetErrorString},
-        {"ncclAllGather", (void **)&g_nccl.AllGather},       {"ncclSend", (void **)&g_nccl.Send},
-        {"ncclRecv", (void **)&g_nccl.Recv},                 {"ncclGroupStart", (void **)&g_nccl.GroupStart},
-        {"ncclGroupEnd", (void **)&g_nccl.GroupEnd},
+        {"ncclAllGather", (void **)&g_nccl.AllGather},
     };
     for (auto &s : syms) {
         *s.slot = dlsym(lib, s.name);
@@ -79,59 +79,266 @@ int load_nccl() {
             return ::gtmoe::fail(GTMOE_ENCCL, "%s failed: %s", #call, g_nccl.GetErrorString(r_));          \
     } while (0)
 
-// One contiguous block of rows moved between two buffers.
-struct Segment {
-    int64_t src_row, dst_row, rows;
+constexpr int kMaxEpRanks = 16;
+// Fixed grids of the push and return kernels: every rank knows how many
+// arrivals a step brings (G sources x this many CTAs).
+constexpr int kPushCtas = 1184;
+constexpr int kPushThreads = 256;
+constexpr int kSigForward = 0, kSigReturn = 1;
+
+struct PeerRows {
+    unsigned char *p[kMaxEpRanks];
+};
+struct PeerSigs {
+    unsigned long long *p[kMaxEpRanks];
 };
 
-__global__ void segment_copy_kernel(const uint4 *__restrict__ src, uint4 *__restrict__ dst,
-                                    const Segment *__restrict__ segs, int n_segs, int vec_per_row) {
-    for (int s = blockIdx.y; s < n_segs; s += gridDim.y) {
-        const Segment g = segs[s];
-        const int64_t n = g.rows * vec_per_row;
-        const uint4 *a = src + g.src_row * vec_per_row;
-        uint4 *b = dst + g.dst_row * vec_per_row;
-        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-            b[i] = a[i];
+// One run of consecutive output rows that returns to one rank.
+struct RetSeg {
+    int64_t src_row;  // first row in this rank's expert output buffer
+    int64_t dst_row;  // first (token, slot) position on the token's rank
+    int64_t rows;
+    int64_t rank;
+};
+
+__device__ __forceinline__ void copy_row(uint4 *__restrict__ dst, const uint4 *__restrict__ src, int nvec, int lane) {
+    int i = lane;
+    for (; i + 96 < nvec; i += 128) {
+        const uint4 a = __ldg(src + i), b = __ldg(src + i + 32), c = __ldg(src + i + 64), e = __ldg(src + i + 96);
+        dst[i] = a;
+        dst[i + 32] = b;
+        dst[i + 64] = c;
+        dst[i + 96] = e;
     }
+    for (; i < nvec; i += 32) dst[i] = __ldg(src + i);
+}
+
+// Every thread fences its own stores at system scope, then one thread per
+// rank adds this CTA's arrival to that rank's counter.
+__device__ __forceinline__ void signal_ranks(const PeerSigs &sig, int G, int which) {
+    __threadfence_system();
+    __syncthreads();
+    if ((int)threadIdx.x < G) atomicAdd_system(sig.p[threadIdx.x] + which, 1ull);
+}
+
+// Rows of this rank's (token, slot) pairs, in dispatch order, to the owning
+// ranks; then (copy_shared) all T token rows to this rank's own buffer after
+// its received rows, for the shared experts.
+__global__ void __launch_bounds__(kPushThreads) ep_push_kernel(
+    const uint4 *__restrict__ x, int vec_per_row, const int32_t *__restrict__ perm, int64_t TK,
+    const int64_t *__restrict__ offsets, int E, int El, const int64_t *__restrict__ dst_base, int64_t T,
+    int copy_shared, int64_t shared_row0, int rank, const __grid_constant__ PeerRows rows,
+    const __grid_constant__ PeerSigs sig, int G) {
+    extern __shared__ int64_t off_s[];  // E + 1 exclusive prefix of this rank's per-expert counts
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) off_s[e] = offsets[e];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int64_t n = TK + (copy_shared ? T : 0);
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < n; w += warps) {
+        if (w < TK) {
+            int lo = 0, hi = E;  // last e with off_s[e] <= w
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (off_s[mid] <= w) lo = mid;
+                else hi = mid;
+            }
+            const int q = lo / El;
+            const int64_t dst = dst_base[lo] + (w - off_s[lo]);
+            copy_row((uint4 *)rows.p[q] + dst * vec_per_row, x + (int64_t)perm[w] * vec_per_row, vec_per_row, lane);
+        } else {
+            const int64_t t = w - TK;
+            copy_row((uint4 *)rows.p[rank] + (shared_row0 + t) * vec_per_row, x + t * vec_per_row, vec_per_row,
+                     lane);
+        }
+    }
+    signal_ranks(sig, G, kSigForward);
+}
+
+// Expert output rows back to their tokens' ranks.
+__global__ void __launch_bounds__(kPushThreads) ep_return_kernel(
+    const uint4 *__restrict__ y, int vec_per_row, const RetSeg *__restrict__ segs, int n_segs, int64_t row0,
+    int64_t n_rows, const __grid_constant__ PeerRows rows, const __grid_constant__ PeerSigs sig, int G) {
+    extern __shared__ int64_t start_s[];  // first row (relative to row0) of each segment
+    for (int i = threadIdx.x; i < n_segs; i += blockDim.x) start_s[i] = segs[i].src_row - row0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < n_rows; w += warps) {
+        int lo = 0, hi = n_segs;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (start_s[mid] <= w) lo = mid;
+            else hi = mid;
+        }
+        const RetSeg g = segs[lo];
+        const int64_t dst = g.dst_row + (w - start_s[lo]);
+        copy_row((uint4 *)rows.p[g.rank] + dst * vec_per_row, y + (row0 + w) * vec_per_row, vec_per_row, lane);
+    }
+    signal_ranks(sig, G, kSigReturn);
+}
+
+// Bounded wait until this rank's arrival counter reaches `target`.
+__global__ void ep_wait_kernel(const unsigned long long *counter, unsigned long long target, int *err, int code) {
+    if (threadIdx.x != 0) return;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counter) : "memory");
+        if (v >= target) break;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicCAS(err, 0, code);
+            return;
+        }
+        __nanosleep(256);
+    }
+    // the next kernels read the rows with TMA (async proxy)
+    asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 }  // namespace
 
 struct EpState {
     ncclComm_t comm = nullptr;
-    DevBuf gathered_load;  // G x E int64 (device)
+    int G = 1, r = 0;
+    DevBuf gathered;  // G x (E + 1) int64: per-expert counts, then the token count (device)
     std::vector<int64_t> h_gathered;
     int have_gathered = 0;
-    DevBuf sendbuf, recvbuf, yback, yret, segs_fwd, segs_back;
+    unsigned long long epoch = 0;  // completed exchanges (same on every rank)
+    // IPC-shared buffers: the GEMM input (received rows, then own token rows)
+    // and the returned expert outputs ((token, slot) order); capacities in
+    // bytes, tracked identically on every rank
+    void *x_local = nullptr, *y_local = nullptr, *sig_local = nullptr;
+    std::vector<void *> peer_x, peer_y, peer_sig;
+    std::vector<size_t> cap_x, cap_y;
+    int *err = nullptr;
+    DevBuf staging, xconv, dst_base, ret_segs;
 };
 
 static EpState *ep_of(gtmoe_handle *h) { return (EpState *)h->ep; }
 
+// NCCL all-gather of `n` bytes per rank through device staging (host in, host out).
+static int allgather_bytes(EpState *ep, const void *mine, size_t n, void *all, cudaStream_t st) {
+    GT_CHECK(ep->staging.ensure(n * ep->G));
+    unsigned char *base = (unsigned char *)ep->staging.p;
+    GT_CUDA(cudaMemcpyAsync(base + n * ep->r, mine, n, cudaMemcpyHostToDevice, st));
+    GT_NCCL(g_nccl.AllGather(base + n * ep->r, base, n, ncclUint8, ep->comm, st));
+    GT_CUDA(cudaMemcpyAsync(all, base, n * ep->G, cudaMemcpyDeviceToHost, st));
+    GT_CUDA(cudaStreamSynchronize(st));
+    return 0;
+}
+
+static void close_peer(void *&p) {
+    if (p) cudaIpcCloseMemHandle(p);
+    p = nullptr;
+}
+
 void ep_destroy(gtmoe_handle *h) {
     EpState *ep = ep_of(h);
     if (!ep) return;
+    cudaSetDevice(h->device);
+    cudaStreamSynchronize(h->stream);
+    for (int q = 0; q < ep->G; q++) {
+        if (q == ep->r) continue;
+        if (q < (int)ep->peer_x.size()) close_peer(ep->peer_x[q]);
+        if (q < (int)ep->peer_y.size()) close_peer(ep->peer_y[q]);
+        if (q < (int)ep->peer_sig.size()) close_peer(ep->peer_sig[q]);
+    }
     if (ep->comm && g_nccl.loaded) g_nccl.CommDestroy(ep->comm);
-    DevBuf *bufs[] = {&ep->gathered_load, &ep->sendbuf, &ep->recvbuf, &ep->yback, &ep->yret, &ep->segs_fwd,
-                      &ep->segs_back};
+    for (void *p : {ep->x_local, ep->y_local, ep->sig_local, (void *)ep->err})
+        if (p) cudaFree(p);
+    DevBuf *bufs[] = {&ep->gathered, &ep->staging, &ep->xconv, &ep->dst_base, &ep->ret_segs};
     for (DevBuf *b : bufs) b->release();
     delete ep;
     h->ep = nullptr;
 }
 
-static int segment_copy(const void *src, void *dst, const std::vector<Segment> &segs, DevBuf &table,
-                        size_t row_bytes, cudaStream_t st) {
-    if (segs.empty()) return 0;
-    if (row_bytes % 16 != 0) return fail(GTMOE_EINVAL, "expert-parallel rows must be a multiple of 16 bytes");
-    GT_CHECK(table.ensure(sizeof(Segment) * segs.size()));
-    GT_CUDA(cudaMemcpyAsync(table.p, segs.data(), sizeof(Segment) * segs.size(), cudaMemcpyHostToDevice, st));
-    dim3 grid(8, (unsigned)(segs.size() < 65535 ? segs.size() : 65535));
-    segment_copy_kernel<<<grid, 256, 0, st>>>((const uint4 *)src, (uint4 *)dst, table.as<Segment>(), (int)segs.size(),
-                                              (int)(row_bytes / 16));
-    GT_CUDA(cudaGetLastError());
-    note_launches(1);
-    // the host table must outlive the copy: wait for it before returning
+// Maps every rank's signal counters (once, at creation).
+static int ep_map_signals(gtmoe_handle *h, EpState *ep) {
+    const int G = ep->G;
+    GT_CUDA(cudaMalloc(&ep->sig_local, 256));
+    GT_CUDA(cudaMemset(ep->sig_local, 0, 256));
+    GT_CUDA(cudaMalloc(&ep->err, sizeof(int)));
+    GT_CUDA(cudaMemset(ep->err, 0, sizeof(int)));
+    GT_CUDA(cudaDeviceSynchronize());
+    cudaIpcMemHandle_t mine;
+    GT_CUDA(cudaIpcGetMemHandle(&mine, ep->sig_local));
+    std::vector<cudaIpcMemHandle_t> all(G);
+    GT_CHECK(allgather_bytes(ep, &mine, sizeof(mine), all.data(), h->stream));
+    ep->peer_sig.assign(G, nullptr);
+    ep->peer_x.assign(G, nullptr);
+    ep->peer_y.assign(G, nullptr);
+    ep->cap_x.assign(G, 0);
+    ep->cap_y.assign(G, 0);
+    for (int q = 0; q < G; q++) {
+        if (q == ep->r) {
+            ep->peer_sig[q] = ep->sig_local;
+            continue;
+        }
+        GT_CUDA(cudaIpcOpenMemHandle(&ep->peer_sig[q], all[q], cudaIpcMemLazyEnablePeerAccess));
+    }
+    return 0;
+}
+
+// Grows the IPC-shared row buffers of every rank that needs more than it has
+// (a collective step: every rank takes it with the same sizes).
+static int ep_ensure_buffers(gtmoe_handle *h, EpState *ep, const std::vector<size_t> &need_x,
+                             const std::vector<size_t> &need_y) {
+    const int G = ep->G, r = ep->r;
+    std::vector<char> grow(G, 0);
+    bool any = false;
+    for (int q = 0; q < G; q++)
+        if (need_x[q] > ep->cap_x[q] || need_y[q] > ep->cap_y[q]) grow[q] = 1, any = true;
+    if (!any) return 0;
+    cudaStream_t st = h->stream;
+    // 1. drop the mappings of buffers about to be replaced; 2. wait until
+    // every rank has (nobody frees a buffer a peer still maps)
+    for (int q = 0; q < G; q++)
+        if (grow[q] && q != r) close_peer(ep->peer_x[q]), close_peer(ep->peer_y[q]);
     GT_CUDA(cudaStreamSynchronize(st));
+    int token = 1;
+    std::vector<int> tokens(G);
+    GT_CHECK(allgather_bytes(ep, &token, sizeof(int), tokens.data(), st));
+    // 3. new capacities (a quarter of headroom), the same on every rank
+    auto grown = [](size_t cap, size_t need) {
+        size_t c = need <= cap ? cap : need + need / 4;
+        if (c < 4096) c = 4096;
+        return (c + 255) / 256 * 256;
+    };
+    for (int q = 0; q < G; q++)
+        if (grow[q]) {
+            ep->cap_x[q] = grown(ep->cap_x[q], need_x[q]);
+            ep->cap_y[q] = grown(ep->cap_y[q], need_y[q]);
+        }
+    struct {
+        cudaIpcMemHandle_t x, y;
+    } mine, zero;
+    memset(&mine, 0, sizeof(mine));
+    memset(&zero, 0, sizeof(zero));
+    if (grow[r]) {
+        if (ep->x_local) cudaFree(ep->x_local);
+        if (ep->y_local) cudaFree(ep->y_local);
+        ep->x_local = ep->y_local = nullptr;
+        cudaError_t e1 = cudaMalloc(&ep->x_local, ep->cap_x[r]);
+        cudaError_t e2 = e1 == cudaSuccess ? cudaMalloc(&ep->y_local, ep->cap_y[r]) : e1;
+        if (e1 != cudaSuccess || e2 != cudaSuccess) {
+            cudaGetLastError();
+            return fail(GTMOE_ENOMEM, "expert-parallel buffers of %zu + %zu bytes: %s", ep->cap_x[r], ep->cap_y[r],
+                        cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
+        }
+        GT_CUDA(cudaIpcGetMemHandle(&mine.x, ep->x_local));
+        GT_CUDA(cudaIpcGetMemHandle(&mine.y, ep->y_local));
+        ep->peer_x[r] = ep->x_local;
+        ep->peer_y[r] = ep->y_local;
+    }
+    // 4. everybody's handles; open the new ones
+    std::vector<decltype(mine)> all(G);
+    GT_CHECK(allgather_bytes(ep, &mine, sizeof(mine), all.data(), st));
+    for (int q = 0; q < G; q++) {
+        if (!grow[q] || q == r) continue;
+        GT_CUDA(cudaIpcOpenMemHandle(&ep->peer_x[q], all[q].x, cudaIpcMemLazyEnablePeerAccess));
+        GT_CUDA(cudaIpcOpenMemHandle(&ep->peer_y[q], all[q].y, cudaIpcMemLazyEnablePeerAccess));
+    }
     return 0;
 }
 
@@ -146,7 +353,7 @@ int ep_global_load(gtmoe_handle *h, int64_t *load) {
     if (!ep->have_gathered) return fail(GTMOE_ENOTREADY, "no Forward yet");
     for (int e = 0; e < E; e++) {
         int64_t s = 0;
-        for (int r = 0; r < h->n_ranks; r++) s += ep->h_gathered[(size_t)r * E + e];
+        for (int r = 0; r < h->n_ranks; r++) s += ep->h_gathered[(size_t)r * (E + 1) + e];
         load[e] = s;
     }
     return 0;
@@ -166,6 +373,8 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
                                                             : GTMOE_DTYPE_F32;
     const size_t cs = dtype_size(compute);
     const size_t row_bytes = cs * d;
+    if (row_bytes % 16 != 0) return fail(GTMOE_EINVAL, "expert-parallel rows must be a multiple of 16 bytes");
+    const int vec = (int)(row_bytes / 16);
     const int64_t TK = T * k;
     const int n_chunks = (int)((T + kDispatchChunk - 1) / kDispatchChunk);
 
@@ -217,7 +426,7 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     GT_CHECK(h->gates64.ensure(sizeof(double) * (size_t)(TK > 0 ? TK : 1)));
     GT_CHECK(h->gates32.ensure(sizeof(float) * (size_t)(TK > 0 ? TK : 1)));
     GT_CHECK(h->counts.ensure(sizeof(int32_t) * (size_t)(n_chunks > 0 ? n_chunks : 1) * E));
-    GT_CHECK(h->load.ensure(sizeof(int64_t) * E));
+    GT_CHECK(h->load.ensure(sizeof(int64_t) * (E + 1)));
     GT_CHECK(h->offsets.ensure(sizeof(int64_t) * (E + 1)));
     GT_CHECK(h->perm.ensure(sizeof(int32_t) * (size_t)(TK > 0 ? TK : 1)));
     GT_CHECK(h->slot_row.ensure(sizeof(int64_t) * (size_t)(TK > 0 ? TK : 1)));
@@ -225,9 +434,8 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     GT_CHECK(h->tile_prefix.ensure(sizeof(int64_t) * (S + E + 1)));
     GT_CHECK(h->fixups.ensure(sizeof(int)));
     GT_CHECK(h->flagged.ensure(sizeof(int) * (size_t)(T > 0 ? T : 1)));
-    GT_CHECK(ep->gathered_load.ensure(sizeof(int64_t) * (size_t)G * E));
-    GT_CHECK(ep->sendbuf.ensure(row_bytes * (size_t)(TK > 0 ? TK : 1)));
-    GT_CHECK(ep->yret.ensure(row_bytes * (size_t)(TK > 0 ? TK : 1)));
+    GT_CHECK(ep->gathered.ensure(sizeof(int64_t) * (size_t)G * (E + 1)));
+    GT_CHECK(ep->dst_base.ensure(sizeof(int64_t) * E));
     GT_CHECK(refresh_table(h));
 
     RouterArgs ra;
@@ -277,80 +485,109 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     GT_CHECK(launch_dispatch(da, st));
     GT_CHECK(h->phase_end(1));
 
-    // ---- send rows in global-expert order, and everybody's per-expert counts
+    // ---- everybody's per-expert counts and token counts
     GT_CHECK(h->phase_begin(6));
-    GT_CHECK(launch_gather(x_dev, x_dtype, T, d, da.perm, TK, 0, 0, ep->sendbuf.p, compute, st));
-    GT_NCCL(g_nccl.AllGather(h->load.p, ep->gathered_load.p, (size_t)E, ncclInt64, ep->comm, st));
-    ep->h_gathered.resize((size_t)G * E);
-    GT_CUDA(cudaMemcpyAsync(ep->h_gathered.data(), ep->gathered_load.p, sizeof(int64_t) * G * E,
+    const int64_t T_mine = T;
+    GT_CUDA(cudaMemcpyAsync(h->load.as<int64_t>() + E, &T_mine, sizeof(int64_t), cudaMemcpyHostToDevice, st));
+    GT_NCCL(g_nccl.AllGather(h->load.p, ep->gathered.p, (size_t)(E + 1), ncclInt64, ep->comm, st));
+    ep->h_gathered.resize((size_t)G * (E + 1));
+    GT_CUDA(cudaMemcpyAsync(ep->h_gathered.data(), ep->gathered.p, sizeof(int64_t) * G * (E + 1),
                             cudaMemcpyDeviceToHost, st));
     GT_CUDA(cudaStreamSynchronize(st));
     ep->have_gathered = 1;
-    const int64_t *Lg = ep->h_gathered.data();  // Lg[s * E + e]: rows of rank s for expert e
-    std::vector<int64_t> send_cnt(G, 0), send_off(G + 1, 0), recv_cnt(G, 0), recv_off(G + 1, 0), tot(El, 0),
-        eoff(El + 1, 0);
-    for (int q = 0; q < G; q++)
-        for (int e = q * El; e < (q + 1) * El; e++) send_cnt[q] += Lg[(size_t)r * E + e];
-    for (int s = 0; s < G; s++)
-        for (int el = 0; el < El; el++) {
-            const int64_t n = Lg[(size_t)s * E + r * El + el];
-            recv_cnt[s] += n;
-            tot[el] += n;
+    const int64_t *hg = ep->h_gathered.data();
+    auto L = [&](int s, int e) { return hg[(size_t)s * (E + 1) + e]; };  // rows of rank s for expert e
+    auto Tof = [&](int s) { return hg[(size_t)s * (E + 1) + E]; };
+    // eoff[e]: first row of expert e in its owner's received block (expert-major)
+    std::vector<int64_t> eoff(E, 0), n_recv(G, 0);
+    for (int q = 0; q < G; q++) {
+        int64_t run = 0;
+        for (int e = q * El; e < (q + 1) * El; e++) {
+            eoff[e] = run;
+            for (int s = 0; s < G; s++) run += L(s, e);
         }
-    for (int q = 0; q < G; q++) send_off[q + 1] = send_off[q] + send_cnt[q];
-    for (int s = 0; s < G; s++) recv_off[s + 1] = recv_off[s] + recv_cnt[s];
-    for (int el = 0; el < El; el++) eoff[el + 1] = eoff[el] + tot[el];
-    const int64_t n_recv = recv_off[G];
-    const int64_t xbase = S > 0 ? T : 0;
-    const int64_t rows_x = xbase + n_recv;
-    const int64_t rows_h = (int64_t)S * T + n_recv;
-    GT_CHECK(ep->recvbuf.ensure(row_bytes * (size_t)(n_recv > 0 ? n_recv : 1)));
-    GT_CHECK(ep->yback.ensure(row_bytes * (size_t)(n_recv > 0 ? n_recv : 1)));
-    GT_CHECK(h->xp.ensure(row_bytes * (size_t)(rows_x > 0 ? rows_x : 1)));
-    GT_CHECK(h->hp.ensure(cs * (size_t)hd * (rows_h > 0 ? rows_h : 1)));
-    GT_CHECK(h->yp.ensure(row_bytes * (size_t)(rows_h > 0 ? rows_h : 1)));
-
-    GT_NCCL(g_nccl.GroupStart());
-    for (int q = 0; q < G; q++)
-        if (send_cnt[q] > 0)
-            GT_NCCL(g_nccl.Send((const char *)ep->sendbuf.p + send_off[q] * row_bytes, send_cnt[q] * row_bytes,
-                                ncclUint8, q, ep->comm, st));
-    for (int s = 0; s < G; s++)
-        if (recv_cnt[s] > 0)
-            GT_NCCL(g_nccl.Recv((char *)ep->recvbuf.p + recv_off[s] * row_bytes, recv_cnt[s] * row_bytes, ncclUint8,
-                                s, ep->comm, st));
-    GT_NCCL(g_nccl.GroupEnd());
-
-    // received [source][expert] -> expert-major, source-ascending
-    std::vector<Segment> fwd, back;
-    for (int el = 0; el < El; el++) {
-        int64_t dst = eoff[el];
-        for (int s = 0; s < G; s++) {
-            int64_t src = recv_off[s];
-            for (int e2 = 0; e2 < el; e2++) src += Lg[(size_t)s * E + r * El + e2];
-            const int64_t n = Lg[(size_t)s * E + r * El + el];
-            if (n > 0) {
-                fwd.push_back({src, xbase + dst, n});
-                back.push_back({(int64_t)S * T + dst, src, n});
-            }
-            dst += n;
-        }
+        n_recv[q] = run;
     }
-    if (S > 0) GT_CHECK(launch_gather(x_dev, x_dtype, T, d, nullptr, 0, 0, 1, h->xp.p, compute, st));
-    GT_CHECK(segment_copy(ep->recvbuf.p, h->xp.p, fwd, ep->segs_fwd, row_bytes, st));
-    GT_CHECK(h->phase_end(6));
+    std::vector<size_t> need_x(G), need_y(G);
+    for (int q = 0; q < G; q++) {
+        need_x[q] = row_bytes * (size_t)(n_recv[q] + (S > 0 ? Tof(q) : 0));
+        need_y[q] = row_bytes * (size_t)(Tof(q) * k);
+    }
+    GT_CHECK(ep_ensure_buffers(h, ep, need_x, need_y));
 
-    // ---- group table of this rank: shared experts on its tokens, owned experts on received rows
+    // where this rank's rows for expert e start in the owner's block
+    std::vector<int64_t> dst_base(E);
+    for (int e = 0; e < E; e++) {
+        int64_t b = eoff[e];
+        for (int s = 0; s < r; s++) b += L(s, e);
+        dst_base[e] = b;
+    }
+    // this rank's group table: owned experts on the received rows, shared
+    // experts on its own tokens (after the received rows)
+    const int64_t nr = n_recv[r];
+    const int64_t rows_x = nr + (S > 0 ? T : 0);
+    const int64_t rows_h = (int64_t)S * T + nr;
     std::vector<Group> groups(S + El);
     std::vector<int64_t> prefix(S + El + 1, 0);
     const int bm = use_tc ? tc_tile_rows(h->tc) : kSimtBM;
-    for (int s = 0; s < S; s++) groups[s] = Group{0, (int64_t)s * T, T, s, 0};
-    for (int el = 0; el < El; el++) groups[S + el] = Group{xbase + eoff[el], (int64_t)S * T + eoff[el], tot[el], S + el, 0};
+    for (int s = 0; s < S; s++) groups[s] = Group{nr, (int64_t)s * T, T, s, 0};
+    std::vector<int64_t> tot(El, 0);
+    for (int el = 0; el < El; el++) {
+        for (int s = 0; s < G; s++) tot[el] += L(s, r * El + el);
+        groups[S + el] = Group{eoff[r * El + el], (int64_t)S * T + eoff[r * El + el], tot[el], S + el, 0};
+    }
     for (int g = 0; g < S + El; g++) prefix[g + 1] = prefix[g] + (groups[g].m + bm - 1) / bm;
+    // output rows back: (owned expert, source) runs to the source's (token, slot) positions
+    std::vector<RetSeg> back;
+    for (int el = 0; el < El; el++) {
+        const int e = r * El + el;
+        int64_t src = (int64_t)S * T + eoff[e];
+        for (int s = 0; s < G; s++) {
+            const int64_t n = L(s, e);
+            if (n > 0) {
+                int64_t slot = 0;  // exclusive prefix of rank s's counts
+                for (int e2 = 0; e2 < e; e2++) slot += L(s, e2);
+                back.push_back(RetSeg{src, slot, n, s});
+            }
+            src += n;
+        }
+    }
+    GT_CUDA(cudaMemcpyAsync(ep->dst_base.p, dst_base.data(), sizeof(int64_t) * E, cudaMemcpyHostToDevice, st));
     GT_CUDA(cudaMemcpyAsync(h->groups.p, groups.data(), sizeof(Group) * (S + El), cudaMemcpyHostToDevice, st));
     GT_CUDA(cudaMemcpyAsync(h->tile_prefix.p, prefix.data(), sizeof(int64_t) * (S + El + 1), cudaMemcpyHostToDevice,
                             st));
+    if (!back.empty()) {
+        GT_CHECK(ep->ret_segs.ensure(sizeof(RetSeg) * back.size()));
+        GT_CUDA(cudaMemcpyAsync(ep->ret_segs.p, back.data(), sizeof(RetSeg) * back.size(), cudaMemcpyHostToDevice,
+                                st));
+    }
+    PeerRows px, py;
+    PeerSigs sg;
+    for (int q = 0; q < kMaxEpRanks; q++) {
+        px.p[q] = q < G ? (unsigned char *)ep->peer_x[q] : nullptr;
+        py.p[q] = q < G ? (unsigned char *)ep->peer_y[q] : nullptr;
+        sg.p[q] = q < G ? (unsigned long long *)ep->peer_sig[q] : nullptr;
+    }
+    // rows in the compute type, token order
+    const void *xrows = x_dev;
+    if (T > 0 && x_dtype != compute) {
+        GT_CHECK(ep->xconv.ensure(row_bytes * (size_t)T));
+        GT_CHECK(launch_gather(x_dev, x_dtype, T, d, nullptr, 0, 0, 1, ep->xconv.p, compute, st));
+        xrows = ep->xconv.p;
+    }
+    ep->epoch++;
+    const unsigned long long arrivals = ep->epoch * (unsigned long long)G * kPushCtas;
+    ep_push_kernel<<<kPushCtas, kPushThreads, sizeof(int64_t) * (E + 1), st>>>(
+        (const uint4 *)xrows, vec, da.perm, TK, da.offsets, E, El, ep->dst_base.as<int64_t>(), T, S > 0 ? 1 : 0, nr,
+        r, px, sg, G);
+    GT_CUDA(cudaGetLastError());
+    ep_wait_kernel<<<1, 32, 0, st>>>((unsigned long long *)ep->sig_local + kSigForward, arrivals, ep->err, 1);
+    GT_CUDA(cudaGetLastError());
+    note_launches(2);
+    GT_CHECK(h->phase_end(6));
 
+    GT_CHECK(h->hp.ensure(cs * (size_t)hd * (rows_h > 0 ? rows_h : 1)));
+    GT_CHECK(h->yp.ensure(row_bytes * (size_t)(rows_h > 0 ? rows_h : 1)));
     if (rows_h > 0) {
         if (use_tc) {
             TcArgs ta;
@@ -359,7 +596,7 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
             ta.tile_prefix = h->tile_prefix.as<int64_t>();
             ta.rows_x = rows_x;
             ta.rows_h = rows_h;
-            ta.xp = h->xp.p;
+            ta.xp = ep->x_local;
             ta.hp = h->hp.p;
             ta.yp = h->yp.p;
             GT_CHECK(launch_grouped_tc(h, h->tc, ta, st));
@@ -375,7 +612,7 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
             ga.h = hd;
             ga.clamped = c.clamped;
             ga.clamp_limit = c.clamp_limit;
-            ga.xp = h->xp.p;
+            ga.xp = ep->x_local;
             ga.hp = h->hp.p;
             ga.yp = h->yp.p;
             GT_CHECK(h->phase_begin(3));
@@ -386,22 +623,15 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
             GT_CHECK(h->phase_end(4));
         }
     }
-    // keep the host tables alive until their copies ran
-    GT_CUDA(cudaStreamSynchronize(st));
-
     // ---- outputs back to the tokens' ranks
     GT_CHECK(h->phase_begin(7));
-    GT_CHECK(segment_copy(h->yp.p, ep->yback.p, back, ep->segs_back, row_bytes, st));
-    GT_NCCL(g_nccl.GroupStart());
-    for (int s = 0; s < G; s++)
-        if (recv_cnt[s] > 0)
-            GT_NCCL(g_nccl.Send((const char *)ep->yback.p + recv_off[s] * row_bytes, recv_cnt[s] * row_bytes,
-                                ncclUint8, s, ep->comm, st));
-    for (int q = 0; q < G; q++)
-        if (send_cnt[q] > 0)
-            GT_NCCL(g_nccl.Recv((char *)ep->yret.p + send_off[q] * row_bytes, send_cnt[q] * row_bytes, ncclUint8, q,
-                                ep->comm, st));
-    GT_NCCL(g_nccl.GroupEnd());
+    ep_return_kernel<<<kPushCtas, kPushThreads, sizeof(int64_t) * (back.empty() ? 1 : back.size()), st>>>(
+        (const uint4 *)h->yp.p, vec, ep->ret_segs.as<RetSeg>(), (int)back.size(), (int64_t)S * T, back.empty() ? 0 : nr,
+        py, sg, G);
+    GT_CUDA(cudaGetLastError());
+    ep_wait_kernel<<<1, 32, 0, st>>>((unsigned long long *)ep->sig_local + kSigReturn, arrivals, ep->err, 2);
+    GT_CUDA(cudaGetLastError());
+    note_launches(2);
     GT_CHECK(h->phase_end(7));
 
     CombineArgs ca;
@@ -410,7 +640,7 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     ca.k = k;
     ca.S = S;
     ca.y = h->yp.p;
-    ca.y_routed = ep->yret.p;
+    ca.y_routed = ep->y_local;
     ca.y_dtype = compute;
     ca.shared_row0 = 0;
     ca.routed_row0 = 0;
@@ -433,6 +663,12 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     if (perm_out && TK) GT_CUDA(cudaMemcpyAsync(perm_out, h->perm.p, sizeof(int32_t) * TK, cudaMemcpyDefault, st));
     if (load_out) GT_CUDA(cudaMemcpyAsync(load_out, h->load.p, sizeof(int64_t) * E, cudaMemcpyDefault, st));
     GT_CUDA(cudaStreamSynchronize(st));
+    int werr = 0;
+    GT_CUDA(cudaMemcpy(&werr, ep->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (werr)
+        return fail(GTMOE_ETIMEOUT,
+                    "expert-parallel exchange gave up waiting for the other ranks' %s; the handle is unusable",
+                    werr == 1 ? "token rows" : "expert outputs");
     GT_CHECK(tc_check_error(h->tc));
     return 0;
 }
@@ -462,11 +698,23 @@ int gtmoe_create_ep(const gtmoe_config *cfg, int device, int n_ranks, int rank, 
     h->ep = ep;
     ncclUniqueId id;
     memcpy(&id, nccl_id_128, sizeof(id));
+    if (n_ranks > kMaxEpRanks) {
+        gtmoe_destroy(h);
+        return fail(GTMOE_EINVAL, "at most %d expert-parallel ranks, got %d", kMaxEpRanks, n_ranks);
+    }
+    ep->G = n_ranks;
+    ep->r = rank;
     ncclResult_t r = g_nccl.CommInitRank(&ep->comm, n_ranks, id, rank);
     if (r != ncclSuccess) {
         ep->comm = nullptr;
         gtmoe_destroy(h);
         return fail(GTMOE_ENCCL, "ncclCommInitRank failed: %s", g_nccl.GetErrorString(r));
+    }
+    int rc = ep_map_signals(h, ep);
+    if (rc != 0) {
+        std::string msg = gtmoe_last_error();
+        gtmoe_destroy(h);
+        return fail(rc, "%s", msg.c_str());
     }
     *out = h;
     return 0;
