@@ -586,17 +586,24 @@ int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_
     std::lock_guard<std::mutex> lock(h->mu);
     GT_CUDA(cudaSetDevice(h->device));
     const gtmoe_config &c = h->cfg;
-    if (T < 0) return fail(GTMOE_EINVAL, "mixture of experts: negative number of rows %lld", (long long)T);
-    if (T > 0 && (!x || !out)) return fail(GTMOE_EINVAL, "mixture of experts: x and out must be given");
-    if (x_dtype < GTMOE_DTYPE_F64 || x_dtype > GTMOE_DTYPE_BF16 || out_dtype < GTMOE_DTYPE_F64 ||
-        out_dtype > GTMOE_DTYPE_BF16)
-        return fail(GTMOE_EINVAL, "unknown dtype");
-    if (c.hash_routing && T > 0 && !token_ids)
-        return fail(GTMOE_EINVAL, "mixture of experts: hash routing needs one token ID per row, got none for %lld rows",
-                    (long long)T);
-    GT_CHECK(all_layers_set(h));
+    auto check_args = [&]() -> int {
+        if (T < 0) return fail(GTMOE_EINVAL, "mixture of experts: negative number of rows %lld", (long long)T);
+        if (T > 0 && (!x || !out)) return fail(GTMOE_EINVAL, "mixture of experts: x and out must be given");
+        if (x_dtype < GTMOE_DTYPE_F64 || x_dtype > GTMOE_DTYPE_BF16 || out_dtype < GTMOE_DTYPE_F64 ||
+            out_dtype > GTMOE_DTYPE_BF16)
+            return fail(GTMOE_EINVAL, "unknown dtype");
+        if (c.hash_routing && T > 0 && !token_ids)
+            return fail(GTMOE_EINVAL,
+                        "mixture of experts: hash routing needs one token ID per row, got none for %lld rows",
+                        (long long)T);
+        return all_layers_set(h);
+    };
+    const int arg_rc = check_args();
+    // expert parallel: a rank whose arguments are wrong still joins the
+    // step's count exchange, so that every rank fails instead of waiting
     if (h->n_ranks > 1)
-        return ep_forward(h, x, x_dtype, T, token_ids, residual, out, out_dtype, chosen, gates, perm, load);
+        return ep_forward(h, x, x_dtype, T, token_ids, residual, out, out_dtype, chosen, gates, perm, load, arg_rc);
+    if (arg_rc != 0) return arg_rc;
 
     cudaStream_t st = h->stream;
     const int d = c.d_model, k = c.experts_per_token, E = c.n_routed;

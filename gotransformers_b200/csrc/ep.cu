@@ -113,12 +113,20 @@ __device__ __forceinline__ void copy_row(uint4 *__restrict__ dst, const uint4 *_
     for (; i < nvec; i += 32) dst[i] = __ldg(src + i);
 }
 
-// Every thread fences its own stores at system scope, then one thread per
-// rank adds this CTA's arrival to that rank's counter.
-__device__ __forceinline__ void signal_ranks(const PeerSigs &sig, int G, int which) {
+// Every thread fences its own stores at system scope; the last CTA of the
+// launch to get here then adds one arrival to every rank's counter `which`
+// (`done` counts the launch's finished CTAs and is reset for the next launch).
+__device__ __forceinline__ void signal_ranks(const PeerSigs &sig, int G, int which, unsigned int *done) {
     __threadfence_system();
     __syncthreads();
-    if ((int)threadIdx.x < G) atomicAdd_system(sig.p[threadIdx.x] + which, 1ull);
+    if (threadIdx.x == 0) {
+        const unsigned int n = atomicAdd(done, 1u);
+        if (n == gridDim.x - 1) {
+            *done = 0;
+            __threadfence_system();
+            for (int q = 0; q < G; q++) atomicAdd_system(sig.p[q] + which, 1ull);
+        }
+    }
 }
 
 // Rows of this rank's (token, slot) pairs, in dispatch order, to the owning
@@ -128,7 +136,7 @@ __global__ void __launch_bounds__(kPushThreads) ep_push_kernel(
     const uint4 *__restrict__ x, int vec_per_row, const int32_t *__restrict__ perm, int64_t TK,
     const int64_t *__restrict__ offsets, int E, int El, const int64_t *__restrict__ dst_base, int64_t T,
     int copy_shared, int64_t shared_row0, int rank, const __grid_constant__ PeerRows rows,
-    const __grid_constant__ PeerSigs sig, int G) {
+    const __grid_constant__ PeerSigs sig, int G, unsigned int *done) {
     extern __shared__ int64_t off_s[];  // E + 1 exclusive prefix of this rank's per-expert counts
     for (int e = threadIdx.x; e <= E; e += blockDim.x) off_s[e] = offsets[e];
     __syncthreads();
@@ -152,13 +160,14 @@ __global__ void __launch_bounds__(kPushThreads) ep_push_kernel(
                      lane);
         }
     }
-    signal_ranks(sig, G, kSigForward);
+    signal_ranks(sig, G, kSigForward, done);
 }
 
 // Expert output rows back to their tokens' ranks.
 __global__ void __launch_bounds__(kPushThreads) ep_return_kernel(
     const uint4 *__restrict__ y, int vec_per_row, const RetSeg *__restrict__ segs, int n_segs, int64_t row0,
-    int64_t n_rows, const __grid_constant__ PeerRows rows, const __grid_constant__ PeerSigs sig, int G) {
+    int64_t n_rows, const __grid_constant__ PeerRows rows, const __grid_constant__ PeerSigs sig, int G,
+    unsigned int *done) {
     extern __shared__ int64_t start_s[];  // first row (relative to row0) of each segment
     for (int i = threadIdx.x; i < n_segs; i += blockDim.x) start_s[i] = segs[i].src_row - row0;
     __syncthreads();
@@ -175,7 +184,24 @@ __global__ void __launch_bounds__(kPushThreads) ep_return_kernel(
         const int64_t dst = g.dst_row + (w - start_s[lo]);
         copy_row((uint4 *)rows.p[g.rank] + dst * vec_per_row, y + (row0 + w) * vec_per_row, vec_per_row, lane);
     }
-    signal_ranks(sig, G, kSigReturn);
+    signal_ranks(sig, G, kSigReturn, done);
+}
+
+// Destination of every output row the down kernel returns: (rank << 48) | row.
+__global__ void ep_route_kernel(const RetSeg *__restrict__ segs, int n_segs, int64_t row0, int64_t n_rows,
+                                int64_t *__restrict__ route) {
+    extern __shared__ int64_t start_s[];
+    for (int i = threadIdx.x; i < n_segs; i += blockDim.x) start_s[i] = segs[i].src_row - row0;
+    __syncthreads();
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n_rows; j += (int64_t)gridDim.x * blockDim.x) {
+        int lo = 0, hi = n_segs;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (start_s[mid] <= j) lo = mid;
+            else hi = mid;
+        }
+        route[j] = (segs[lo].rank << 48) | (segs[lo].dst_row + (j - start_s[lo]));
+    }
 }
 
 // Bounded wait until this rank's arrival counter reaches `target`.
@@ -212,7 +238,8 @@ struct EpState {
     std::vector<void *> peer_x, peer_y, peer_sig;
     std::vector<size_t> cap_x, cap_y;
     int *err = nullptr;
-    DevBuf staging, xconv, dst_base, ret_segs;
+    unsigned int *done = nullptr;  // [0] push, [1] return, [2] fused down kernel: finished CTAs
+    DevBuf staging, xconv, dst_base, ret_segs, route, peer_tab;
 };
 
 static EpState *ep_of(gtmoe_handle *h) { return (EpState *)h->ep; }
@@ -245,9 +272,10 @@ void ep_destroy(gtmoe_handle *h) {
         if (q < (int)ep->peer_sig.size()) close_peer(ep->peer_sig[q]);
     }
     if (ep->comm && g_nccl.loaded) g_nccl.CommDestroy(ep->comm);
-    for (void *p : {ep->x_local, ep->y_local, ep->sig_local, (void *)ep->err})
+    for (void *p : {ep->x_local, ep->y_local, ep->sig_local, (void *)ep->err, (void *)ep->done})
         if (p) cudaFree(p);
-    DevBuf *bufs[] = {&ep->gathered, &ep->staging, &ep->xconv, &ep->dst_base, &ep->ret_segs};
+    DevBuf *bufs[] = {&ep->gathered, &ep->staging, &ep->xconv, &ep->dst_base, &ep->ret_segs, &ep->route,
+                      &ep->peer_tab};
     for (DevBuf *b : bufs) b->release();
     delete ep;
     h->ep = nullptr;
@@ -260,6 +288,8 @@ static int ep_map_signals(gtmoe_handle *h, EpState *ep) {
     GT_CUDA(cudaMemset(ep->sig_local, 0, 256));
     GT_CUDA(cudaMalloc(&ep->err, sizeof(int)));
     GT_CUDA(cudaMemset(ep->err, 0, sizeof(int)));
+    GT_CUDA(cudaMalloc(&ep->done, 4 * sizeof(unsigned int)));
+    GT_CUDA(cudaMemset(ep->done, 0, 4 * sizeof(unsigned int)));
     GT_CUDA(cudaDeviceSynchronize());
     cudaIpcMemHandle_t mine;
     GT_CUDA(cudaIpcGetMemHandle(&mine, ep->sig_local));
@@ -359,10 +389,27 @@ int ep_global_load(gtmoe_handle *h, int64_t *load) {
     return 0;
 }
 
+// The step's count exchange with this rank's counts replaced by a refusal
+// marker (token count -1): every rank then fails the step together.
+static int ep_refuse_step(gtmoe_handle *h, EpState *ep, int rc) {
+    const std::string msg = gtmoe_last_error();
+    const int E = h->cfg.n_routed, G = ep->G;
+    cudaStream_t st = h->stream;
+    GT_CHECK(h->load.ensure(sizeof(int64_t) * (E + 1)));
+    GT_CHECK(ep->gathered.ensure(sizeof(int64_t) * (size_t)G * (E + 1)));
+    std::vector<int64_t> mine(E + 1, 0);
+    mine[E] = -1;
+    GT_CUDA(cudaMemcpyAsync(h->load.p, mine.data(), sizeof(int64_t) * (E + 1), cudaMemcpyHostToDevice, st));
+    GT_NCCL(g_nccl.AllGather(h->load.p, ep->gathered.p, (size_t)(E + 1), ncclInt64, ep->comm, st));
+    GT_CUDA(cudaStreamSynchronize(st));
+    return fail(rc, "%s", msg.c_str());
+}
+
 int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
                void *out, int out_dtype, int32_t *chosen_out, double *gates_out, int32_t *perm_out,
-               int64_t *load_out) {
+               int64_t *load_out, int arg_rc) {
     EpState *ep = ep_of(h);
+    if (arg_rc != 0) return ep_refuse_step(h, ep, arg_rc);
     const gtmoe_config &c = h->cfg;
     const int E = c.n_routed, k = c.experts_per_token, S = c.n_shared, d = c.d_model, hd = c.hidden;
     const int G = h->n_ranks, r = h->rank, El = h->e_local;
@@ -373,7 +420,8 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
                                                             : GTMOE_DTYPE_F32;
     const size_t cs = dtype_size(compute);
     const size_t row_bytes = cs * d;
-    if (row_bytes % 16 != 0) return fail(GTMOE_EINVAL, "expert-parallel rows must be a multiple of 16 bytes");
+    if (row_bytes % 16 != 0)
+        return ep_refuse_step(h, ep, fail(GTMOE_EINVAL, "expert-parallel rows must be a multiple of 16 bytes"));
     const int vec = (int)(row_bytes / 16);
     const int64_t TK = T * k;
     const int n_chunks = (int)((T + kDispatchChunk - 1) / kDispatchChunk);
@@ -401,8 +449,9 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
         GT_CUDA(cudaMemcpy(hid.data(), token_ids, sizeof(int64_t) * T, cudaMemcpyDefault));
         for (int64_t t = 0; t < T; t++)
             if (hid[t] < 0)
-                return fail(GTMOE_EINVAL, "mixture of experts: token ID %lld at row %lld is negative",
-                            (long long)hid[t], (long long)t);
+                return ep_refuse_step(h, ep,
+                                      fail(GTMOE_EINVAL, "mixture of experts: token ID %lld at row %lld is negative",
+                                           (long long)hid[t], (long long)t));
         GT_CHECK(h->ids.ensure(sizeof(int64_t) * T));
         GT_CUDA(cudaMemcpyAsync(h->ids.p, hid.data(), sizeof(int64_t) * T, cudaMemcpyHostToDevice, st));
         ids_dev = h->ids.as<int64_t>();
@@ -498,6 +547,9 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     const int64_t *hg = ep->h_gathered.data();
     auto L = [&](int s, int e) { return hg[(size_t)s * (E + 1) + e]; };  // rows of rank s for expert e
     auto Tof = [&](int s) { return hg[(size_t)s * (E + 1) + E]; };
+    for (int s = 0; s < G; s++)
+        if (Tof(s) < 0)
+            return fail(GTMOE_EINVAL, "expert-parallel rank %d refused its Forward arguments; no rank ran this step", s);
     // eoff[e]: first row of expert e in its owner's received block (expert-major)
     std::vector<int64_t> eoff(E, 0), n_recv(G, 0);
     for (int q = 0; q < G; q++) {
@@ -576,10 +628,10 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
         xrows = ep->xconv.p;
     }
     ep->epoch++;
-    const unsigned long long arrivals = ep->epoch * (unsigned long long)G * kPushCtas;
+    const unsigned long long arrivals = ep->epoch * (unsigned long long)G;  // one per source rank and step
     ep_push_kernel<<<kPushCtas, kPushThreads, sizeof(int64_t) * (E + 1), st>>>(
         (const uint4 *)xrows, vec, da.perm, TK, da.offsets, E, El, ep->dst_base.as<int64_t>(), T, S > 0 ? 1 : 0, nr,
-        r, px, sg, G);
+        r, px, sg, G, ep->done + 0);
     GT_CUDA(cudaGetLastError());
     ep_wait_kernel<<<1, 32, 0, st>>>((unsigned long long *)ep->sig_local + kSigForward, arrivals, ep->err, 1);
     GT_CUDA(cudaGetLastError());
@@ -588,6 +640,22 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
 
     GT_CHECK(h->hp.ensure(cs * (size_t)hd * (rows_h > 0 ? rows_h : 1)));
     GT_CHECK(h->yp.ensure(row_bytes * (size_t)(rows_h > 0 ? rows_h : 1)));
+    // the tensor-core down kernel returns the routed rows itself
+    const bool fused_return = use_tc && rows_h > 0;
+    if (fused_return) {
+        GT_CHECK(ep->route.ensure(sizeof(int64_t) * (size_t)(nr > 0 ? nr : 1)));
+        GT_CHECK(ep->peer_tab.ensure(2 * sizeof(void *) * G));
+        std::vector<void *> tab(2 * G);
+        for (int q = 0; q < G; q++)
+            tab[q] = ep->peer_y[q], tab[G + q] = (unsigned long long *)ep->peer_sig[q] + kSigReturn;
+        GT_CUDA(cudaMemcpyAsync(ep->peer_tab.p, tab.data(), sizeof(void *) * 2 * G, cudaMemcpyHostToDevice, st));
+        if (nr > 0) {
+            ep_route_kernel<<<296, 256, sizeof(int64_t) * back.size(), st>>>(
+                ep->ret_segs.as<RetSeg>(), (int)back.size(), (int64_t)S * T, nr, ep->route.as<int64_t>());
+            GT_CUDA(cudaGetLastError());
+            note_launches(1);
+        }
+    }
     if (rows_h > 0) {
         if (use_tc) {
             TcArgs ta;
@@ -599,6 +667,12 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
             ta.xp = ep->x_local;
             ta.hp = h->hp.p;
             ta.yp = h->yp.p;
+            ta.ret_ranks = G;
+            ta.ret_row0 = (int64_t)S * T;
+            ta.ret_route = ep->route.as<int64_t>();
+            ta.ret_peers = ep->peer_tab.as<unsigned char *const>();
+            ta.ret_sigs = (unsigned long long *const *)(ep->peer_tab.as<void *>() + G);
+            ta.ret_done = ep->done + 2;
             GT_CHECK(launch_grouped_tc(h, h->tc, ta, st));
         } else {
             GroupedArgs ga;
@@ -625,13 +699,16 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     }
     // ---- outputs back to the tokens' ranks
     GT_CHECK(h->phase_begin(7));
-    ep_return_kernel<<<kPushCtas, kPushThreads, sizeof(int64_t) * (back.empty() ? 1 : back.size()), st>>>(
-        (const uint4 *)h->yp.p, vec, ep->ret_segs.as<RetSeg>(), (int)back.size(), (int64_t)S * T, back.empty() ? 0 : nr,
-        py, sg, G);
-    GT_CUDA(cudaGetLastError());
+    if (!fused_return) {
+        ep_return_kernel<<<kPushCtas, kPushThreads, sizeof(int64_t) * (back.empty() ? 1 : back.size()), st>>>(
+            (const uint4 *)h->yp.p, vec, ep->ret_segs.as<RetSeg>(), (int)back.size(), (int64_t)S * T,
+            back.empty() ? 0 : nr, py, sg, G, ep->done + 1);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+    }
     ep_wait_kernel<<<1, 32, 0, st>>>((unsigned long long *)ep->sig_local + kSigReturn, arrivals, ep->err, 2);
     GT_CUDA(cudaGetLastError());
-    note_launches(2);
+    note_launches(1);
     GT_CHECK(h->phase_end(7));
 
     CombineArgs ca;

@@ -108,7 +108,7 @@ int create_handle(const gtmoe_config *cfg, int device, int n_ranks, int rank, gt
 // expert parallelism (ep.cu)
 void ep_destroy(gtmoe_handle *h);
 int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
-               void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load);
+               void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load, int arg_rc);
 int ep_global_load(gtmoe_handle *h, int64_t *load);
 
 // kernel launches made by the library (all handles)

@@ -54,6 +54,10 @@ constexpr int kChunkRows = 128;      // weight rows per raw chunk = one CTA's ha
 constexpr int kNumDequantWarps = 8;
 constexpr int kDequantThreads = kNumDequantWarps * 32;
 constexpr int kNumThreads = (6 + kNumDequantWarps) * 32;  // 448
+// Expert parallel: two more warps in the down kernel copy finished output
+// rows to their tokens' ranks (coalesced 512-byte row segments).
+constexpr int kReturnWarps = 4;
+constexpr int kMaxThreads = kNumThreads + kReturnWarps * 32;
 constexpr int kTmemCols = 512;
 constexpr int kATileBytes = kCtaRows * kBK * 2;    // 16 KB per CTA
 constexpr int kBTileBytes = kChunkRows * kBK * 2;  // 16 KB per CTA
@@ -85,6 +89,13 @@ struct TcKernelArgs {
     float clamp_limit;
     __nv_bfloat16 *out;  // hp (GATED) or yp (DOWN)
     int *err;
+    // expert-parallel return of the down kernel (TcArgs)
+    int ret_ranks;
+    int64_t ret_row0;
+    const int64_t *ret_route;
+    unsigned char *const *ret_peers;
+    unsigned long long *const *ret_sigs;
+    unsigned int *ret_done;
 };
 
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
@@ -251,7 +262,7 @@ __device__ __forceinline__ void dequant_stage(const uint8_t *raw, uint8_t *btile
 // 0..127 / 128..255 of each TMEM lane are the gate / up values of one
 // (token, feature).  Rank 0 (the leader) issues the MMAs.
 template <int PREC, bool GATED>
-__global__ void __launch_bounds__(kNumThreads, 1)
+__global__ void __launch_bounds__(kMaxThreads, 1)
     grouped_tc_kernel(const __grid_constant__ CUtensorMap amap, const TcKernelArgs a) {
     using R = Raw<PREC>;
     constexpr int S = R::kStages;
@@ -269,6 +280,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     uint64_t *tmem_empty = bars + 4 * S + 2;  // [2] both epilogues done (leader)
     uint32_t *tmem_slot = (uint32_t *)(bars + 4 * S + 4);
     volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+    volatile int *tiles_out = (volatile int *)(tmem_slot + 2);  // epilogue warps' finished tiles (x4)
     int *prefix_s = (int *)(smem + S * (kATileBytes + kBTileBytes + R::kStageBytes) + 256);
 
     const int warp = threadIdx.x >> 5;
@@ -295,6 +307,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             mbar_init(&tmem_empty[b], 2 * 4);
         }
         *abort_flag = 0;
+        *tiles_out = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -463,11 +476,73 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(tmem_empty_leader0 + (uint32_t)(acc * sizeof(uint64_t)));
+            if (!GATED && a.ret_ranks > 0 && lane == 0) {
+                // the tile's rows are in global memory: hand them to the return warps
+                __threadfence_block();
+                atomicAdd((int *)tiles_out, 1);
+            }
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
             }
         }
+    } else if (warp >= 6 + kNumDequantWarps) {
+        // ---------------- expert parallel (down kernel): finished output rows
+        // of routed experts to their tokens' ranks, one tile behind the epilogue
+        const int rw = warp - (6 + kNumDequantWarps);
+        UnitDecoder dec{prefix_s, a.groups, a.n_groups, n_tiles};
+        int done = 0;
+        for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
+            Unit w;
+            dec.advance(u, w);
+            const Group &grp = dec.grp;
+            done += 4;
+            if (*tiles_out < done) {
+                const uint64_t t0 = global_timer_ns();
+                bool ok = true;
+                while (*tiles_out < done) {
+                    if (*abort_flag) {
+                        ok = false;
+                        break;
+                    }
+                    if (global_timer_ns() - t0 > kWaitLimitNs) {
+                        atomicCAS(a.err, 0, 8);
+                        *abort_flag = 1;
+                        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1) : "memory");
+                        ok = false;
+                        break;
+                    }
+                }
+                if (!ok) break;
+            }
+            __threadfence_block();
+            const int f0 = w.nt * kTileN;  // this tile's 256 output features: 512 bytes per row
+            const int64_t row_base = grp.h_row0 + w.mt * kTileM + (int64_t)rank * kCtaRows;
+            const int64_t left = grp.m - w.mt * kTileM - (int64_t)rank * kCtaRows;
+            const int n_valid = left < kCtaRows ? (int)left : kCtaRows;
+            const int r0 = rw * (kCtaRows / kReturnWarps);
+            const int r1 = min(n_valid, r0 + kCtaRows / kReturnWarps);
+            for (int r = r0; r < r1; r += 8) {
+                uint4 v[8];
+                uint4 *dst[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int64_t out_row = row_base + r + j;
+                    dst[j] = nullptr;
+                    if (r + j < r1 && out_row >= a.ret_row0) {
+                        const int64_t route = __ldg(a.ret_route + (out_row - a.ret_row0));
+                        dst[j] = reinterpret_cast<uint4 *>((__nv_bfloat16 *)a.ret_peers[route >> 48] +
+                                                           (route & 0xFFFFFFFFFFFFll) * (int64_t)a.n_out + f0) +
+                                 lane;
+                        v[j] = __ldcg(reinterpret_cast<const uint4 *>(a.out + out_row * (int64_t)a.n_out + f0) + lane);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    if (dst[j]) *dst[j] = v[j];
+            }
+        }
+        __threadfence_system();  // rows on other GPUs visible before the arrival below
     } else {
         // ---------------- dequantisation of this CTA's half of the weight tile
         const int tid = threadIdx.x - 6 * 32;
@@ -496,6 +571,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (warp == 1) {
         asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
     }
+    // expert parallel: the last CTA to finish tells every rank that this
+    // rank's output rows have landed (an aborted CTA never counts, so the
+    // other ranks' waits run out instead of reading partial rows)
+    if (!GATED && a.ret_ranks > 0 && threadIdx.x == 0 && !*abort_flag) {
+        const unsigned int done = atomicAdd(a.ret_done, 1u);
+        if (done == gridDim.x - 1) {
+            *a.ret_done = 0;
+            __threadfence_system();
+            for (int q = 0; q < a.ret_ranks; q++) atomicAdd_system(a.ret_sigs[q], 1ull);
+        }
+    }
 }
 
 // Re-lays one Int8/FP4 layer (rows x K, reference snapshot layout) into
@@ -519,6 +605,7 @@ __global__ void relayout_kernel(const uint8_t *__restrict__ codes, const float *
 
 template <int PREC, bool GATED>
 int launch_one(const CUtensorMap &map, const TcKernelArgs &ka, int sms, cudaStream_t st) {
+    const int threads = (!GATED && ka.ret_ranks > 0) ? kMaxThreads : kNumThreads;
     auto kern = grouped_tc_kernel<PREC, GATED>;
     static int grid = 0;
     if (!grid) {
@@ -526,7 +613,7 @@ int launch_one(const CUtensorMap &map, const TcKernelArgs &ka, int sms, cudaStre
         // one CTA pair per two SMs, as many pairs as can be resident at once
         cudaLaunchConfig_t q = {};
         q.gridDim = dim3(2 * ((sms + 1) / 2));
-        q.blockDim = dim3(kNumThreads);
+        q.blockDim = dim3(kMaxThreads);
         q.dynamicSmemBytes = Raw<PREC>::kSmemBytes;
         cudaLaunchAttribute qa;
         qa.id = cudaLaunchAttributeClusterDimension;
@@ -542,7 +629,7 @@ int launch_one(const CUtensorMap &map, const TcKernelArgs &ka, int sms, cudaStre
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kNumThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = Raw<PREC>::kSmemBytes;
     cfg.stream = st;
     cudaLaunchAttribute attr;
@@ -612,6 +699,12 @@ int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, cudaStrea
     ka.tile_prefix = ta.tile_prefix;
     ka.experts = h->table.as<ExpertLayers>();
     ka.n_groups = ta.n_groups;
+    ka.ret_ranks = 0;
+    ka.ret_row0 = 0;
+    ka.ret_route = nullptr;
+    ka.ret_peers = nullptr;
+    ka.ret_sigs = nullptr;
+    ka.ret_done = nullptr;
     ka.clamped = c.clamped;
     ka.clamp_limit = (float)c.clamp_limit;
     ka.err = w.err;
@@ -632,6 +725,12 @@ int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, cudaStrea
     ka.K = c.hidden;
     ka.n_out = c.d_model;
     ka.out = (__nv_bfloat16 *)ta.yp;
+    ka.ret_ranks = ta.ret_ranks;
+    ka.ret_row0 = ta.ret_row0;
+    ka.ret_route = ta.ret_route;
+    ka.ret_peers = ta.ret_peers;
+    ka.ret_sigs = ta.ret_sigs;
+    ka.ret_done = ta.ret_done;
     if (prec == GTMOE_INT8) GT_CHECK((launch_one<GTMOE_INT8, false>(hmap, ka, w.sms, st)));
     else GT_CHECK((launch_one<GTMOE_FP4, false>(hmap, ka, w.sms, st)));
     GT_CHECK(h->phase_end(4));

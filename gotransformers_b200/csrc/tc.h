@@ -26,6 +26,15 @@ struct TcArgs {
     void *xp;  // rows_x x d bf16
     void *hp;  // rows_h x h bf16
     void *yp;  // rows_h x d bf16
+    // Expert parallel: the down kernel writes output rows at or after
+    // ret_row0 straight to their token's rank instead of yp, and its last CTA
+    // then adds one arrival to every rank's counter (ret_ranks = 0: off).
+    int ret_ranks = 0;
+    int64_t ret_row0 = 0;
+    const int64_t *ret_route = nullptr;             // per row: (rank << 48) | row on that rank
+    unsigned char *const *ret_peers = nullptr;      // per rank: its returned-output buffer (device array)
+    unsigned long long *const *ret_sigs = nullptr;  // per rank: its return arrival counter (device array)
+    unsigned int *ret_done = nullptr;               // CTAs of this launch that finished (device, starts at 0)
 };
 
 bool tc_supported(const gtmoe_handle *h, int64_t T);

@@ -159,7 +159,22 @@ class MixtureOfExperts:
     # -- forward
     def forward(self, x, token_ids=None, residual=None, out=None, out_dtype=None, want_routing: bool = True):
         """Forward (mixtureofexperts.go:122-216).  Returns the T x d output in
-        `out_dtype` (default: x's dtype) on the same side (host/device) as x."""
+        `out_dtype` (default: x's dtype) on the same side (host/device) as x.
+
+        On an expert-parallel handle every rank must call this for every step;
+        a rank whose arguments are refused here still joins the step (as a
+        refusal, T = -1), so that every rank fails instead of waiting."""
+        try:
+            return self._forward(x, token_ids, residual, out, out_dtype, want_routing)
+        except ValueError:
+            if self.ep_ranks > 1 and not self._in_library:
+                _lib.lib().gtmoe_forward(self._h, None, 0, -1, None, None, None, 0, None, None, None, None)
+            raise
+
+    _in_library = False
+
+    def _forward(self, x, token_ids, residual, out, out_dtype, want_routing):
+        self._in_library = False
         T = x.shape[0]
         if x.ndim != 2 or x.shape[1] != self.cfg.d_model:
             raise ValueError(
@@ -194,6 +209,7 @@ class MixtureOfExperts:
             gates = np.empty((T, k), np.float64)
             perm = np.empty(T * k, np.int32)
             load = np.empty(self.cfg.n_routed, np.int64)
+        self._in_library = True
         check(_lib.lib().gtmoe_forward(self._h, _addr(x), xdt, T, _addr(ids), _addr(residual), _addr(out), odt_code,
                                        _addr(chosen), _addr(gates), _addr(perm), _addr(load)))
         if want_routing:

@@ -152,7 +152,12 @@ GTMOE_API int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, 
  *   load      int64[E]    lastExpertLoad
  * In expert-parallel handles T, x, out and the optional outputs are this
  * rank's tokens: perm lists their rows in expert order and load counts them
- * per expert (all n_routed experts).
+ * per expert (all n_routed experts).  Forward is then a collective step:
+ * every rank calls it once per step, in the same order.  A rank that cannot
+ * run a step calls it with T = -1 (any argument error does the same): the
+ * step then fails on every rank with GTMOE_EINVAL and the handles stay
+ * usable.  A device wait for the other ranks' rows that runs out (about 2 s)
+ * fails the step with GTMOE_ETIMEOUT and leaves the handle unusable.
  * With host output pointers the call returns after the results are there;
  * with device pointers it is asynchronous on the handle's stream. */
 GTMOE_API int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,

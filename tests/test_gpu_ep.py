@@ -1,8 +1,10 @@
-"""Expert parallelism on 2 GPUs through the C ABI: each process owns half of
-the routed experts and its slice of the tokens; concatenated outputs must
-equal one single-GPU handle's outputs on the same weights (same expert
-choices, output within 1e-6 rel-L2), and the balance update must use the
-load summed over ranks."""
+"""Expert parallelism on 2-8 GPUs through the C ABI: each process owns
+n_routed/G of the routed experts and an uneven slice of the tokens (one rank
+may have none); concatenated outputs must equal one single-GPU handle's
+outputs on the same weights (same expert choices, output within 1e-6
+rel-L2), and the balance update must use the load summed over ranks.  Each
+rank first runs a smaller prefix of its slice and then its whole slice twice,
+so the peer buffers grow once and are then reused."""
 import os
 import socket
 
@@ -19,8 +21,27 @@ CASES = {
                              x_bf16=True),
     "int8 f32 input": dict(T=600, d=256, h=128, n_shared=0, n_routed=8, k=2, precision=O.INT8, seed=32),
     "float32 simt": dict(T=300, d=64, h=96, n_shared=1, n_routed=6, k=2, precision=O.FLOAT32, seed=33),
+    # also: a step where one rank's arguments are wrong fails on every rank
+    "hash routing, refused step": dict(T=512, d=256, h=128, n_shared=1, n_routed=8, k=3, precision=O.INT8, seed=34,
+                                       hash_routing=True, x_bf16=True),
 }
-SPLIT = 0.62  # uneven token split between the ranks
+# uneven token split between the ranks, as fractions of T (rank 1 of 4 and 8 gets none)
+SPLITS = {2: [0.62], 4: [0.3, 0.3, 0.72], 8: [0.1, 0.1, 0.25, 0.4, 0.55, 0.7, 0.9]}
+
+
+def _world(n_routed):
+    import torch
+
+    n = torch.cuda.device_count()
+    for g in (8, 4, 2):
+        if g <= n and n_routed % g == 0:
+            return g
+    return 0
+
+
+def _slice(rank, world, T):
+    cuts = [0] + [int(T * f) for f in SPLITS[world]] + [T]
+    return slice(cuts[rank], cuts[rank + 1])
 
 
 def _free_port():
@@ -52,9 +73,10 @@ def _rank(rank, world, port, name, outdir):
     obj = [bytes(idbuf)]
     dist.broadcast_object_list(obj, src=0)
     m = G.MixtureOfExperts(spec.d, spec.h, spec.n_shared, spec.n_routed, spec.k,
-                           weight_precision=spec.experts[0][0].precision, device=rank, ep_ranks=world,
-                           ep_rank=rank, nccl_id=obj[0])
-    m.set_router(to_rows(spec.router), spec.router.bias)
+                           weight_precision=spec.experts[0][0].precision, hash_routing=spec.hash_routing,
+                           device=rank, ep_ranks=world, ep_rank=rank, nccl_id=obj[0])
+    if not spec.hash_routing:
+        m.set_router(to_rows(spec.router), spec.router.bias)
     El = spec.n_routed // world
     for e, layers in enumerate(spec.experts):
         if e < spec.n_shared:
@@ -66,12 +88,25 @@ def _rank(rank, world, port, name, outdir):
             kind = G.ROUTED
         for which, L in enumerate(layers):
             m.set_expert_layer(kind, idx, which, to_rows(L), L.bias)
-    cut = int(x.shape[0] * SPLIT)
-    sl = slice(0, cut) if rank == 0 else slice(cut, x.shape[0])
+    sl = _slice(rank, world, x.shape[0])
     xs = torch.from_numpy(np.ascontiguousarray(x[sl]))
     xs = xs.to(torch.bfloat16 if CASES[name].get("x_bf16") else torch.float32).cuda()
+    half = xs.shape[0] // 2
     torch.cuda.synchronize()
-    for _ in range(2):  # the second call reuses every buffer
+    if spec.hash_routing:
+        bad = ids[sl].copy()
+        if rank == world - 1:
+            bad[-1] = -5  # the reference panics on a negative token ID
+        try:
+            m.forward(xs, bad, out_dtype=_lib.DTYPE_F32)
+            refused = "ran"
+        except (_lib.GtmoeError, ValueError) as e:
+            refused = str(e)
+        with open(os.path.join(outdir, f"refused{rank}.txt"), "w") as f:
+            f.write(refused)
+    first = m.forward(xs[:half].contiguous(), ids[sl][:half], out_dtype=_lib.DTYPE_F32)
+    np.save(os.path.join(outdir, f"first{rank}.npy"), first.cpu().numpy())
+    for _ in range(2):  # larger than the first call: the buffers grow, then are reused
         out = m.forward(xs, ids[sl], out_dtype=_lib.DTYPE_F32)
     torch.cuda.synchronize()
     np.save(os.path.join(outdir, f"out{rank}.npy"), out.cpu().numpy())
@@ -91,10 +126,11 @@ def test_expert_parallel_matches_single_gpu(name, tmp_path):
     from gotransformers_b200 import _lib
     from gpu_helpers import gpu_moe, rel_l2
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    mp.start_processes(_rank, args=(2, _free_port(), name, str(tmp_path)), nprocs=2, start_method="spawn")
     spec, x, ids = make_case(**CASES[name])
+    world = _world(spec.n_routed)
+    if world < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_rank, args=(world, _free_port(), name, str(tmp_path)), nprocs=world, start_method="spawn")
     m = gpu_moe(spec)
     xt = torch.from_numpy(x).to(torch.bfloat16 if CASES[name].get("x_bf16") else torch.float32).cuda()
     torch.cuda.synchronize()
@@ -104,10 +140,22 @@ def test_expert_parallel_matches_single_gpu(name, tmp_path):
     m.update_balance(0.05)
     bal = m.balance_biases
     m.close()
-    got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(2)])
-    got_chosen = np.concatenate([np.load(tmp_path / f"chosen{r}.npy") for r in range(2)])
+    got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(world)])
+    got_chosen = np.concatenate([np.load(tmp_path / f"chosen{r}.npy") for r in range(world)])
     assert np.array_equal(got_chosen, chosen)
     assert rel_l2(got, ref) <= 1e-6
-    for r in range(2):
+    # the first, smaller call: each rank's prefix rows (rows are independent)
+    for r in range(world):
+        sl = _slice(r, world, x.shape[0])
+        first = np.load(tmp_path / f"first{r}.npy")
+        want = ref[sl][: first.shape[0]]
+        if first.shape[0]:
+            assert rel_l2(first, want) <= 1e-6, r
+    for r in range(world):
         assert np.array_equal(np.load(tmp_path / f"bal{r}.npy"), bal), r
+    if spec.hash_routing:
+        msgs = [(tmp_path / f"refused{r}.txt").read_text() for r in range(world)]
+        assert "negative" in msgs[world - 1], msgs
+        for r in range(world - 1):
+            assert f"rank {world - 1} refused" in msgs[r], msgs
     assert load.sum() == x.shape[0] * spec.k
