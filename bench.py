@@ -238,11 +238,13 @@ def main():
     barrier()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")  # lets ncu list exactly the timed launches (--nvtx-include timed/)
     ev0.record(stream)
     for _ in range(args.steps):
         moe.forward(x, out=out, want_routing=False)
     ev1.record(stream)
     ev1.synchronize()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     barrier()
     clocks = sampler.stop(physical_gpu_index(local_rank))
