@@ -236,19 +236,30 @@ def main():
     sampler = ClockSampler()
     torch.cuda.synchronize(dev)
     barrier()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
+    # decode-shaped batches touch less than a few L2s of weights: write a
+    # buffer larger than L2 between steps (outside each step's events)
+    flush = decode_shaped(cfg)
+    flush_buf = torch.empty((512 << 20) // 4, dtype=torch.int32, device=dev) if flush else None
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps if flush else 1)]
     torch.cuda.nvtx.range_push("timed")  # lets ncu list exactly the timed launches (--nvtx-include timed/)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        moe.forward(x, out=out, want_routing=False)
-    ev1.record(stream)
-    ev1.synchronize()
+    if flush:
+        for i in range(args.steps):
+            flush_buf.fill_(i)
+            evs[i][0].record(stream)
+            moe.forward(x, out=out, want_routing=False)
+            evs[i][1].record(stream)
+    else:
+        evs[0][0].record(stream)
+        for _ in range(args.steps):
+            moe.forward(x, out=out, want_routing=False)
+        evs[0][1].record(stream)
+    evs[-1][1].synchronize()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     barrier()
     clocks = sampler.stop(physical_gpu_index(local_rank))
-    ms = ev0.elapsed_time(ev1) / args.steps
+    ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
     import ctypes
 
     phase_ms = (ctypes.c_double * _lib.N_PHASES)()
@@ -263,16 +274,23 @@ def main():
     for _ in range(2):
         moe.forward(x_host, out=out_host, want_routing=False)
     barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
     e2e_steps = max(3, args.steps // 2)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        moe.forward(x_host, out=out_host, want_routing=False)
-    e1.record(stream)
-    e1.synchronize()
+    eevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(e2e_steps if flush else 1)]
+    if flush:
+        for i in range(e2e_steps):
+            flush_buf.fill_(i)
+            eevs[i][0].record(stream)
+            moe.forward(x_host, out=out_host, want_routing=False)
+            eevs[i][1].record(stream)
+    else:
+        eevs[0][0].record(stream)
+        for _ in range(e2e_steps):
+            moe.forward(x_host, out=out_host, want_routing=False)
+        eevs[0][1].record(stream)
+    eevs[-1][1].synchronize()
     barrier()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    e2e_ms = sum(a.elapsed_time(b) for a, b in eevs) / e2e_steps
 
     # expert rows this rank ran: its tokens through the shared experts plus the
     # rows routed to the experts it owns
@@ -295,20 +313,34 @@ def main():
         phases = {n: max(v[3 + i] for v in per_rank) for i, n in enumerate(_lib.PHASES)}
 
     peaks = measured_peaks()
-    # dominant kernel: the grouped gate/up GEMM (2/3 of the expert FLOPs), on
-    # the rank where it took longest, with that rank's own rows
+    # dominant kernel: the grouped gate/up GEMM (2/3 of the expert FLOPs and
+    # weight bytes), on the rank where it took longest, with its own rows
     ig, idn = 3 + _lib.PHASES.index("expert_gate_up"), 3 + _lib.PHASES.index("expert_down")
     kname, col = max((("expert_gate_up", ig), ("expert_down", idn)), key=lambda kv: phases[kv[0]])
     slow = max(per_rank, key=lambda v: v[col])
     kms, rows = slow[col], slow[2]
-    kflops = rows * (4.0 if kname == "expert_gate_up" else 2.0) * cfg.d * cfg.h
-    achieved = kflops / (kms * 1e-3) / 1e12 if kms > 0 else 0.0
     traffic = profiled_traffic(kname, cfg.name, T_local)
-    roofline = {"kernel": kname, "bound": "tensor", "achieved": round(achieved, 2),
-                "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": traffic,
-                "peak_source": f"{peaks['source']} bf16 sustained (kernel timed inside a long step loop)",
-                "algorithmic_flops_per_launch": kflops, "avg_ms": round(kms, 4)}
+    if decode_shaped(cfg):
+        # weight streaming: bytes of the touched experts' layers (codes + block
+        # scales) plus activation rows in and out, over the kernel's time
+        touched = int((moe.last_expert_load() > 0).sum()) + cfg.n_shared
+        bpv = {2: 1.0 + 4 / 16, 3: 0.5 + 4 / 16}[cfg.precision]
+        n_layers, k_in, n_out = (2, cfg.d, cfg.h) if kname == "expert_gate_up" else (1, cfg.h, cfg.d)
+        kbytes = touched * n_layers * cfg.h * cfg.d * bpv + rows * (k_in + n_out) * 2
+        achieved = kbytes / (kms * 1e-3) / 1e9 if kms > 0 else 0.0
+        roofline = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                    "peak_source": f"{peaks['source']} HBM copy bandwidth",
+                    "algorithmic_bytes_per_launch": int(kbytes), "touched_experts": touched,
+                    "avg_ms": round(kms, 4)}
+    else:
+        kflops = rows * (4.0 if kname == "expert_gate_up" else 2.0) * cfg.d * cfg.h
+        achieved = kflops / (kms * 1e-3) / 1e12 if kms > 0 else 0.0
+        roofline = {"kernel": kname, "bound": "tensor", "achieved": round(achieved, 2),
+                    "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                    "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": traffic,
+                    "peak_source": f"{peaks['source']} bf16 sustained (kernel timed inside a long step loop)",
+                    "algorithmic_flops_per_launch": kflops, "avg_ms": round(kms, 4)}
 
     cpu_baseline = None
     if want_cpu:
@@ -353,13 +385,21 @@ def main():
         dist.destroy_process_group()
 
 
+def decode_shaped(cfg) -> bool:
+    """A few tokens per expert: the forward streams expert weights (HBM-bound)."""
+    return cfg.T <= 64
+
+
 def l2_note(cfg) -> str:
     """Why no L2 flush is needed between steps: the step's inputs exceed L2."""
     l2 = 126 << 20
     xb = cfg.T * cfg.d * (2 if cfg.x_bf16 else 8)
     code = {0: 8.0, 1: 4.0, 2: 1.0 + 4 / 16, 3: 0.5 + 4 / 16}[cfg.precision]
     wb = (cfg.n_routed + cfg.n_shared) * 3 * cfg.d * cfg.h * code
-    verdict = "no flush" if xb + wb > l2 else "weights and activations fit in L2: not flushed (warm-L2 figure)"
+    if decode_shaped(cfg):
+        verdict = "512 MiB buffer written between steps (L2 flushed), each step timed by its own events"
+    else:
+        verdict = "no flush" if xb + wb > l2 else "weights and activations fit in L2: not flushed (warm-L2 figure)"
     return f"x {xb / 2**20:.0f} MiB, expert weights {wb / 1e9:.2f} GB, L2 126 MiB: {verdict}"
 
 

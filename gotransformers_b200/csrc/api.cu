@@ -258,6 +258,9 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     const int E = c.n_routed, k = c.experts_per_token, S = c.n_shared, d = c.d_model, hd = c.hidden;
     cudaStream_t st = h->stream;
     const bool use_tc = tc_supported(h, T);
+    // few rows per expert: stream the weights (decode.cu) instead of 256-row tiles
+    const bool use_decode =
+        use_tc && decode_usable(c.weight_precision, d, hd, T) && !getenv("GTMOE_DISABLE_DECODE");
     const int compute = c.weight_precision == GTMOE_FLOAT64 ? GTMOE_DTYPE_F64
                         : use_tc                            ? GTMOE_DTYPE_BF16
                                                             : GTMOE_DTYPE_F32;
@@ -327,7 +330,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     da.slot_row = h->slot_row.as<int64_t>();
     da.groups = h->groups.as<Group>();
     da.tile_prefix = h->tile_prefix.as<int64_t>();
-    da.bm = use_tc ? tc_tile_rows(h->tc) : kSimtBM;
+    da.bm = use_decode ? kDecodeTileRows : use_tc ? tc_tile_rows(h->tc) : kSimtBM;
     GT_CHECK(h->phase_begin(1));
     GT_CHECK(launch_dispatch(da, st));
     GT_CHECK(h->phase_end(1));
@@ -336,7 +339,29 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     GT_CHECK(launch_gather(x_dev, x_dtype, T, d, da.perm, TK, S > 0 ? T : 0, S > 0, h->xp.p, compute, st));
     GT_CHECK(h->phase_end(2));
 
-    if (use_tc) {
+    if (use_decode) {
+        DecodeArgs dc;
+        dc.groups = da.groups;
+        dc.tile_prefix = da.tile_prefix;
+        dc.n_groups = S + E;
+        dc.experts = h->table.as<ExpertLayers>();
+        dc.d = d;
+        dc.h = hd;
+        dc.precision = c.weight_precision;
+        dc.clamped = c.clamped;
+        dc.clamp_limit = c.clamp_limit;
+        dc.xp = h->xp.p;
+        dc.hp = h->hp.p;
+        dc.yp = h->yp.p;
+        dc.sms = h->tc.sms;
+        dc.err = h->tc.err;
+        GT_CHECK(h->phase_begin(3));
+        GT_CHECK(launch_decode(dc, 1, st));
+        GT_CHECK(h->phase_end(3));
+        GT_CHECK(h->phase_begin(4));
+        GT_CHECK(launch_decode(dc, 2, st));
+        GT_CHECK(h->phase_end(4));
+    } else if (use_tc) {
         TcArgs ta;
         ta.n_groups = S + E;
         ta.groups = da.groups;

@@ -1,0 +1,256 @@
+// decode.cu -- grouped SwiGLU expert products for few rows per expert
+// (decode-shaped batches, every group <= kDecodeMaxRows rows, run in tiles
+// of 16 rows).
+//
+// With a handful of tokens per expert the expert products are bound by the
+// bytes of the expert weights (feedforward/gatedfeedforward.go:49-57 over
+// lowprecision rows, rows.go:207-257), not by tensor throughput.  These
+// kernels stream each touched expert's Int8/FP4 weight rows once, in the
+// tile-chunk layout the tensor-core kernels use (128 rows x 64 inputs: codes
+// then block scales), dequantise them in registers straight into mma.sync
+// B fragments (no shared-memory round trip for the bf16 weights) and run them
+// against the few token rows (16 per m-tile).
+//
+// Work unit: (16-row tile of a group, block of 64 output features).  A CTA of eight
+// warps runs a unit: a 4-stage pipeline of bulk copies (TMA engine, mbarrier
+// completion) brings, per 64-input step,
+// the 64 weight rows of the block (gate and up rows for kernel 1) and the
+// group's token rows (bf16, padded rows: conflict-free fragment loads).  The
+// tokens are the MMA's M side (16 per m-tile) and the weights its N side:
+// warp w owns features 8w..8w+7, so each lane decodes one weight row per
+// 16-input block.  Inside a block the MMA's k-slots are mapped to the
+// physical inputs {4q..4q+3} of lane q, identically for weights and tokens,
+// so a lane decodes one 32-bit word of Int8 codes (or one 16-bit pair of FP4
+// codes) per row and block.
+#include "common.cuh"
+#include "dequant.cuh"
+#include "internal.h"
+
+namespace gtmoe {
+
+namespace {
+
+constexpr int kDecodeThreads = 256;  // 8 warps x 8 features
+constexpr int kDecodeFeatures = 64;  // output features per unit (half a 128-row chunk)
+constexpr int kDecodeStages = 4;
+constexpr int kXPitch = 160;  // bytes per token row in shared memory (128 + 32: conflict-free 8-byte loads)
+
+template <int PREC>
+struct DecodeLayout {
+    static constexpr int kCodeBytes = PREC == GTMOE_INT8 ? 64 : 32;  // per row and 64 inputs
+    static constexpr int kChunkRowBytes = kCodeBytes + 16;           // codes + 4 float scales
+    static constexpr int kCodes = kDecodeFeatures * kCodeBytes;      // one layer's 64 rows of codes
+    static constexpr int kScales = kDecodeFeatures * 16;
+    static constexpr int kLayer = kCodes + kScales;
+};
+
+template <int PREC, bool GATED>
+struct DecodeStage {
+    static constexpr int kLayers = GATED ? 2 : 1;
+    static constexpr int kWeights = kLayers * DecodeLayout<PREC>::kLayer;
+    static constexpr int kBytes = kWeights + kDecodeTileRows * kXPitch;
+};
+
+__device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// B fragment of one weight row (16 inputs of block s): two bf16x2, k-slots
+// (2q, 2q+1) and (2q+8, 2q+9) = physical inputs 4q..4q+3.
+template <int PREC>
+__device__ __forceinline__ void decode_row_block(const uint8_t *codes, float sc, int row, int s, int q, uint32_t *o) {
+    using DL = DecodeLayout<PREC>;
+    if (PREC == GTMOE_INT8) {
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(codes + row * DL::kCodeBytes + 16 * s + 4 * q);
+        int8_decode4(w, sc, o);
+    } else {
+        const uint32_t w = *reinterpret_cast<const uint16_t *>(codes + row * DL::kCodeBytes + 8 * s + 2 * q);
+        const Fp4Tables t = fp4_tables(sc);
+        uint32_t v[4];
+        fp4_decode8(w, t, v);
+        o[0] = v[0];
+        o[1] = v[1];
+    }
+}
+
+// Unit u -> (group, 16-row tile, feature block): the m-tile prefix counts
+// tiles of kDecodeTileRows rows per group.
+__device__ __forceinline__ int unit_group(const int64_t *prefix, int n_groups, int64_t tile) {
+    int lo = 0, hi = n_groups;  // last g with prefix[g] <= tile
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(prefix + mid) <= tile) lo = mid;
+        else hi = mid;
+    }
+    return lo;
+}
+
+template <int PREC, bool GATED>
+__global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs a) {
+    using DL = DecodeLayout<PREC>;
+    using ST = DecodeStage<PREC, GATED>;
+    extern __shared__ __align__(128) uint8_t dsmem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g8 = lane >> 2, q = lane & 3;
+    const int K = GATED ? a.d : a.h;
+    const int n_out = GATED ? a.h : a.d;
+    const int KB = K / 64;
+    const int blocks = n_out / kDecodeFeatures;
+    const int which = GATED ? 0 : 2;
+    const int64_t chunk_bytes = (int64_t)128 * DL::kChunkRowBytes;
+    const __nv_bfloat16 *xin = (const __nv_bfloat16 *)(GATED ? a.xp : a.hp);
+    __nv_bfloat16 *out = (__nv_bfloat16 *)(GATED ? a.hp : a.yp);
+    const int64_t units = __ldg(a.tile_prefix + a.n_groups) * blocks;
+
+    __shared__ uint64_t full[kDecodeStages];  // stage landed (expect_tx by the issuing lane)
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kDecodeStages; s++) mbar_init(&full[s], 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    uint32_t issued = 0, consumed = 0;  // stages over all units: slot = n % S, parity = (n / S) & 1
+
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+        const int64_t tile = u / blocks;
+        const int fb = (int)(u % blocks);
+        const int gi = unit_group(a.tile_prefix, a.n_groups, tile);
+        const Group grp = a.groups[gi];
+        const ExpertLayers &L = a.experts[grp.expert];
+        const int64_t r0 = (tile - __ldg(a.tile_prefix + gi)) * kDecodeTileRows;  // first row of this tile
+        const int m = grp.m - r0 < kDecodeTileRows ? (int)(grp.m - r0) : kDecodeTileRows;
+        const int nt = fb >> 1, half = fb & 1;
+        const uint8_t *wsrc[2];
+        wsrc[0] = L.tiled[which] + (int64_t)nt * KB * chunk_bytes;
+        wsrc[1] = GATED ? L.tiled[1] + (int64_t)nt * KB * chunk_bytes : nullptr;
+        const uint8_t *xrow0 = (const uint8_t *)(xin + ((GATED ? grp.x_row0 : grp.h_row0) + r0) * (int64_t)K);
+
+        // warp 0: one lane arms the stage's barrier and copies the weight
+        // blocks, then the lanes copy the token rows (128 bytes each)
+        auto issue = [&](int kb) {
+            const uint32_t slot = issued % kDecodeStages;
+            uint8_t *st = dsmem + slot * ST::kBytes;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[slot], ST::kWeights + m * 128);
+#pragma unroll
+                for (int l = 0; l < ST::kLayers; l++) {
+                    const uint8_t *chunk = wsrc[l] + kb * chunk_bytes;
+                    uint8_t *dst = st + l * DL::kLayer;
+                    bulk_copy(dst, chunk + half * kDecodeFeatures * DL::kCodeBytes, DL::kCodes, &full[slot]);
+                    bulk_copy(dst + DL::kCodes, chunk + 128 * DL::kCodeBytes + half * kDecodeFeatures * 16,
+                              DL::kScales, &full[slot]);
+                }
+            }
+            __syncwarp();
+            uint8_t *xs = st + ST::kWeights;
+            for (int r = lane; r < m; r += 32)
+                bulk_copy(xs + r * kXPitch, xrow0 + (int64_t)r * K * 2 + kb * 128, 128, &full[slot]);
+            issued++;
+        };
+
+        // acc[l]: this tile's 16 tokens x this warp's 8 features
+        float acc[2][4];
+#pragma unroll
+        for (int l = 0; l < 2; l++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) acc[l][c] = 0.f;
+
+        if (warp == 0)
+            for (int kb = 0; kb < kDecodeStages - 1 && kb < KB; kb++) issue(kb);
+        for (int kb = 0; kb < KB; kb++) {
+            // every warp is done with stage kb-1, whose slot stage kb+S-1 refills
+            __syncthreads();
+            if (warp == 0 && kb + kDecodeStages - 1 < KB) issue(kb + kDecodeStages - 1);
+            const uint32_t slot = consumed % kDecodeStages;
+            if (!abort_flag)
+                mbar_wait(&full[slot], (consumed / kDecodeStages) & 1, (volatile int *)&abort_flag, a.err, 9);
+            consumed++;
+
+            const uint8_t *st = dsmem + slot * ST::kBytes;
+            const uint8_t *xs = st + ST::kWeights;
+            const int row = warp * 8 + g8;  // this lane's weight row (feature) in the block
+            float4 sc[2];
+#pragma unroll
+            for (int l = 0; l < ST::kLayers; l++)
+                sc[l] = *reinterpret_cast<const float4 *>(st + l * DL::kLayer + DL::kCodes + row * 16);
+#pragma unroll
+            for (int s = 0; s < 4; s++) {
+                const uint8_t *xa = xs + g8 * kXPitch + 32 * s + 8 * q;
+                const uint2 lo = *reinterpret_cast<const uint2 *>(xa);
+                const uint2 hi = *reinterpret_cast<const uint2 *>(xa + 8 * kXPitch);
+                const uint32_t af[4] = {lo.x, hi.x, lo.y, hi.y};
+#pragma unroll
+                for (int l = 0; l < ST::kLayers; l++) {
+                    const float scl = s == 0 ? sc[l].x : s == 1 ? sc[l].y : s == 2 ? sc[l].z : sc[l].w;
+                    uint32_t bw[2];
+                    decode_row_block<PREC>(st + l * DL::kLayer, scl, row, s, q, bw);
+                    mma_bf16_16816(acc[l], af, bw[0], bw[1]);
+                }
+            }
+        }
+        __syncthreads();  // the next unit's first stages refill slots read above
+
+        // epilogue: acc[l] = tokens (r0 + g8, r0 + g8 + 8) x features (f, f + 1)
+        const int f = fb * kDecodeFeatures + warp * 8 + 2 * q;
+        const float *bias0 = L.b32[which];
+        const float *bias1 = GATED ? L.b32[1] : nullptr;
+        const float lim = (float)a.clamp_limit;
+        const float b00 = bias0 ? __ldg(bias0 + f) : 0.f, b01 = bias0 ? __ldg(bias0 + f + 1) : 0.f;
+        const float b10 = bias1 ? __ldg(bias1 + f) : 0.f, b11 = bias1 ? __ldg(bias1 + f + 1) : 0.f;
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+            const int t = g8 + 8 * hf;
+            if (t >= m) continue;
+            float v0 = acc[0][2 * hf] + b00, v1 = acc[0][2 * hf + 1] + b01;
+            if (GATED) {
+                const float u0 = acc[1][2 * hf] + b10, u1 = acc[1][2 * hf + 1] + b11;
+                v0 = gate_act<float>(v0, a.clamped, lim) * up_act<float>(u0, a.clamped, lim);
+                v1 = gate_act<float>(v1, a.clamped, lim) * up_act<float>(u1, a.clamped, lim);
+            }
+            *reinterpret_cast<uint32_t *>(out + (grp.h_row0 + r0 + t) * (int64_t)n_out + f) = pack_bf16(v0, v1);
+        }
+    }
+}
+
+template <int PREC, bool GATED>
+int launch_decode_one(const DecodeArgs &a, cudaStream_t st) {
+    auto kern = decode_kernel<PREC, GATED>;
+    const int smem = kDecodeStages * DecodeStage<PREC, GATED>::kBytes;
+    static bool attr = false;
+    if (!attr) {
+        GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr = true;
+    }
+    kern<<<4 * a.sms, kDecodeThreads, smem, st>>>(a);  // up to four resident CTAs per SM
+    GT_CUDA(cudaGetLastError());
+    note_launches(1);
+    return 0;
+}
+
+}  // namespace
+
+bool decode_usable(int precision, int d, int h, int64_t T) {
+    return (precision == GTMOE_INT8 || precision == GTMOE_FP4) && T <= kDecodeMaxRows && d % 128 == 0 &&
+           h % 128 == 0;
+}
+
+int launch_decode(const DecodeArgs &a, int which, cudaStream_t st) {
+    if (a.precision == GTMOE_INT8)
+        return which == 1 ? launch_decode_one<GTMOE_INT8, true>(a, st) : launch_decode_one<GTMOE_INT8, false>(a, st);
+    return which == 1 ? launch_decode_one<GTMOE_FP4, true>(a, st) : launch_decode_one<GTMOE_FP4, false>(a, st);
+}
+
+}  // namespace gtmoe

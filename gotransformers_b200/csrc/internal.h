@@ -87,6 +87,27 @@ struct GroupedArgs {
     void *yp;                  // rows x d   (compute dtype)
 };
 constexpr int kSimtBM = 64;
+
+// Weight-streaming expert products for decode-shaped batches (decode.cu):
+// every group has at most kDecodeMaxRows rows; weights in the tile-chunk
+// layout of the tensor-core path (ExpertLayers::tiled).
+constexpr int kDecodeMaxRows = 64;
+constexpr int kDecodeTileRows = 16;  // rows per decode work unit (dispatch tile height)
+struct DecodeArgs {
+    const Group *groups;
+    const int64_t *tile_prefix;  // one tile per non-empty group
+    int n_groups;
+    const ExpertLayers *experts;
+    int d, h, precision, clamped;
+    double clamp_limit;
+    const void *xp;  // bf16 rows x d
+    void *hp;        // bf16 rows x h
+    void *yp;        // bf16 rows x d
+    int sms;
+    int *err;  // device flag: nonzero when a bounded wait expired
+};
+bool decode_usable(int precision, int d, int h, int64_t T);
+int launch_decode(const DecodeArgs &a, int which, cudaStream_t st);  // which: 1 gate/up, 2 down
 // which: 1 = gate/up + SwiGLU into hp, 2 = down into yp
 int launch_grouped_simt(const GroupedArgs &a, int which, cudaStream_t st);
 

@@ -92,6 +92,45 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void *__restri
     }
 }
 
+// Few tokens (decode-shaped batches): one warp per (token, expert) instead of
+// 64 x 64 tiles, so that the whole GPU works on a handful of tokens.  The
+// arithmetic is router_logits_kernel's, operation for operation: float32
+// sums of each 16-input block by sequential fmaf from zero, then the blocks
+// added in float64 in input order -- both kernels give the same bits.
+constexpr int kRouterSmallT = 256;
+constexpr int kRouterSmallWarps = 8;
+
+template <int XDT>
+__global__ void __launch_bounds__(kRouterSmallWarps * 32)
+    router_logits_small_kernel(const void *__restrict__ x, const float *__restrict__ w, int64_t T, int E, int d,
+                               double *__restrict__ logits) {
+    extern __shared__ float blk[];  // [warp][d/16 rounded up] block sums
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = (d + kRouterK - 1) / kRouterK;
+    const int e = blockIdx.x * kRouterSmallWarps + warp;
+    const int64_t t = blockIdx.y;
+    if (e >= E) return;
+    float *mine = blk + warp * nb;
+    const float *we = w + (int64_t)e * d;
+    for (int b = lane; b < nb; b += 32) {
+        float p = 0.f;
+#pragma unroll
+        for (int c = 0; c < kRouterK; c++) {
+            const int kk = b * kRouterK + c;
+            const float xv = kk < d ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
+            const float wv = kk < d ? __ldg(we + kk) : 0.f;
+            p = fmaf(xv, wv, p);
+        }
+        mine[b] = p;
+    }
+    __syncwarp();
+    if (lane == 0) {
+        double acc = 0.0;
+        for (int b = 0; b < nb; b++) acc += (double)mine[b];
+        logits[t * E + e] = acc;
+    }
+}
+
 // activationfunction/moreactivationfunctions.go:8-16, mixtureofexperts.go:80-82
 __device__ __forceinline__ double affinity_d(double logit) {
     double sp;
@@ -359,6 +398,21 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
     }
     if (a.use_tc) {
         GT_CHECK(launch_router_logits_tc(a.x, a.T, a.d, a.E, a.e_pad, a.w3, a.logits, a.err, a.sms, st));
+    } else if (a.T <= kRouterSmallT) {
+        dim3 grid((unsigned)((a.E + kRouterSmallWarps - 1) / kRouterSmallWarps), (unsigned)a.T);
+        const size_t smem = sizeof(float) * kRouterSmallWarps * ((a.d + kRouterK - 1) / kRouterK);
+        if (smem > 48 * 1024) return fail(GTMOE_EINVAL, "router: d_model %d too large", a.d);
+        if (a.x_dtype == GTMOE_DTYPE_F64)
+            router_logits_small_kernel<GTMOE_DTYPE_F64><<<grid, kRouterSmallWarps * 32, smem, st>>>(a.x, a.w32, a.T,
+                                                                                                     a.E, a.d, a.logits);
+        else if (a.x_dtype == GTMOE_DTYPE_F32)
+            router_logits_small_kernel<GTMOE_DTYPE_F32><<<grid, kRouterSmallWarps * 32, smem, st>>>(a.x, a.w32, a.T,
+                                                                                                     a.E, a.d, a.logits);
+        else
+            router_logits_small_kernel<GTMOE_DTYPE_BF16><<<grid, kRouterSmallWarps * 32, smem, st>>>(
+                a.x, a.w32, a.T, a.E, a.d, a.logits);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
     } else {
         dim3 grid((unsigned)((a.T + kRouterTile - 1) / kRouterTile),
                   (unsigned)((a.E + kRouterTile - 1) / kRouterTile));

@@ -38,6 +38,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include "dequant.cuh"
 #include "handle.h"
 #include "sm100.cuh"
 
@@ -162,63 +163,6 @@ struct UnitDecoder {
         return changed;
     }
 };
-
-// prmt with the sign-replicating selector mode (msb of a selector nibble set)
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t d;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-    return d;
-}
-
-// FP4 (E2M1 magnitudes {0,.5,1,1.5,2,3,4,6}, sign in bit 3; lowprecision.go:48,
-// rows.go:205) -> bf16(code * scale).  The eight scaled magnitudes of one
-// 16-value block, rounded once to bf16, are split into a high-byte and a
-// low-byte table of 8 bytes each; prmt then looks up four codes at a time.
-struct Fp4Tables {
-    uint32_t hlo, hhi, llo, lhi;
-};
-__device__ __forceinline__ Fp4Tables fp4_tables(float s) {
-    const uint32_t p0 = pack_bf16(0.f, 0.5f * s);
-    const uint32_t p1 = pack_bf16(s, 1.5f * s);
-    const uint32_t p2 = pack_bf16(2.f * s, 3.f * s);
-    const uint32_t p3 = pack_bf16(4.f * s, 6.f * s);
-    Fp4Tables t;
-    t.hlo = prmt(p0, p1, 0x7531);
-    t.hhi = prmt(p2, p3, 0x7531);
-    t.llo = prmt(p0, p1, 0x6420);
-    t.lhi = prmt(p2, p3, 0x6420);
-    return t;
-}
-// Eight codes (low nibble = even element, rows.go:68-74) -> four bf16x2.
-__device__ __forceinline__ void fp4_decode8(uint32_t w, const Fp4Tables &t, uint32_t *o) {
-    const uint32_t mag = w & 0x77777777u;
-    const uint32_t magh = mag >> 16;
-    uint32_t h0 = prmt(t.hlo, t.hhi, mag);
-    uint32_t h1 = prmt(t.hlo, t.hhi, magh);
-    const uint32_t l0 = prmt(t.llo, t.lhi, mag);
-    const uint32_t l1 = prmt(t.llo, t.lhi, magh);
-    // sign of code i is bit 4i+3: replicate it into the msb of high byte i
-    const uint32_t w4 = w << 4;
-    h0 |= prmt(w, w4, 0x9D8C) & 0x80808080u;
-    h1 |= prmt(w, w4, 0xBFAE) & 0x80808080u;
-    o[0] = prmt(l0, h0, 0x5140);
-    o[1] = prmt(l0, h0, 0x7362);
-    o[2] = prmt(l1, h1, 0x5140);
-    o[3] = prmt(l1, h1, 0x7362);
-}
-
-// Four Int8 codes -> two bf16x2 of bf16(code * scale): q + 128 becomes the
-// low byte of the float 2^23 + q + 128, from which q is recovered exactly.
-__device__ __forceinline__ void int8_decode4(uint32_t w, float s, uint32_t *o) {
-    const uint32_t u = w ^ 0x80808080u;
-    const float magic = 8388736.f;  // 2^23 + 128
-    const float f0 = __uint_as_float(prmt(u, 0x4B000000u, 0x7650)) - magic;
-    const float f1 = __uint_as_float(prmt(u, 0x4B000000u, 0x7651)) - magic;
-    const float f2 = __uint_as_float(prmt(u, 0x4B000000u, 0x7652)) - magic;
-    const float f3 = __uint_as_float(prmt(u, 0x4B000000u, 0x7653)) - magic;
-    o[0] = pack_bf16(f0 * s, f1 * s);
-    o[1] = pack_bf16(f2 * s, f3 * s);
-}
 
 // Dequantises one stage of this CTA's 128 B rows: item (r, b) = 16 values of
 // row r, k-block quarter b.  The raw stage is one chunk: codes

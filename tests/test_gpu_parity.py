@@ -35,6 +35,11 @@ CASES = {
     "tc bias clamped": dict(T=300, d=256, h=128, n_shared=1, n_routed=5, k=2, precision=O.FP4, layer_bias=0.3,
                             clamped=True, clamp_limit=0.7),
     "tc one token": dict(T=1, d=256, h=256, n_shared=1, n_routed=16, k=4, precision=O.INT8),
+    # decode-shaped batches (T <= 64): weight-streaming kernels (decode.cu)
+    "decode int8 T8 bias": dict(T=8, d=256, h=384, n_shared=1, n_routed=16, k=4, precision=O.INT8, layer_bias=0.1),
+    "decode fp4 T64 clamped": dict(T=64, d=512, h=256, n_shared=1, n_routed=8, k=3, precision=O.FP4, x_bf16=True,
+                                   layer_bias=0.2, clamped=True, clamp_limit=0.6),
+    "decode int8 T37 two shared": dict(T=37, d=256, h=128, n_shared=2, n_routed=6, k=2, precision=O.INT8),
     "f32 biases": dict(T=40, d=64, h=48, n_shared=1, n_routed=5, k=2, precision=O.FLOAT32, layer_bias=0.2),
     "compressed router": dict(T=50, d=64, h=32, n_shared=0, n_routed=8, k=2, precision=O.INT8,
                               router_precision=O.INT8),
@@ -291,4 +296,25 @@ def test_config_sampled(name):
     sample = np.sort(rng.choice(x.shape[0], size=min(64, x.shape[0]), replace=False))
     ref = O.moe_forward(spec, x[sample], ids[sample], threads=os.cpu_count() or 8)["out"]
     assert rel_l2(out[sample], ref) <= TOL[spec.experts[0][0].precision]
+    m.close()
+
+
+@pytest.mark.parametrize("prec", [O.INT8, O.FP4])
+def test_decode_path_matches_tensor_core_path(prec):
+    """The same decode-shaped batch through the weight-streaming kernels and
+    through the 256-row tensor-core kernels: identical routing, outputs equal
+    up to float32 summation order."""
+    spec, x, ids = make_case(T=48, d=256, h=256, n_shared=1, n_routed=12, k=3, precision=prec, seed=23,
+                             x_bf16=True, layer_bias=0.1)
+    m = gpu_moe(spec)
+    out_dec = m.forward(x, ids)
+    chosen = m.last_chosen_experts.copy()
+    os.environ["GTMOE_DISABLE_DECODE"] = "1"
+    try:
+        out_tc = m.forward(x, ids)
+    finally:
+        del os.environ["GTMOE_DISABLE_DECODE"]
+    assert np.array_equal(m.last_chosen_experts, chosen)
+    assert rel_l2(out_dec, out_tc) <= 1e-3
+    check_against_oracle(spec, x, ids, out_dec, m)
     m.close()
