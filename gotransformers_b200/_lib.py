@@ -40,6 +40,7 @@ EXPORTS = [
     "gtmoe_create_ep",
     "gtmoe_destroy",
     "gtmoe_set_stream",
+    "gtmoe_set_graphs",
     "gtmoe_set_router",
     "gtmoe_set_balance",
     "gtmoe_get_balance",
@@ -103,6 +104,7 @@ def lib():
             L.gtmoe_destroy.argtypes = [vp]
             L.gtmoe_destroy.restype = None
             L.gtmoe_set_stream.argtypes = [vp, vp]
+            L.gtmoe_set_graphs.argtypes = [vp, i32]
             L.gtmoe_set_router.argtypes = [vp, i32, vp, vp, vp]
             L.gtmoe_set_balance.argtypes = [vp, vp]
             L.gtmoe_get_balance.argtypes = [vp, vp]

@@ -252,15 +252,11 @@ int refresh_table(gtmoe_handle *h) {
 }
 
 // Single-GPU forward on device-resident x (x_dev) producing device out.
-int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, const int64_t *ids_dev,
-                   const void *res_dev, void *out_dev, int out_dtype) {
+// Workspace of a T-row forward on one GPU (grow-only; no-op when it fits).
+static int forward_prepare(gtmoe_handle *h, int64_t T) {
     const gtmoe_config &c = h->cfg;
     const int E = c.n_routed, k = c.experts_per_token, S = c.n_shared, d = c.d_model, hd = c.hidden;
-    cudaStream_t st = h->stream;
     const bool use_tc = tc_supported(h, T);
-    // few rows per expert: stream the weights (decode.cu) instead of 256-row tiles
-    const bool use_decode =
-        use_tc && decode_usable(c.weight_precision, d, hd, T) && !getenv("GTMOE_DISABLE_DECODE");
     const int compute = c.weight_precision == GTMOE_FLOAT64 ? GTMOE_DTYPE_F64
                         : use_tc                            ? GTMOE_DTYPE_BF16
                                                             : GTMOE_DTYPE_F32;
@@ -269,7 +265,6 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     const int64_t rows_x = (S > 0 ? T : 0) + TK;
     const int64_t rows_h = (int64_t)S * T + TK;
     const int n_chunks = (int)((T + kDispatchChunk - 1) / kDispatchChunk);
-
     GT_CHECK(h->logits.ensure(sizeof(double) * (size_t)T * E));
     GT_CHECK(h->chosen.ensure(sizeof(int32_t) * (size_t)TK));
     GT_CHECK(h->gates64.ensure(sizeof(double) * (size_t)TK));
@@ -287,6 +282,95 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     GT_CHECK(h->fixups.ensure(sizeof(int)));
     GT_CHECK(h->flagged.ensure(sizeof(int) * (size_t)(T > 0 ? T : 1)));
     GT_CHECK(refresh_table(h));
+    return 0;
+}
+
+// Arguments and every device address a captured forward bakes in.
+static std::vector<uint64_t> graph_key(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const void *res,
+                                       void *out, int out_dtype) {
+    uint64_t wbits;
+    memcpy(&wbits, &h->wmax, sizeof(wbits));
+    const bool use_tc = tc_supported(h, T);
+    const bool use_decode = use_tc && decode_usable(h->cfg.weight_precision, h->cfg.d_model, h->cfg.hidden, T) &&
+                            !getenv("GTMOE_DISABLE_DECODE");
+    std::vector<uint64_t> k = {(uint64_t)(uintptr_t)x, (uint64_t)x_dtype, (uint64_t)T, (uint64_t)(uintptr_t)res,
+                               (uint64_t)(uintptr_t)out, (uint64_t)out_dtype, (uint64_t)(uintptr_t)h->stream, wbits,
+                               (uint64_t)h->e_pad, (uint64_t)use_tc, (uint64_t)use_decode,
+                               (uint64_t)(uintptr_t)h->tc.err};
+    const gtmoe::DevBuf *bufs[] = {&h->wr64,   &h->wr32,   &h->br,     &h->bal,    &h->wr3,   &h->table,
+                                   &h->logits, &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load,
+                                   &h->offsets, &h->perm,  &h->slot_row, &h->groups, &h->tile_prefix, &h->xp,
+                                   &h->hp,     &h->yp,     &h->fixups, &h->flagged};
+    for (const gtmoe::DevBuf *b : bufs) k.push_back((uint64_t)(uintptr_t)b->p);
+    return k;
+}
+
+// forward_device, or its CUDA-graph replay when this call repeats the last
+// one exactly (same arguments and workspace): a decode loop calls the mixture
+// once per token with the same buffers, and replaying the dozen small launches
+// as one graph takes the host's launch cost off the GPU's timeline.
+static int run_forward(gtmoe_handle *h, bool graphable, const void *x_dev, int x_dtype, int64_t T,
+                       const int64_t *ids_dev, const void *res_dev, void *out_dev, int out_dtype) {
+    if (!graphable || !h->graphs || h->timing || T == 0) {
+        h->drop_graph();
+        return forward_device(h, x_dev, x_dtype, T, ids_dev, res_dev, out_dev, out_dtype);
+    }
+    GT_CHECK(forward_prepare(h, T));  // every allocation happens outside a capture
+    std::vector<uint64_t> key = graph_key(h, x_dev, x_dtype, T, res_dev, out_dev, out_dtype);
+    if (key != h->gkey) {
+        h->drop_graph();
+        h->gkey = key;
+        return forward_device(h, x_dev, x_dtype, T, ids_dev, res_dev, out_dev, out_dtype);
+    }
+    if (!h->gexec) {
+        // second identical call: capture it, then replay from now on
+        const int64_t before = launches_so_far();
+        GT_CUDA(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+        int rc = forward_device(h, x_dev, x_dtype, T, ids_dev, res_dev, out_dev, out_dtype);
+        cudaGraph_t graph = nullptr;
+        cudaError_t e = cudaStreamEndCapture(h->stream, &graph);
+        if (rc != 0 || e != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            cudaGetLastError();
+            h->drop_graph();
+            if (rc != 0) return rc;
+            return fail(GTMOE_ECUDA, "stream capture of the forward failed: %s", cudaGetErrorString(e));
+        }
+        h->glaunches = launches_so_far() - before;
+        e = cudaGraphInstantiate(&h->gexec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) {
+            h->gexec = nullptr;
+            h->drop_graph();
+            return fail(GTMOE_ECUDA, "cudaGraphInstantiate failed: %s", cudaGetErrorString(e));
+        }
+    } else {
+        note_launches((int)h->glaunches);
+    }
+    GT_CUDA(cudaGraphLaunch(h->gexec, h->stream));
+    h->last_T = T;
+    h->have_load = 1;
+    return 0;
+}
+
+int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, const int64_t *ids_dev,
+                   const void *res_dev, void *out_dev, int out_dtype) {
+    const gtmoe_config &c = h->cfg;
+    const int E = c.n_routed, k = c.experts_per_token, S = c.n_shared, d = c.d_model, hd = c.hidden;
+    cudaStream_t st = h->stream;
+    const bool use_tc = tc_supported(h, T);
+    // few rows per expert: stream the weights (decode.cu) instead of 256-row tiles
+    const bool use_decode =
+        use_tc && decode_usable(c.weight_precision, d, hd, T) && !getenv("GTMOE_DISABLE_DECODE");
+    const int compute = c.weight_precision == GTMOE_FLOAT64 ? GTMOE_DTYPE_F64
+                        : use_tc                            ? GTMOE_DTYPE_BF16
+                                                            : GTMOE_DTYPE_F32;
+    const size_t cs = dtype_size(compute);
+    const int64_t TK = T * k;
+    const int64_t rows_x = (S > 0 ? T : 0) + TK;
+    const int64_t rows_h = (int64_t)S * T + TK;
+
+    GT_CHECK(forward_prepare(h, T));
 
     RouterArgs ra;
     ra.hash = c.hash_routing;
@@ -438,6 +522,7 @@ void gtmoe_destroy(gtmoe_t h) {
         std::lock_guard<std::mutex> lock(h->mu);
         cudaSetDevice(h->device);
         if (h->stream) cudaStreamSynchronize(h->stream);
+        h->drop_graph();
         ep_destroy(h);
         tc_release(h->tc);
         for (auto &L : h->layers) {
@@ -466,6 +551,15 @@ int gtmoe_set_stream(gtmoe_t h, void *stream) {
     if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
     std::lock_guard<std::mutex> lock(h->mu);
     h->stream = stream ? (cudaStream_t)stream : h->own_stream;
+    return 0;
+}
+
+int gtmoe_set_graphs(gtmoe_t h, int on) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    GT_CUDA(cudaSetDevice(h->device));
+    h->graphs = on ? 1 : 0;
+    if (!on) h->drop_graph();
     return 0;
 }
 
@@ -663,7 +757,9 @@ int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_
         GT_CHECK(h->out_dev.ensure(obytes));
         out_dev = h->out_dev.p;
     }
-    GT_CHECK(forward_device(h, x_dev, x_dtype, T, ids_dev, res_dev, out_dev, out_dtype));
+    // device pointers only, no host round trip inside: the forward may be replayed as a CUDA graph
+    const bool graphable = !c.hash_routing && x_dev == x && out_dev == out && res_dev == residual;
+    GT_CHECK(run_forward(h, graphable, x_dev, x_dtype, T, ids_dev, res_dev, out_dev, out_dtype));
 
     bool sync = out_host;
     const int64_t TK = T * k;

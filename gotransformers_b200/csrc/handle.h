@@ -93,6 +93,22 @@ struct gtmoe_handle {
     std::vector<PhaseEvents> tev;
     size_t tev_used = 0;
     int64_t launches_at_read = 0;
+
+    // CUDA-graph replay of the device forward (gtmoe_set_graphs): a call
+    // whose arguments and workspace equal the previous call's replays the
+    // graph captured on the second such call
+    int graphs = 1;
+    std::vector<uint64_t> gkey;  // arguments and workspace of the last call
+    int gkey_hits = 0;
+    cudaGraphExec_t gexec = nullptr;
+    int64_t glaunches = 0;  // kernel launches inside the graph
+    void drop_graph() {
+        if (gexec) cudaGraphExecDestroy(gexec);
+        gexec = nullptr;
+        gkey.clear();
+        gkey_hits = 0;
+    }
+
     int phase_begin(int p);
     int phase_end(int p);
 };

@@ -131,6 +131,10 @@ class MixtureOfExperts:
     def set_stream(self, stream_ptr: int | None):
         check(_lib.lib().gtmoe_set_stream(self._h, stream_ptr))
 
+    def set_graphs(self, on: bool):
+        """CUDA-graph replay of repeated device-pointer forwards (default on)."""
+        check(_lib.lib().gtmoe_set_graphs(self._h, int(on)))
+
     # -- weights
     def set_router(self, rows: Rows | np.ndarray, bias=None):
         """RouterLayer weights (E x d) and biases (E)."""

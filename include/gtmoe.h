@@ -112,6 +112,15 @@ GTMOE_API void gtmoe_destroy(gtmoe_t h);
  * own stream). */
 GTMOE_API int gtmoe_set_stream(gtmoe_t h, void *stream);
 
+/* CUDA-graph replay (default on).  A Forward with device pointers for x, out
+ * and residual (no hash routing) that repeats the previous call exactly --
+ * same T, pointers and dtypes, and no weight buffer reallocated since -- is
+ * captured on its second occurrence and replayed as one CUDA graph from then
+ * on, the way a generation loop calls the mixture once per token
+ * (transformer/block.go:111-128).  No counterpart in the reference.  Timing
+ * (gtmoe_set_timing) runs the forward without graphs. */
+GTMOE_API int gtmoe_set_graphs(gtmoe_t h, int on);
+
 /* RouterLayer weights and biases (perceptron.Layer d -> E, Linear;
  * mixtureofexperts.go:60; Layer.SetWeights/SetBiases layer.go:234-254).
  * precision GTMOE_FLOAT64 takes values = double[E*d] and scales = NULL;
