@@ -11,11 +11,15 @@
 // B fragments (no shared-memory round trip for the bf16 weights) and run them
 // against the few token rows (16 per m-tile).
 //
-// Work unit: (16-row tile of a group, block of 64 output features).  A CTA of eight
-// warps runs a unit: a 4-stage pipeline of bulk copies (TMA engine, mbarrier
-// completion) brings, per 64-input step,
-// the 64 weight rows of the block (gate and up rows for kernel 1) and the
-// group's token rows (bf16, padded rows: conflict-free fragment loads).  The
+// Work unit: (16-row tile of a group, block of 64 output features = one
+// 64-row half of a weight chunk).  A CTA of eight compute warps and one
+// producer warp runs a unit.  The producer copies the tile's token rows once
+// per unit (one bulk copy per row, all inputs; padded rows: conflict-free
+// fragment loads) and keeps a 4-stage ring of weight steps, one contiguous
+// bulk copy per layer per 64-input step (gate and up for kernel 1): the TMA
+// engine's rate per CTA grows with the size of each copy, so few large copies
+// replace many small ones.  "full" mbarriers carry the transaction counts,
+// "empty" ones are released by each compute warp; no CTA-wide barrier.  The
 // tokens are the MMA's M side (16 per m-tile) and the weights its N side:
 // warp w owns features 8w..8w+7, so each lane decodes one weight row per
 // 16-input block.  Inside a block the MMA's k-slots are mapped to the
@@ -30,26 +34,28 @@ namespace gtmoe {
 
 namespace {
 
-constexpr int kDecodeThreads = 256;  // 8 warps x 8 features
-constexpr int kDecodeFeatures = 64;  // output features per unit (half a 128-row chunk)
+constexpr int kComputeWarps = 8;                          // 8 features each
+constexpr int kDecodeThreads = (kComputeWarps + 1) * 32;  // + one producer warp
+constexpr int kDecodeFeatures = kChunkHalfRows;           // output features per unit
 constexpr int kDecodeStages = 4;
-constexpr int kXPitch = 160;  // bytes per token row in shared memory (128 + 32: conflict-free 8-byte loads)
 
 template <int PREC>
 struct DecodeLayout {
     static constexpr int kCodeBytes = PREC == GTMOE_INT8 ? 64 : 32;  // per row and 64 inputs
     static constexpr int kChunkRowBytes = kCodeBytes + 16;           // codes + 4 float scales
-    static constexpr int kCodes = kDecodeFeatures * kCodeBytes;      // one layer's 64 rows of codes
-    static constexpr int kScales = kDecodeFeatures * 16;
-    static constexpr int kLayer = kCodes + kScales;
+    static constexpr int kCodes = kDecodeFeatures * kCodeBytes;      // one half's codes
+    static constexpr int kHalf = kDecodeFeatures * kChunkRowBytes;   // codes + scales: one bulk copy
 };
 
 template <int PREC, bool GATED>
 struct DecodeStage {
     static constexpr int kLayers = GATED ? 2 : 1;
-    static constexpr int kWeights = kLayers * DecodeLayout<PREC>::kLayer;
-    static constexpr int kBytes = kWeights + kDecodeTileRows * kXPitch;
+    static constexpr int kBytes = kLayers * DecodeLayout<PREC>::kHalf;
 };
+
+// Token-row pitch in shared memory for K inputs: 32 bytes of padding make
+// the 8-byte fragment loads of one warp conflict-free.
+__host__ __device__ __forceinline__ int decode_x_pitch(int K) { return 2 * K + 32; }
 
 __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(
@@ -59,8 +65,10 @@ __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
+// Not volatile: a pure function of its operands, so the compiler may overlap
+// the next block's loads and decoding with it.
 __device__ __forceinline__ void mma_bf16_16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -109,22 +117,34 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     const int KB = K / 64;
     const int blocks = n_out / kDecodeFeatures;
     const int which = GATED ? 0 : 2;
+    const int xpitch = decode_x_pitch(K);
     const int64_t chunk_bytes = (int64_t)128 * DL::kChunkRowBytes;
     const __nv_bfloat16 *xin = (const __nv_bfloat16 *)(GATED ? a.xp : a.hp);
     __nv_bfloat16 *out = (__nv_bfloat16 *)(GATED ? a.hp : a.yp);
     const int64_t units = __ldg(a.tile_prefix + a.n_groups) * blocks;
+    uint8_t *xs = dsmem;                                      // kDecodeTileRows x xpitch
+    uint8_t *ring = dsmem + kDecodeTileRows * xpitch;         // kDecodeStages x ST::kBytes
 
-    __shared__ uint64_t full[kDecodeStages];  // stage landed (expect_tx by the issuing lane)
+    __shared__ uint64_t full[kDecodeStages];   // weight step landed (expect_tx by the producer)
+    __shared__ uint64_t empty[kDecodeStages];  // every compute warp is done with the step
+    __shared__ uint64_t xfull, xempty;         // token rows of the unit landed / released
     __shared__ int abort_flag;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kDecodeStages; s++) mbar_init(&full[s], 1);
+        for (int s = 0; s < kDecodeStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kComputeWarps);
+        }
+        mbar_init(&xfull, 1);
+        mbar_init(&xempty, kComputeWarps);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    uint32_t issued = 0, consumed = 0;  // stages over all units: slot = n % S, parity = (n / S) & 1
+    volatile int *abort_p = (volatile int *)&abort_flag;
+    uint32_t n = 0;      // weight steps of this CTA so far: slot = n % S, parity = (n / S) & 1
+    uint32_t nu = 0;     // units of this CTA so far (token-row buffer parity)
 
-    for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    for (int64_t u = blockIdx.x; u < units && !*abort_p; u += gridDim.x, nu++) {
         const int64_t tile = u / blocks;
         const int fb = (int)(u % blocks);
         const int gi = unit_group(a.tile_prefix, a.n_groups, tile);
@@ -132,76 +152,70 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
         const ExpertLayers &L = a.experts[grp.expert];
         const int64_t r0 = (tile - __ldg(a.tile_prefix + gi)) * kDecodeTileRows;  // first row of this tile
         const int m = grp.m - r0 < kDecodeTileRows ? (int)(grp.m - r0) : kDecodeTileRows;
-        const int nt = fb >> 1, half = fb & 1;
-        const uint8_t *wsrc[2];
-        wsrc[0] = L.tiled[which] + (int64_t)nt * KB * chunk_bytes;
-        wsrc[1] = GATED ? L.tiled[1] + (int64_t)nt * KB * chunk_bytes : nullptr;
-        const uint8_t *xrow0 = (const uint8_t *)(xin + ((GATED ? grp.x_row0 : grp.h_row0) + r0) * (int64_t)K);
 
-        // warp 0: one lane arms the stage's barrier and copies the weight
-        // blocks, then the lanes copy the token rows (128 bytes each)
-        auto issue = [&](int kb) {
-            const uint32_t slot = issued % kDecodeStages;
-            uint8_t *st = dsmem + slot * ST::kBytes;
-            if (lane == 0) {
-                mbar_arrive_expect_tx(&full[slot], ST::kWeights + m * 128);
-#pragma unroll
-                for (int l = 0; l < ST::kLayers; l++) {
-                    const uint8_t *chunk = wsrc[l] + kb * chunk_bytes;
-                    uint8_t *dst = st + l * DL::kLayer;
-                    bulk_copy(dst, chunk + half * kDecodeFeatures * DL::kCodeBytes, DL::kCodes, &full[slot]);
-                    bulk_copy(dst + DL::kCodes, chunk + 128 * DL::kCodeBytes + half * kDecodeFeatures * 16,
-                              DL::kScales, &full[slot]);
-                }
-            }
+        if (warp == kComputeWarps) {
+            // ---- producer
+            const int nt = fb >> 1, half = fb & 1;
+            const uint8_t *w0 = L.tiled[which] + (int64_t)nt * KB * chunk_bytes + half * DL::kHalf;
+            const uint8_t *w1 = GATED ? L.tiled[1] + (int64_t)nt * KB * chunk_bytes + half * DL::kHalf : nullptr;
+            const uint8_t *xrow0 = (const uint8_t *)(xin + ((GATED ? grp.x_row0 : grp.h_row0) + r0) * (int64_t)K);
+            if (nu > 0 && !*abort_p) mbar_wait(&xempty, (nu - 1) & 1, abort_p, a.err, 13);
+            if (lane == 0) mbar_arrive_expect_tx(&xfull, (uint32_t)m * K * 2);
             __syncwarp();
-            uint8_t *xs = st + ST::kWeights;
-            for (int r = lane; r < m; r += 32)
-                bulk_copy(xs + r * kXPitch, xrow0 + (int64_t)r * K * 2 + kb * 128, 128, &full[slot]);
-            issued++;
-        };
+            for (int r = lane; r < m; r += 32) bulk_copy(xs + r * xpitch, xrow0 + (int64_t)r * K * 2, K * 2, &xfull);
+            for (int kb = 0; kb < KB; kb++, n++) {
+                const uint32_t slot = n % kDecodeStages;
+                if (n >= kDecodeStages && !*abort_p)
+                    mbar_wait(&empty[slot], ((n / kDecodeStages) - 1) & 1, abort_p, a.err, 10);
+                if (*abort_p) break;
+                if (lane == 0) {
+                    uint8_t *st = ring + slot * ST::kBytes;
+                    mbar_arrive_expect_tx(&full[slot], ST::kBytes);
+                    bulk_copy(st, w0 + kb * chunk_bytes, DL::kHalf, &full[slot]);
+                    if (GATED) bulk_copy(st + DL::kHalf, w1 + kb * chunk_bytes, DL::kHalf, &full[slot]);
+                }
+                __syncwarp();
+            }
+            continue;
+        }
 
-        // acc[l]: this tile's 16 tokens x this warp's 8 features
+        // ---- compute warps: acc[l] = this tile's 16 tokens x the warp's 8 features
         float acc[2][4];
 #pragma unroll
         for (int l = 0; l < 2; l++)
 #pragma unroll
             for (int c = 0; c < 4; c++) acc[l][c] = 0.f;
-
-        if (warp == 0)
-            for (int kb = 0; kb < kDecodeStages - 1 && kb < KB; kb++) issue(kb);
-        for (int kb = 0; kb < KB; kb++) {
-            // every warp is done with stage kb-1, whose slot stage kb+S-1 refills
-            __syncthreads();
-            if (warp == 0 && kb + kDecodeStages - 1 < KB) issue(kb + kDecodeStages - 1);
-            const uint32_t slot = consumed % kDecodeStages;
-            if (!abort_flag)
-                mbar_wait(&full[slot], (consumed / kDecodeStages) & 1, (volatile int *)&abort_flag, a.err, 9);
-            consumed++;
-
-            const uint8_t *st = dsmem + slot * ST::kBytes;
-            const uint8_t *xs = st + ST::kWeights;
-            const int row = warp * 8 + g8;  // this lane's weight row (feature) in the block
+        const int row = warp * 8 + g8;  // this lane's weight row (feature) in the half
+        if (!*abort_p) mbar_wait(&xfull, nu & 1, abort_p, a.err, 14);
+        const uint8_t *xrow = xs + g8 * xpitch + 8 * q;
+        for (int kb = 0; kb < KB; kb++, n++) {
+            const uint32_t slot = n % kDecodeStages;
+            if (!*abort_p) mbar_wait(&full[slot], (n / kDecodeStages) & 1, abort_p, a.err, 9);
+            if (*abort_p) break;
+            const uint8_t *st = ring + slot * ST::kBytes;
             float4 sc[2];
 #pragma unroll
             for (int l = 0; l < ST::kLayers; l++)
-                sc[l] = *reinterpret_cast<const float4 *>(st + l * DL::kLayer + DL::kCodes + row * 16);
+                sc[l] = *reinterpret_cast<const float4 *>(st + l * DL::kHalf + DL::kCodes + row * 16);
 #pragma unroll
             for (int s = 0; s < 4; s++) {
-                const uint8_t *xa = xs + g8 * kXPitch + 32 * s + 8 * q;
+                const uint8_t *xa = xrow + kb * 128 + 32 * s;
                 const uint2 lo = *reinterpret_cast<const uint2 *>(xa);
-                const uint2 hi = *reinterpret_cast<const uint2 *>(xa + 8 * kXPitch);
+                const uint2 hi = *reinterpret_cast<const uint2 *>(xa + 8 * xpitch);
                 const uint32_t af[4] = {lo.x, hi.x, lo.y, hi.y};
 #pragma unroll
                 for (int l = 0; l < ST::kLayers; l++) {
                     const float scl = s == 0 ? sc[l].x : s == 1 ? sc[l].y : s == 2 ? sc[l].z : sc[l].w;
                     uint32_t bw[2];
-                    decode_row_block<PREC>(st + l * DL::kLayer, scl, row, s, q, bw);
+                    decode_row_block<PREC>(st + l * DL::kHalf, scl, row, s, q, bw);
                     mma_bf16_16816(acc[l], af, bw[0], bw[1]);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
         }
-        __syncthreads();  // the next unit's first stages refill slots read above
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xempty);
 
         // epilogue: acc[l] = tokens (r0 + g8, r0 + g8 + 8) x features (f, f + 1)
         const int f = fb * kDecodeFeatures + warp * 8 + 2 * q;
@@ -223,18 +237,27 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             *reinterpret_cast<uint32_t *>(out + (grp.h_row0 + r0 + t) * (int64_t)n_out + f) = pack_bf16(v0, v1);
         }
     }
+    // every copy the producer issued was waited for by the compute warps
+    // (or a wait gave up), so no copy lands after the CTA has exited
+}
+
+template <int PREC, bool GATED>
+int decode_smem_bytes(const DecodeArgs &a) {
+    return kDecodeTileRows * decode_x_pitch(GATED ? a.d : a.h) + kDecodeStages * DecodeStage<PREC, GATED>::kBytes;
 }
 
 template <int PREC, bool GATED>
 int launch_decode_one(const DecodeArgs &a, cudaStream_t st) {
     auto kern = decode_kernel<PREC, GATED>;
-    const int smem = kDecodeStages * DecodeStage<PREC, GATED>::kBytes;
-    static bool attr = false;
-    if (!attr) {
+    const int smem = decode_smem_bytes<PREC, GATED>(a);
+    static int attr = 0;
+    if (smem > attr) {
         GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr = true;
+        attr = smem;
     }
-    kern<<<4 * a.sms, kDecodeThreads, smem, st>>>(a);  // up to four resident CTAs per SM
+    int per_sm = (220 * 1024) / smem;  // resident CTAs per SM the shared memory allows
+    per_sm = per_sm < 1 ? 1 : per_sm > 4 ? 4 : per_sm;
+    kern<<<per_sm * a.sms, kDecodeThreads, smem, st>>>(a);
     GT_CUDA(cudaGetLastError());
     note_launches(1);
     return 0;
@@ -243,8 +266,11 @@ int launch_decode_one(const DecodeArgs &a, cudaStream_t st) {
 }  // namespace
 
 bool decode_usable(int precision, int d, int h, int64_t T) {
+    // the token tile of a unit (16 rows x all inputs) and the weight ring fit in shared memory
+    const int kmax = d > h ? d : h;
+    const int smem = kDecodeTileRows * decode_x_pitch(kmax) + kDecodeStages * DecodeStage<GTMOE_INT8, true>::kBytes;
     return (precision == GTMOE_INT8 || precision == GTMOE_FP4) && T <= kDecodeMaxRows && d % 128 == 0 &&
-           h % 128 == 0;
+           h % 128 == 0 && smem <= 200 * 1024;
 }
 
 int launch_decode(const DecodeArgs &a, int which, cudaStream_t st) {

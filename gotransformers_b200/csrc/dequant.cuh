@@ -8,6 +8,19 @@
 
 namespace gtmoe {
 
+// Tile-chunk layout of Int8/FP4 weights (tc.cu, decode.cu): per 128-row block
+// and 64-input step one chunk of two 64-row halves, each codes
+// [64][code_bytes] then block scales [64][4 floats], so that a half is one
+// contiguous bulk copy.
+constexpr int kChunkHalfRows = 64;
+__host__ __device__ __forceinline__ int chunk_code_off(int r, int code_bytes) {
+    return (r / kChunkHalfRows) * kChunkHalfRows * (code_bytes + 16) + (r % kChunkHalfRows) * code_bytes;
+}
+__host__ __device__ __forceinline__ int chunk_scale_off(int r, int code_bytes) {
+    return (r / kChunkHalfRows) * kChunkHalfRows * (code_bytes + 16) + kChunkHalfRows * code_bytes +
+           (r % kChunkHalfRows) * 16;
+}
+
 // prmt with the sign-replicating selector mode (msb of a selector nibble set)
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t d;

@@ -52,6 +52,7 @@ constexpr int kCtaRows = 128;        // token rows per CTA (UMMA M=256 over the 
 constexpr int kTileM = 2 * kCtaRows; // rows per cluster tile
 constexpr int kTileN = 256;          // B rows (output columns) per cluster tile, 128 per CTA
 constexpr int kChunkRows = 128;      // weight rows per raw chunk = one CTA's half of B
+static_assert(kChunkRows == 2 * kChunkHalfRows, "a chunk is two halves");
 constexpr int kNumDequantWarps = 8;
 constexpr int kDequantThreads = kNumDequantWarps * 32;
 constexpr int kNumThreads = (6 + kNumDequantWarps) * 32;  // 448
@@ -165,8 +166,8 @@ struct UnitDecoder {
 };
 
 // Dequantises one stage of this CTA's 128 B rows: item (r, b) = 16 values of
-// row r, k-block quarter b.  The raw stage is one chunk: codes
-// [128][kCodeBytes] then scales [128][4].
+// row r, k-block quarter b.  The raw stage is one chunk (two 64-row halves of
+// codes then scales, chunk_code_off / chunk_scale_off).
 template <int PREC>
 __device__ __forceinline__ void dequant_stage(const uint8_t *raw, uint8_t *btile, int tid) {
     using R = Raw<PREC>;
@@ -175,16 +176,16 @@ __device__ __forceinline__ void dequant_stage(const uint8_t *raw, uint8_t *btile
         const int item = tid + i * kDequantThreads;
         const int r = item >> 2;
         const int b = item & 3;
-        const float s = *reinterpret_cast<const float *>(raw + kChunkRows * R::kCodeBytes + r * 16 + b * 4);
+        const float s = *reinterpret_cast<const float *>(raw + chunk_scale_off(r, R::kCodeBytes) + b * 4);
         uint32_t w[8];
         if (PREC == GTMOE_INT8) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(raw + r * R::kCodeBytes + b * 16);
+            const uint4 c = *reinterpret_cast<const uint4 *>(raw + chunk_code_off(r, R::kCodeBytes) + b * 16);
             int8_decode4(c.x, s, w);
             int8_decode4(c.y, s, w + 2);
             int8_decode4(c.z, s, w + 4);
             int8_decode4(c.w, s, w + 6);
         } else {
-            const uint2 c = *reinterpret_cast<const uint2 *>(raw + r * R::kCodeBytes + b * 8);
+            const uint2 c = *reinterpret_cast<const uint2 *>(raw + chunk_code_off(r, R::kCodeBytes) + b * 8);
             const Fp4Tables t = fp4_tables(s);
             fp4_decode8(c.x, t, w);
             fp4_decode8(c.y, t, w + 4);
@@ -529,8 +530,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
 }
 
 // Re-lays one Int8/FP4 layer (rows x K, reference snapshot layout) into
-// chunks of (chunk_rows rows, 64-wide k-block): codes [rows][code bytes]
-// then scales [rows][4].  One thread per (row, k-block).
+// chunks of (chunk_rows rows, 64-wide k-block), each two 64-row halves of
+// codes [64][code bytes] then scales [64][4].  One thread per (row, k-block).
 __global__ void relayout_kernel(const uint8_t *__restrict__ codes, const float *__restrict__ scales, int rows, int K,
                                 int code_bytes, int chunk_rows, uint8_t *__restrict__ out) {
     const int KB = K / kBK;
@@ -542,9 +543,10 @@ __global__ void relayout_kernel(const uint8_t *__restrict__ codes, const float *
     uint8_t *chunk = out + ((int64_t)nt * KB + kb) * chunk_rows * row_bytes;
     const int64_t src_row = (int64_t)row * KB * code_bytes + (int64_t)kb * code_bytes;
     for (int i = 0; i < code_bytes; i += 16)
-        *reinterpret_cast<uint4 *>(chunk + lr * code_bytes + i) = *reinterpret_cast<const uint4 *>(codes + src_row + i);
+        *reinterpret_cast<uint4 *>(chunk + chunk_code_off(lr, code_bytes) + i) =
+            *reinterpret_cast<const uint4 *>(codes + src_row + i);
     const float4 s = *reinterpret_cast<const float4 *>(scales + (int64_t)row * (K / 16) + kb * 4);
-    *reinterpret_cast<float4 *>(chunk + chunk_rows * code_bytes + lr * 16) = s;
+    *reinterpret_cast<float4 *>(chunk + chunk_scale_off(lr, code_bytes)) = s;
 }
 
 template <int PREC, bool GATED>
