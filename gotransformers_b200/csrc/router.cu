@@ -272,6 +272,46 @@ __global__ void __launch_bounds__(256)
     write_choice(t, k, pick, paff, chosen, gates64, gates32);
 }
 
+// x[x0 .. x0+d) . w[0 .. d) as one sequential float64 sum, each product and
+// each partial sum rounded separately, in input order (vectormath.DotProduct,
+// vector.go:67-74), by the whole warp: lane l fetches inputs 32b+l of every
+// batch b (four batches ahead) and forms the products, lane 0 adds each
+// batch's 32 products in order from shared memory.  Only the additions are
+// serial.  Every lane calls it with the same arguments; all get the result.
+template <int XDT>
+__device__ double exact_dot_warp(const void *x, int64_t x0, const double *__restrict__ w, int d, double *buf,
+                                 int lane) {
+    constexpr int R = 4;
+    const int nb = (d + 31) / 32;
+    double xr[R], wr[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        const int i = 32 * r + lane;
+        xr[r] = i < d ? load_as_double(x, XDT, x0 + i) : 0.0;
+        wr[r] = i < d ? __ldg(w + i) : 0.0;
+    }
+    double s = 0;
+    for (int b = 0; b < nb; b++) {
+        const double p = __dmul_rn(xr[0], wr[0]);
+#pragma unroll
+        for (int r = 0; r < R - 1; r++) {
+            xr[r] = xr[r + 1];
+            wr[r] = wr[r + 1];
+        }
+        const int i = 32 * (b + R) + lane;
+        xr[R - 1] = i < d ? load_as_double(x, XDT, x0 + i) : 0.0;
+        wr[R - 1] = i < d ? __ldg(w + i) : 0.0;
+        buf[lane] = p;
+        __syncwarp();
+        if (lane == 0) {
+            const int n = d - 32 * b < 32 ? d - 32 * b : 32;
+            for (int j = 0; j < n; j++) s = __dadd_rn(s, buf[j]);
+        }
+        __syncwarp();
+    }
+    return __shfl_sync(0xffffffffu, s, 0);
+}
+
 // One warp per flagged token.  With fast scores s^ within eps of the exact
 // ones (thresh = 2 eps), L = s^_(k) and U = s^_(k+1): an expert with
 // s^ > U + thresh is certainly chosen (only the other computed top-k experts
@@ -290,6 +330,8 @@ __global__ void __launch_bounds__(256)
     const int lane = threadIdx.x & 31;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int n = *n_flagged;
+    __shared__ double wsum[8][32];  // per warp: one batch of products (exact_dot_warp)
+    double *wbuf = wsum[threadIdx.x >> 5];
     for (int wi = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); wi < n; wi += warps) {
         const int64_t t = flagged[wi];
         double score[MAXJ], aff[MAXJ];
@@ -309,14 +351,18 @@ __global__ void __launch_bounds__(256)
         }
 #pragma unroll
         for (int j = 0; j < MAXJ; j++) {
-            if (!((unsure >> j) & 1u)) continue;
-            const int e = lane + 32 * j;
-            const double *wr = w64 + (int64_t)e * d;
-            double s = 0;
-            for (int i = 0; i < d; i++) s = __dadd_rn(s, __dmul_rn(load_as_double(x, XDT, t * d + i), wr[i]));
-            s = __dadd_rn(s, bias[e]);
-            aff[j] = affinity_d(s);
-            score[j] = aff[j] + balance[e];
+            uint32_t todo = __ballot_sync(0xffffffffu, (unsure >> j) & 1u);
+            while (todo) {
+                const int src = __ffs(todo) - 1;
+                todo &= todo - 1;
+                const int e = src + 32 * j;
+                double s = exact_dot_warp<XDT>(x, t * d, w64 + (int64_t)e * d, d, wbuf, lane);
+                if (lane == src) {
+                    s = __dadd_rn(s, bias[e]);
+                    aff[j] = affinity_d(s);
+                    score[j] = aff[j] + balance[e];
+                }
+            }
         }
         int n_sure = 0;
 #pragma unroll
