@@ -8,8 +8,17 @@
 // kernels stream each touched expert's Int8/FP4 weight rows once, in the
 // tile-chunk layout the tensor-core kernels use (128 rows x 64 inputs: codes
 // then block scales), dequantise them in registers straight into mma.sync
-// B fragments (no shared-memory round trip for the bf16 weights) and run them
-// against the few token rows (16 per m-tile).
+// B fragments (no shared-memory round trip for the decoded weights) and run
+// them against the few token rows (16 per m-tile).
+//
+// Arithmetic: the token rows (bf16) are converted once per unit to f16,
+// each row scaled by a power of two that puts its largest magnitude in
+// [2^14, 2^15) (exact for every value above 2^-28 of the row's largest,
+// since bf16 significands fit f16's), and the weights
+// are decoded to f16(code * scale) -- for Int8 two byte permutes, a packed
+// subtraction and a packed multiplication per four codes, half the work of a
+// bf16 decode, with 11 significant bits instead of 8.  Products accumulate in
+// float32; the epilogue takes the row scales back out.
 //
 // Work unit: (16-row tile of a group, block of 64 output features = one
 // 64-row half of a weight chunk).  A CTA of eight compute warps and one
@@ -67,25 +76,25 @@ __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t b
 
 // Not volatile: a pure function of its operands, so the compiler may overlap
 // the next block's loads and decoding with it.
-__device__ __forceinline__ void mma_bf16_16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_f16_16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
     asm(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// B fragment of one weight row (16 inputs of block s): two bf16x2, k-slots
+// B fragment of one weight row (16 inputs of block s): two f16x2, k-slots
 // (2q, 2q+1) and (2q+8, 2q+9) = physical inputs 4q..4q+3.
 template <int PREC>
 __device__ __forceinline__ void decode_row_block(const uint8_t *codes, float sc, int row, int s, int q, uint32_t *o) {
     using DL = DecodeLayout<PREC>;
     if (PREC == GTMOE_INT8) {
         const uint32_t w = *reinterpret_cast<const uint32_t *>(codes + row * DL::kCodeBytes + 16 * s + 4 * q);
-        int8_decode4(w, sc, o);
+        int8_decode4_f16(w, pack_f16(sc, sc), o);
     } else {
         const uint32_t w = *reinterpret_cast<const uint16_t *>(codes + row * DL::kCodeBytes + 8 * s + 2 * q);
-        const Fp4Tables t = fp4_tables(sc);
+        const Fp4Tables t = fp4_tables_f16(sc);
         uint32_t v[4];
         fp4_decode8(w, t, v);
         o[0] = v[0];
@@ -128,6 +137,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     __shared__ uint64_t full[kDecodeStages];   // weight step landed (expect_tx by the producer)
     __shared__ uint64_t empty[kDecodeStages];  // every compute warp is done with the step
     __shared__ uint64_t xfull, xempty;         // token rows of the unit landed / released
+    __shared__ float rscale[kDecodeTileRows];  // 2^-e of each token row (f16 tile = bf16 row * 2^e)
     __shared__ int abort_flag;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDecodeStages; s++) {
@@ -187,6 +197,32 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             for (int c = 0; c < 4; c++) acc[l][c] = 0.f;
         const int row = warp * 8 + g8;  // this lane's weight row (feature) in the half
         if (!*abort_p) mbar_wait(&xfull, nu & 1, abort_p, a.err, 14);
+        // bf16 token rows -> f16 in place, each row scaled by the power of two
+        // that puts its largest magnitude in [2^14, 2^15): exact, no overflow
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const int r = warp + kComputeWarps * rr;
+            if (r >= m) continue;
+            uint32_t *p = reinterpret_cast<uint32_t *>(xs + r * xpitch);
+            float mx = 0.f;
+            for (int i = lane; i < K / 2; i += 32) {
+                const uint32_t v = p[i];
+                mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(v << 16)), fabsf(__uint_as_float(v & 0xFFFF0000u))));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            int e = mx > 0.f ? 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127) : 0;
+            e = e < -100 ? -100 : e > 100 ? 100 : e;
+            const float up = __uint_as_float((uint32_t)(e + 127) << 23);
+            for (int i = lane; i < K / 2; i += 32) {
+                const uint32_t v = p[i];
+                p[i] = pack_f16(__uint_as_float(v << 16) * up, __uint_as_float(v & 0xFFFF0000u) * up);
+            }
+            if (lane == 0) rscale[r] = __uint_as_float((uint32_t)(127 - e) << 23);
+        }
+        // the producer's next copies into the tile come after these writes
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
         const uint8_t *xrow = xs + g8 * xpitch + 8 * q;
         for (int kb = 0; kb < KB; kb++, n++) {
             const uint32_t slot = n % kDecodeStages;
@@ -208,7 +244,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
                     const float scl = s == 0 ? sc[l].x : s == 1 ? sc[l].y : s == 2 ? sc[l].z : sc[l].w;
                     uint32_t bw[2];
                     decode_row_block<PREC>(st + l * DL::kHalf, scl, row, s, q, bw);
-                    mma_bf16_16816(acc[l], af, bw[0], bw[1]);
+                    mma_f16_16816(acc[l], af, bw[0], bw[1]);
                 }
             }
             __syncwarp();
@@ -217,7 +253,16 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
         __syncwarp();
         if (lane == 0) mbar_arrive(&xempty);
 
-        // epilogue: acc[l] = tokens (r0 + g8, r0 + g8 + 8) x features (f, f + 1)
+        // epilogue: acc[l] = tokens (r0 + g8, r0 + g8 + 8) x features (f, f + 1),
+        // in units of the rows' scales
+        const float rs0 = rscale[g8], rs1 = rscale[g8 + 8];
+#pragma unroll
+        for (int l = 0; l < 2; l++) {
+            acc[l][0] *= rs0;
+            acc[l][1] *= rs0;
+            acc[l][2] *= rs1;
+            acc[l][3] *= rs1;
+        }
         const int f = fb * kDecodeFeatures + warp * 8 + 2 * q;
         const float *bias0 = L.b32[which];
         const float *bias1 = GATED ? L.b32[1] : nullptr;

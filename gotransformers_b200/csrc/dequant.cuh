@@ -2,6 +2,7 @@
 // registers (shared by the tensor-core kernels and the decode kernels).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include "sm100.cuh"
@@ -78,5 +79,41 @@ __device__ __forceinline__ void int8_decode4(uint32_t w, float s, uint32_t *o) {
     o[1] = pack_bf16(f2 * s, f3 * s);
 }
 
+
+// ---- f16 variants (decode kernels): the same codes to f16(code * scale)
+
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// FP4 tables as in fp4_tables, with the eight scaled magnitudes rounded to f16.
+__device__ __forceinline__ Fp4Tables fp4_tables_f16(float s) {
+    const uint32_t p0 = pack_f16(0.f, 0.5f * s);
+    const uint32_t p1 = pack_f16(s, 1.5f * s);
+    const uint32_t p2 = pack_f16(2.f * s, 3.f * s);
+    const uint32_t p3 = pack_f16(4.f * s, 6.f * s);
+    Fp4Tables t;
+    t.hlo = prmt(p0, p1, 0x7531);
+    t.hhi = prmt(p2, p3, 0x7531);
+    t.llo = prmt(p0, p1, 0x6420);
+    t.lhi = prmt(p2, p3, 0x6420);
+    return t;
+}
+
+// Four Int8 codes -> two f16x2 of f16(code * scale): q + 128 becomes the low
+// byte of the f16 1024 + (q + 128); subtracting 1152 leaves q exactly, and one
+// multiplication by the f16 scale rounds once.
+__device__ __forceinline__ void int8_decode4_f16(uint32_t w, uint32_t s2, uint32_t *o) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t h01 = prmt(u, 0x64646464u, 0x5140);
+    const uint32_t h23 = prmt(u, 0x64646464u, 0x7362);
+    const __half2 bias = __floats2half2_rn(1152.f, 1152.f);
+    const __half2 sc = *reinterpret_cast<const __half2 *>(&s2);
+    __half2 v01 = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&h01), bias), sc);
+    __half2 v23 = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&h23), bias), sc);
+    o[0] = *reinterpret_cast<uint32_t *>(&v01);
+    o[1] = *reinterpret_cast<uint32_t *>(&v23);
+}
 
 }  // namespace gtmoe

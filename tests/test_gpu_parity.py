@@ -302,8 +302,9 @@ def test_config_sampled(name):
 @pytest.mark.parametrize("prec", [O.INT8, O.FP4])
 def test_decode_path_matches_tensor_core_path(prec):
     """The same decode-shaped batch through the weight-streaming kernels and
-    through the 256-row tensor-core kernels: identical routing, outputs equal
-    up to float32 summation order."""
+    through the 256-row tensor-core kernels: identical routing, both within
+    tolerance of the oracle, and the decode path (f16 weights, 11 significant
+    bits) at least as close to it as the tensor-core path (bf16 weights)."""
     spec, x, ids = make_case(T=48, d=256, h=256, n_shared=1, n_routed=12, k=3, precision=prec, seed=23,
                              x_bf16=True, layer_bias=0.1)
     m = gpu_moe(spec)
@@ -315,6 +316,7 @@ def test_decode_path_matches_tensor_core_path(prec):
     finally:
         del os.environ["GTMOE_DISABLE_DECODE"]
     assert np.array_equal(m.last_chosen_experts, chosen)
-    assert rel_l2(out_dec, out_tc) <= 1e-3
-    check_against_oracle(spec, x, ids, out_dec, m)
+    err_dec = check_against_oracle(spec, x, ids, out_dec, m)
+    err_tc = check_against_oracle(spec, x, ids, out_tc, m)
+    assert err_dec <= err_tc + 1e-4, (err_dec, err_tc)
     m.close()
