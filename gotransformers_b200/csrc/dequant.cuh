@@ -12,7 +12,8 @@ namespace gtmoe {
 // Tile-chunk layout of Int8/FP4 weights (tc.cu, decode.cu): per 128-row block
 // and 64-input step one chunk of two 64-row halves, each codes
 // [64][code_bytes] then block scales [64][4 floats], so that a half is one
-// contiguous bulk copy.
+// contiguous bulk copy.  Int8 codes are stored biased, as the bytes q + 128
+// (the decoders place them straight into a float or half mantissa).
 constexpr int kChunkHalfRows = 64;
 __host__ __device__ __forceinline__ int chunk_code_off(int r, int code_bytes) {
     return (r / kChunkHalfRows) * kChunkHalfRows * (code_bytes + 16) + (r % kChunkHalfRows) * code_bytes;
@@ -66,10 +67,10 @@ __device__ __forceinline__ void fp4_decode8(uint32_t w, const Fp4Tables &t, uint
     o[3] = prmt(l1, h1, 0x7362);
 }
 
-// Four Int8 codes -> two bf16x2 of bf16(code * scale): q + 128 becomes the
-// low byte of the float 2^23 + q + 128, from which q is recovered exactly.
-__device__ __forceinline__ void int8_decode4(uint32_t w, float s, uint32_t *o) {
-    const uint32_t u = w ^ 0x80808080u;
+// Four biased Int8 codes (bytes q + 128) -> two bf16x2 of bf16(q * scale):
+// the byte becomes the low byte of the float 2^23 + q + 128, from which q is
+// recovered exactly.
+__device__ __forceinline__ void int8_decode4(uint32_t u, float s, uint32_t *o) {
     const float magic = 8388736.f;  // 2^23 + 128
     const float f0 = __uint_as_float(prmt(u, 0x4B000000u, 0x7650)) - magic;
     const float f1 = __uint_as_float(prmt(u, 0x4B000000u, 0x7651)) - magic;
@@ -101,11 +102,10 @@ __device__ __forceinline__ Fp4Tables fp4_tables_f16(float s) {
     return t;
 }
 
-// Four Int8 codes -> two f16x2 of f16(code * scale): q + 128 becomes the low
-// byte of the f16 1024 + (q + 128); subtracting 1152 leaves q exactly, and one
-// multiplication by the f16 scale rounds once.
-__device__ __forceinline__ void int8_decode4_f16(uint32_t w, uint32_t s2, uint32_t *o) {
-    const uint32_t u = w ^ 0x80808080u;
+// Four biased Int8 codes (bytes q + 128) -> two f16x2 of f16(q * scale): the
+// byte becomes the low byte of the f16 1024 + (q + 128); subtracting 1152
+// leaves q exactly, and one multiplication by the f16 scale rounds once.
+__device__ __forceinline__ void int8_decode4_f16(uint32_t u, uint32_t s2, uint32_t *o) {
     const uint32_t h01 = prmt(u, 0x64646464u, 0x5140);
     const uint32_t h23 = prmt(u, 0x64646464u, 0x7362);
     const __half2 bias = __floats2half2_rn(1152.f, 1152.f);

@@ -542,9 +542,16 @@ __global__ void relayout_kernel(const uint8_t *__restrict__ codes, const float *
     const int row_bytes = code_bytes + 16;
     uint8_t *chunk = out + ((int64_t)nt * KB + kb) * chunk_rows * row_bytes;
     const int64_t src_row = (int64_t)row * KB * code_bytes + (int64_t)kb * code_bytes;
-    for (int i = 0; i < code_bytes; i += 16)
-        *reinterpret_cast<uint4 *>(chunk + chunk_code_off(lr, code_bytes) + i) =
-            *reinterpret_cast<const uint4 *>(codes + src_row + i);
+    // Int8 codes biased to q + 128 (see chunk_code_off)
+    const uint32_t bias = code_bytes == 64 ? 0x80808080u : 0u;
+    for (int i = 0; i < code_bytes; i += 16) {
+        uint4 c = *reinterpret_cast<const uint4 *>(codes + src_row + i);
+        c.x ^= bias;
+        c.y ^= bias;
+        c.z ^= bias;
+        c.w ^= bias;
+        *reinterpret_cast<uint4 *>(chunk + chunk_code_off(lr, code_bytes) + i) = c;
+    }
     const float4 s = *reinterpret_cast<const float4 *>(scales + (int64_t)row * (K / 16) + kb * 4);
     *reinterpret_cast<float4 *>(chunk + chunk_scale_off(lr, code_bytes)) = s;
 }
