@@ -87,7 +87,7 @@ class ClockSampler:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
 
@@ -226,6 +226,9 @@ def main():
         if world > 1:
             dist.barrier()
 
+    # clocks: nvidia-smi starts sampling before the warm-up steps, so that it
+    # is running through the whole timed region, and stops right after it
+    sampler = ClockSampler()
     for _ in range(args.warmup):
         moe.forward(x, out=out, want_routing=False)
     torch.cuda.synchronize(dev)
@@ -236,7 +239,6 @@ def main():
 
     launches = ctypes.c_int64()
     _lib.check(L.gtmoe_read_timing(moe.handle, None, 0, None, ctypes.byref(launches)))  # restarts the count
-    sampler = ClockSampler()
     torch.cuda.synchronize(dev)
     barrier()
     # decode-shaped batches touch less than a few L2s of weights: write a
