@@ -252,6 +252,80 @@ int refresh_table(gtmoe_handle *h) {
 }
 
 // Single-GPU forward on device-resident x (x_dev) producing device out.
+static int forward_prepare(gtmoe_handle *h, int64_t T);
+// Host-buffer batches from this many rows on are pipelined in chunks.
+constexpr int64_t kPipelineMinRows = 16384;
+
+__global__ void add_load_kernel(int64_t *__restrict__ acc, const int64_t *__restrict__ load, int E) {
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < E; e += gridDim.x * blockDim.x) acc[e] += load[e];
+}
+
+// A large batch in host memory, as chunks: chunk c+1's input copy and chunk
+// c-1's output copy (their own streams) run while chunk c computes.  Rows are
+// independent, so the outputs equal one whole-batch forward's; the per-expert
+// load is summed over the chunks (LastExpertLoad sees the whole batch).
+static int forward_pipelined(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int64_t *ids_dev,
+                             const void *res_dev, void *out, int out_dtype, int32_t *chosen, double *gates,
+                             int64_t *load, int nc) {
+    const gtmoe_config &c = h->cfg;
+    const int d = c.d_model, k = c.experts_per_token, E = c.n_routed;
+    cudaStream_t st = h->stream;
+    const size_t xrow = dtype_size(x_dtype) * d, orow = dtype_size(out_dtype) * d;
+    const int64_t Tc = (T + nc - 1) / nc;
+    if (!h->h2d_stream) GT_CUDA(cudaStreamCreateWithFlags(&h->h2d_stream, cudaStreamNonBlocking));
+    if (!h->d2h_stream) GT_CUDA(cudaStreamCreateWithFlags(&h->d2h_stream, cudaStreamNonBlocking));
+    for (cudaEvent_t &e : h->pipe_ev)
+        if (!e) GT_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (int s = 0; s < 2; s++) {
+        GT_CHECK(h->x_pipe[s].ensure(xrow * (size_t)Tc));
+        GT_CHECK(h->out_pipe[s].ensure(orow * (size_t)Tc));
+    }
+    GT_CHECK(h->load_acc.ensure(sizeof(int64_t) * E));
+    GT_CHECK(forward_prepare(h, Tc));
+    GT_CUDA(cudaMemsetAsync(h->load_acc.p, 0, sizeof(int64_t) * E, st));
+    // the side streams start after everything already queued on the handle's stream
+    cudaEvent_t *x_ready = h->pipe_ev, *x_free = h->pipe_ev + 2, *out_ready = h->pipe_ev + 4,
+                *out_free = h->pipe_ev + 6;
+    GT_CUDA(cudaEventRecord(x_free[0], st));
+    GT_CUDA(cudaStreamWaitEvent(h->h2d_stream, x_free[0], 0));
+    GT_CUDA(cudaStreamWaitEvent(h->d2h_stream, x_free[0], 0));
+    for (int ci = 0; ci < nc; ci++) {
+        const int64_t t0 = (int64_t)ci * Tc;
+        const int64_t n = T - t0 < Tc ? T - t0 : Tc;
+        if (n <= 0) break;
+        const int s = ci & 1;
+        if (ci >= 2) GT_CUDA(cudaStreamWaitEvent(h->h2d_stream, x_free[s], 0));
+        GT_CUDA(cudaMemcpyAsync(h->x_pipe[s].p, (const char *)x + t0 * xrow, n * xrow, cudaMemcpyHostToDevice,
+                                h->h2d_stream));
+        GT_CUDA(cudaEventRecord(x_ready[s], h->h2d_stream));
+        GT_CUDA(cudaStreamWaitEvent(st, x_ready[s], 0));
+        if (ci >= 2) GT_CUDA(cudaStreamWaitEvent(st, out_free[s], 0));
+        GT_CHECK(forward_device(h, h->x_pipe[s].p, x_dtype, n, ids_dev ? ids_dev + t0 : nullptr,
+                                res_dev ? (const char *)res_dev + t0 * orow : nullptr, h->out_pipe[s].p, out_dtype));
+        GT_CUDA(cudaEventRecord(x_free[s], st));
+        add_load_kernel<<<1, 256, 0, st>>>(h->load_acc.as<int64_t>(), h->load.as<int64_t>(), E);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+        // the next chunk overwrites the routing workspace: copy this chunk's now
+        if (chosen) GT_CUDA(cudaMemcpyAsync(chosen + t0 * k, h->chosen.p, sizeof(int32_t) * n * k, cudaMemcpyDefault, st));
+        if (gates) GT_CUDA(cudaMemcpyAsync(gates + t0 * k, h->gates64.p, sizeof(double) * n * k, cudaMemcpyDefault, st));
+        GT_CUDA(cudaEventRecord(out_ready[s], st));
+        GT_CUDA(cudaStreamWaitEvent(h->d2h_stream, out_ready[s], 0));
+        GT_CUDA(cudaMemcpyAsync((char *)out + t0 * orow, h->out_pipe[s].p, n * orow, cudaMemcpyDeviceToHost,
+                                h->d2h_stream));
+        GT_CUDA(cudaEventRecord(out_free[s], h->d2h_stream));
+    }
+    // the whole batch's load where LastExpertLoad and UpdateBalance read it
+    GT_CUDA(cudaMemcpyAsync(h->load.p, h->load_acc.p, sizeof(int64_t) * E, cudaMemcpyDeviceToDevice, st));
+    if (load) GT_CUDA(cudaMemcpyAsync(load, h->load.p, sizeof(int64_t) * E, cudaMemcpyDefault, st));
+    GT_CUDA(cudaStreamSynchronize(h->d2h_stream));
+    GT_CUDA(cudaStreamSynchronize(st));
+    GT_CHECK(tc_check_error(h->tc));
+    h->last_T = T;
+    h->have_load = 1;
+    return 0;
+}
+
 // Workspace of a T-row forward on one GPU (grow-only; no-op when it fits).
 static int forward_prepare(gtmoe_handle *h, int64_t T) {
     const gtmoe_config &c = h->cfg;
@@ -535,8 +609,13 @@ void gtmoe_destroy(gtmoe_t h) {
         DevBuf *bufs[] = {&h->wr64, &h->wr32, &h->wr3, &h->br, &h->bal, &h->table, &h->x_in, &h->ids, &h->logits,
                           &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load, &h->offsets, &h->perm,
                           &h->slot_row, &h->groups, &h->tile_prefix, &h->xp, &h->hp, &h->yp, &h->out_dev,
-                          &h->res_dev, &h->fixups, &h->flagged};
+                          &h->res_dev, &h->fixups, &h->flagged, &h->x_pipe[0], &h->x_pipe[1], &h->out_pipe[0],
+                          &h->out_pipe[1], &h->load_acc};
         for (DevBuf *b : bufs) b->release();
+        for (cudaEvent_t e : h->pipe_ev)
+            if (e) cudaEventDestroy(e);
+        if (h->h2d_stream) cudaStreamDestroy(h->h2d_stream);
+        if (h->d2h_stream) cudaStreamDestroy(h->d2h_stream);
         for (auto &pe : h->tev)
             for (int i = 0; i < GTMOE_N_PHASES; i++) {
                 cudaEventDestroy(pe.start[i]);
@@ -729,8 +808,13 @@ int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_
     const size_t xbytes = dtype_size(x_dtype) * (size_t)T * d;
     const size_t obytes = dtype_size(out_dtype) * (size_t)T * d;
 
+    // a large batch in host memory runs as chunks whose copies overlap compute
+    // (not with timing, a host residual, or the whole-batch permutation asked for)
+    const bool pipelined = T >= kPipelineMinRows && !h->timing && !perm && !is_device_ptr(x) &&
+                           !is_device_ptr(out) && (!residual || is_device_ptr(residual));
+
     const void *x_dev = x;
-    if (T > 0 && !is_device_ptr(x)) {
+    if (T > 0 && !pipelined && !is_device_ptr(x)) {
         GT_CHECK(upload(h->x_in, x, xbytes, st));
         x_dev = h->x_in.p;
     }
@@ -752,10 +836,15 @@ int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_
         res_dev = h->res_dev.p;
     }
     void *out_dev = out;
-    const bool out_host = T > 0 && !is_device_ptr(out);
+    const bool out_host = T > 0 && !pipelined && !is_device_ptr(out);
     if (out_host) {
         GT_CHECK(h->out_dev.ensure(obytes));
         out_dev = h->out_dev.p;
+    }
+    if (pipelined) {
+        h->drop_graph();
+        return forward_pipelined(h, x, x_dtype, T, ids_dev, res_dev, out, out_dtype, chosen, gates, load,
+                                 T >= 4 * kPipelineMinRows ? 4 : 2);
     }
     // device pointers only, no host round trip inside: the forward may be replayed as a CUDA graph
     const bool graphable = !c.hash_routing && x_dev == x && out_dev == out && res_dev == residual;

@@ -94,6 +94,12 @@ struct gtmoe_handle {
     size_t tev_used = 0;
     int64_t launches_at_read = 0;
 
+    // host-buffer forwards of large batches: chunks whose copies overlap the
+    // compute of their neighbours (api.cu, forward_pipelined)
+    DevBuf x_pipe[2], out_pipe[2], load_acc;
+    cudaStream_t h2d_stream = nullptr, d2h_stream = nullptr;
+    cudaEvent_t pipe_ev[8] = {};  // x ready / x free / out ready / out free, per slot
+
     // CUDA-graph replay of the device forward (gtmoe_set_graphs): a call
     // whose arguments and workspace equal the previous call's replays the
     // graph captured on the second such call
