@@ -53,6 +53,12 @@ EXPORTS = [
     "gtmoe_quantize_rows",
     "gtmoe_fill_normal",
     "gtmoe_route_noalloc",
+    "gtmoe_weightfile_open",
+    "gtmoe_weightfile_close",
+    "gtmoe_weightfile_count",
+    "gtmoe_weightfile_info",
+    "gtmoe_weightfile_set_expert_layer",
+    "gtmoe_weightfile_set_router",
 ]
 
 
@@ -117,8 +123,17 @@ def lib():
             L.gtmoe_quantize_rows.argtypes = [i32, vp, i64, i32, vp, vp]
             L.gtmoe_route_noalloc.argtypes = [vp, vp, i32, i64, vp, vp, vp]
             L.gtmoe_fill_normal.argtypes = [vp, i32, i64, ctypes.c_uint64, ctypes.c_uint64, i64, d]
+            L.gtmoe_weightfile_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(vp)]
+            L.gtmoe_weightfile_close.argtypes = [vp]
+            L.gtmoe_weightfile_close.restype = None
+            L.gtmoe_weightfile_count.argtypes = [vp]
+            L.gtmoe_weightfile_info.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(i32),
+                                                ctypes.POINTER(i32), ctypes.POINTER(i64), ctypes.POINTER(i64),
+                                                ctypes.POINTER(i64)]
+            L.gtmoe_weightfile_set_expert_layer.argtypes = [vp, vp, i32, i32, i32, ctypes.c_char_p, ctypes.c_char_p]
+            L.gtmoe_weightfile_set_router.argtypes = [vp, vp, ctypes.c_char_p, ctypes.c_char_p]
             for name in EXPORTS:
-                if name not in ("gtmoe_destroy",):
+                if name not in ("gtmoe_destroy", "gtmoe_weightfile_close"):
                     fn = getattr(L, name)
                     if fn.restype is not ctypes.c_char_p:
                         fn.restype = i32

@@ -232,6 +232,46 @@ class MixtureOfExperts:
         check(_lib.lib().gtmoe_update_balance(self._h, rate))
 
 
+class WeightFile:
+    """A GoTransformers binary weights file (weightfile/binaryfile.go) opened
+    for loading straight into MixtureOfExperts layers.  ``params`` maps each
+    parameter name to (stored_as, precision, rows, width, values): stored_as 1
+    float64, 2 float32, 3 bfloat16, 4 compressed rows."""
+
+    def __init__(self, path: str):
+        L = _lib.lib()
+        self._wf = ctypes.c_void_p()
+        check(L.gtmoe_weightfile_open(str(path).encode(), ctypes.byref(self._wf)))
+        self.params = {}
+        name = ctypes.c_char_p()
+        st, prec = ctypes.c_int(), ctypes.c_int()
+        rows, width, vals = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        for i in range(L.gtmoe_weightfile_count(self._wf)):
+            check(L.gtmoe_weightfile_info(self._wf, i, ctypes.byref(name), ctypes.byref(st), ctypes.byref(prec),
+                                          ctypes.byref(rows), ctypes.byref(width), ctypes.byref(vals)))
+            self.params[name.value.decode()] = (st.value, prec.value, rows.value, width.value, vals.value)
+
+    def close(self):
+        if self._wf:
+            _lib.lib().gtmoe_weightfile_close(self._wf)
+            self._wf = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_expert_layer(self, moe: "MixtureOfExperts", kind: int, index: int, which: int, weights: str,
+                         bias: str | None = None):
+        check(_lib.lib().gtmoe_weightfile_set_expert_layer(self._wf, moe.handle, kind, index, which, weights.encode(),
+                                                           bias.encode() if bias else None))
+
+    def set_router(self, moe: "MixtureOfExperts", weights: str, bias: str | None = None):
+        check(_lib.lib().gtmoe_weightfile_set_router(self._wf, moe.handle, weights.encode(),
+                                                     bias.encode() if bias else None))
+
+
 def fill_normal(tensor, seed: int, stream: int, offset: int = 0, stddev: float = 1.0):
     """Benchmark input generator on device memory (synthetic.normal's definition)."""
     check(_lib.lib().gtmoe_fill_normal(_addr(tensor), _dtype_code(tensor), tensor.numel(), seed, stream, offset,
@@ -243,6 +283,7 @@ __all__ = [
     "Rows",
     "quantize_rows",
     "fill_normal",
+    "WeightFile",
     "FLOAT64",
     "FLOAT32",
     "INT8",

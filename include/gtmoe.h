@@ -105,6 +105,34 @@ GTMOE_API int gtmoe_ep_unique_id(void *nccl_id_128);
 GTMOE_API int gtmoe_create_ep(const gtmoe_config *cfg, int device, int n_ranks, int rank, const void *nccl_id_128,
                     gtmoe_t *out);
 
+/* GoTransformers binary weights files (weightfile/binaryfile.go): a saved
+ * model's parameters read straight into a handle.  gtmoe_weightfile_open maps
+ * the file, checks its marker (GOTRANSFORMERS-WEIGHTS-1 or -2,
+ * binaryfile.go:13-14) and indexes every parameter record the way
+ * ReadBinaryKeepingCompressed walks them (:157-230), with the same checks on
+ * names, counts and sizes (and RowsFromSnapshot's, lowprecision/rows.go:
+ * 172-203); errors are GTMOE_EINVAL with the reference's message.  Host only:
+ * needs no GPU.  No counterpart in the reference's MoE API (it loads through
+ * weightfile.ReadBinaryKeepingCompressed into Go memory). */
+typedef struct gtmoe_weightfile *gtmoe_wf_t;
+GTMOE_API int gtmoe_weightfile_open(const char *path, gtmoe_wf_t *out);
+GTMOE_API void gtmoe_weightfile_close(gtmoe_wf_t wf);
+GTMOE_API int gtmoe_weightfile_count(gtmoe_wf_t wf);
+/* Parameter i: its name (valid until close), how it is stored (1 float64,
+ * 2 float32, 3 bfloat16, 4 compressed rows, binaryfile.go:16-21); for
+ * compressed rows its precision (GTMOE_FLOAT64..GTMOE_FP4), rows and width
+ * (-1, 0, 0 otherwise); values = rows*width or the dense value count. */
+GTMOE_API int gtmoe_weightfile_info(gtmoe_wf_t wf, int i, const char **name, int *stored_as, int *precision,
+                                    int64_t *rows, int64_t *width, int64_t *values);
+/* gtmoe_set_expert_layer from the file: `weights` names a compressed-rows
+ * parameter (its RowsSnapshot lists go to the device as they are in the file)
+ * or a dense one (float64 layer; float32/bfloat16 values widened as
+ * ReadBinary does); `bias` a dense parameter of `rows` values or NULL. */
+GTMOE_API int gtmoe_weightfile_set_expert_layer(gtmoe_wf_t wf, gtmoe_t h, int kind, int index, int which,
+                                                const char *weights, const char *bias);
+/* gtmoe_set_router from the file (E x d weights, E-value bias or NULL). */
+GTMOE_API int gtmoe_weightfile_set_router(gtmoe_wf_t wf, gtmoe_t h, const char *weights, const char *bias);
+
 /* Frees every device allocation of the handle.  NULL is ignored. */
 GTMOE_API void gtmoe_destroy(gtmoe_t h);
 
