@@ -610,7 +610,7 @@ void gtmoe_destroy(gtmoe_t h) {
                           &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load, &h->offsets, &h->perm,
                           &h->slot_row, &h->groups, &h->tile_prefix, &h->xp, &h->hp, &h->yp, &h->out_dev,
                           &h->res_dev, &h->fixups, &h->flagged, &h->x_pipe[0], &h->x_pipe[1], &h->out_pipe[0],
-                          &h->out_pipe[1], &h->load_acc};
+                          &h->out_pipe[1], &h->load_acc, &h->norm_w, &h->block_x, &h->block_xn};
         for (DevBuf *b : bufs) b->release();
         for (cudaEvent_t e : h->pipe_ev)
             if (e) cudaEventDestroy(e);
@@ -782,6 +782,15 @@ int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_
                   void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load) {
     if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
     std::lock_guard<std::mutex> lock(h->mu);
+    return forward_locked(h, x, x_dtype, T, token_ids, residual, out, out_dtype, chosen, gates, perm, load);
+}
+
+}  // extern "C"
+
+namespace gtmoe {
+
+int forward_locked(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
+                   void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load) {
     GT_CUDA(cudaSetDevice(h->device));
     const gtmoe_config &c = h->cfg;
     auto check_args = [&]() -> int {
@@ -875,6 +884,10 @@ int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_
     }
     return 0;
 }
+
+}  // namespace gtmoe
+
+extern "C" {
 
 int gtmoe_last_expert_load(gtmoe_t h, int64_t *load) {
     if (!h || !load) return fail(GTMOE_EINVAL, "handle or load is NULL");

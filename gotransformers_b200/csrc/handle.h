@@ -94,6 +94,12 @@ struct gtmoe_handle {
     size_t tev_used = 0;
     int64_t launches_at_read = 0;
 
+    // the block's RMSNorm (block.cu): weights (d, float64), epsilon, and the
+    // input / normalized rows of gtmoe_forward_block
+    DevBuf norm_w, block_x, block_xn;
+    double norm_eps = 0;
+    int norm_set = 0;
+
     // host-buffer forwards of large batches: chunks whose copies overlap the
     // compute of their neighbours (api.cu, forward_pipelined)
     DevBuf x_pipe[2], out_pipe[2], load_acc;
@@ -129,6 +135,9 @@ int create_handle(const gtmoe_config *cfg, int device, int n_ranks, int rank, gt
 
 // expert parallelism (ep.cu)
 void ep_destroy(gtmoe_handle *h);
+// gtmoe_forward with the handle's lock already held
+int forward_locked(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
+                   void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load);
 int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
                void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load, int arg_rc);
 int ep_global_load(gtmoe_handle *h, int64_t *load);

@@ -223,6 +223,45 @@ class MixtureOfExperts:
             self._last_load = load
         return out
 
+    # -- the block's feed-forward step (transformer.Block.Forward, block.go:72-77)
+    def set_norm(self, weights, epsilon: float = 1e-6):
+        """The block's FeedForwardNorm (RMSNorm weights and epsilon)."""
+        weights = np.ascontiguousarray(weights, np.float64)
+        if weights.shape != (self.cfg.d_model,):
+            raise ValueError(f"RMSNorm has {weights.shape[0]} weights but the vectors have {self.cfg.d_model} values")
+        check(_lib.lib().gtmoe_set_norm(self._h, _addr(weights), float(epsilon)))
+
+    def forward_block(self, x, token_ids=None, out=None, want_routing: bool = True):
+        """x + Forward(RMSNorm(x)), in one call; out has x's dtype."""
+        T = x.shape[0]
+        if x.ndim != 2 or x.shape[1] != self.cfg.d_model:
+            raise ValueError(f"each row has {x.shape[-1]} values but the experts take {self.cfg.d_model}")
+        xdt = _dtype_code(x)
+        ids = None
+        if token_ids is not None:
+            ids = token_ids if hasattr(token_ids, "data_ptr") else np.ascontiguousarray(token_ids, np.int64)
+        if out is None:
+            if isinstance(x, np.ndarray):
+                out = np.empty_like(x)
+            else:
+                import torch
+
+                out = torch.empty_like(x)
+        k = self.cfg.experts_per_token
+        chosen = gates = perm = load = None
+        if want_routing:
+            chosen = np.empty((T, k), np.int32)
+            gates = np.empty((T, k), np.float64)
+            perm = np.empty(T * k, np.int32)
+            load = np.empty(self.cfg.n_routed, np.int64)
+        check(_lib.lib().gtmoe_forward_block(self._h, _addr(x), xdt, T, _addr(ids), _addr(out), _dtype_code(out),
+                                             _addr(chosen), _addr(gates), _addr(perm), _addr(load)))
+        if want_routing:
+            self.last_chosen_experts = chosen
+            self.last_gates = gates
+            self.last_rows_for_expert = perm
+        return out
+
     def last_expert_load(self) -> np.ndarray:
         out = np.empty(self.cfg.n_routed, np.int64)
         check(_lib.lib().gtmoe_last_expert_load(self._h, _addr(out)))

@@ -105,6 +105,20 @@ GTMOE_API int gtmoe_ep_unique_id(void *nccl_id_128);
 GTMOE_API int gtmoe_create_ep(const gtmoe_config *cfg, int device, int n_ranks, int rank, const void *nccl_id_128,
                     gtmoe_t *out);
 
+/* The mixture-of-experts half of transformer.Block.Forward (block.go:72-77,
+ * no hyper-connections, dropout off): out = x + Forward(RMSNorm(x)), in one
+ * call.  gtmoe_set_norm sets the block's FeedForwardNorm (RMSNorm weights,
+ * d_model float64, and epsilon; normalization/rmsnorm.go:10-31);
+ * gtmoe_forward_block normalizes on the GPU in float64 exactly as
+ * RMSNorm.Forward (:33-53) does, routes and runs the experts on the
+ * normalized rows and adds x.  out_dtype must equal x_dtype.  The optional
+ * routing outputs are gtmoe_forward's.  One GPU (not expert parallel).  No
+ * counterpart in the reference's MoE API. */
+GTMOE_API int gtmoe_set_norm(gtmoe_t h, const double *weights, double epsilon);
+GTMOE_API int gtmoe_forward_block(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids,
+                                  void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm,
+                                  int64_t *load);
+
 /* GoTransformers binary weights files (weightfile/binaryfile.go): a saved
  * model's parameters read straight into a handle.  gtmoe_weightfile_open maps
  * the file, checks its marker (GOTRANSFORMERS-WEIGHTS-1 or -2,

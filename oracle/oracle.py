@@ -20,6 +20,8 @@ import subprocess
 import threading
 from dataclasses import dataclass, field
 
+import math
+
 import numpy as np
 
 FLOAT64, FLOAT32, INT8, FP4 = 0, 1, 2, 3
@@ -304,3 +306,21 @@ def softplus(x: float) -> float:
 
 def affinity(x: float) -> float:
     return lib().gto_affinity(x)
+
+
+def rmsnorm(x: np.ndarray, weights: np.ndarray, epsilon: float) -> np.ndarray:
+    """RMSNorm.Forward (normalization/rmsnorm.go:33-53) in float64: the sum of
+    squares as one sequential DotProduct (vectormath/vector.go:67-74), / d,
+    + epsilon, math.Sqrt, then value / rms * weight.  Python floats are IEEE
+    doubles with each operation rounded, as in Go; plain loops, small cases."""
+    x = np.asarray(x, np.float64)
+    T, d = x.shape
+    out = np.empty_like(x)
+    for t in range(T):
+        row = [float(v) for v in x[t]]
+        s = 0.0
+        for v in row:
+            s += v * v
+        rms = math.sqrt(s / d + epsilon)
+        out[t] = [v / rms * float(w) for v, w in zip(row, weights)]
+    return out

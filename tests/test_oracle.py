@@ -298,3 +298,15 @@ def test_generator_is_deterministic_and_normal():
     b = synthetic.normal(1, 5, 1000, offset=500)
     assert np.array_equal(a[500:1500], b)
     assert abs(a.mean()) < 0.02 and abs(a.std() - 1) < 0.02
+
+
+def test_rmsnorm_restatement():
+    # normalization/rmsnorm.go:33-53 on a hand-checkable row: mean of squares
+    # (9 + 16) / 2 = 12.5, rms = sqrt(12.5 + eps)
+    out = O.rmsnorm(np.array([[3.0, -4.0]]), np.array([1.0, 2.0]), 0.0)
+    r = np.sqrt(12.5)
+    assert out[0, 0] == 3.0 / r * 1.0 and out[0, 1] == -4.0 / r * 2.0
+    x = np.random.default_rng(3).standard_normal((5, 37))
+    w = np.linspace(0.5, 1.5, 37)
+    ref = x / np.sqrt((x * x).mean(axis=1, keepdims=True) + 1e-6) * w
+    np.testing.assert_allclose(O.rmsnorm(x, w, 1e-6), ref, rtol=1e-13)
