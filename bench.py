@@ -1,11 +1,11 @@
 #!/usr/bin/env python
-"""MoE-layer forward benchmark (BASELINE metric: MoE-layer tokens/s).
+"""MoE-layer forward benchmark (metric: MoE-layer tokens/s).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5] [--impl ours|reference]
 
 One step = one MixtureOfExperts.Forward of the config's whole token batch
 (whole-job: all ranks' tokens).  Under torchrun (N > 1) each rank owns T/N
-tokens; the default workload is BASELINE config 5 (65536 tokens x d 4096,
+tokens; the default workload is config c5 (65536 tokens x d 4096,
 256 routed experts + 1 shared, hidden 2048, top-8, FP4 experts, bf16
 activations, Zipf(1.0) router bias), the configuration the metric is quoted
 on at 1/2/4/8 GPUs.  Inputs are seeded synthetic data of the config's shape

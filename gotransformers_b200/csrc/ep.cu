@@ -1,7 +1,7 @@
 // ep.cu -- expert parallelism across GPUs (one process per GPU).
 //
 // The reference runs MixtureOfExperts.Forward in one process
-// (mixtureofexperts.go:122-216); BASELINE's config 5 shards its routed
+// (mixtureofexperts.go:122-216); the benchmark's config c5 shards its routed
 // experts over 1-8 GPUs.  Per rank r of G (routed experts r*E/G .. (r+1)*E/G-1
 // owned, router and shared experts replicated, tokens split by the caller):
 //   1. route this rank's tokens (router.cu) and dispatch them over all E

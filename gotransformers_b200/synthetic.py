@@ -1,6 +1,6 @@
 """Seeded synthetic inputs for the benchmark and the parity tests.
 
-The reference publishes no dataset for this path; BASELINE's configs describe
+The reference publishes no dataset for this path; the benchmark configs describe
 synthetic inputs (activations N(0,1), weights N(0, 1/fan_in) quantised by the
 reference quantiser, Zipf-skewed router biases).  Value i of a stream is a
 pure function of (seed, stream, i):
@@ -98,7 +98,7 @@ class MoEConfig:
         return self.T * (self.k + self.n_shared) * 6.0 * self.d * self.h + self.T * 2.0 * self.d * self.n_routed
 
 
-# BASELINE configs.  c4 has three batch sizes.
+# The benchmark configs c1-c5.  c4 has three batch sizes.
 CONFIGS = {
     "c1": MoEConfig("c1", 512, 256, 512, 0, 8, 2, 1, False),
     "c2": MoEConfig("c2", 4096, 1024, 2048, 0, 16, 2, 2, False, weight_seed=2, act_seed=3),

@@ -238,7 +238,7 @@ def test_gpu_generator_matches_numpy():
 
 
 def config_case(name):
-    """Full-size BASELINE config, weights generated and quantised on the GPU
+    """Full-size benchmark config, weights generated and quantised on the GPU
     (gtmoe_fill_normal + gtmoe_quantize_rows); the oracle gets the same bytes."""
     import torch
 
@@ -262,7 +262,7 @@ def config_case(name):
 
 
 def test_config_c1_full():
-    """BASELINE config 1 (Float32, 512 x 256, E8 k2 h512), every token."""
+    """Benchmark config c1 (Float32, 512 x 256, E8 k2 h512), every token."""
     spec, x, ids, m = config_case("c1")
     out = m.forward(x, ids)
     err = check_against_oracle(spec, x, ids, out, m)
