@@ -45,15 +45,15 @@ namespace {
 
 constexpr int kComputeWarps = 8;                          // 8 features each
 constexpr int kDecodeThreads = (kComputeWarps + 1) * 32;  // + one producer warp
-constexpr int kDecodeFeatures = kChunkHalfRows;           // output features per unit
+constexpr int kDecodeFeatures = kHalfRows;               // output features per unit
 constexpr int kDecodeStages = 4;
 
 template <int PREC>
 struct DecodeLayout {
     static constexpr int kCodeBytes = PREC == GTMOE_INT8 ? 64 : 32;  // per row and 64 inputs
     static constexpr int kChunkRowBytes = kCodeBytes + 16;           // codes + 4 float scales
-    static constexpr int kCodes = kDecodeFeatures * kCodeBytes;      // one half's codes
-    static constexpr int kHalf = kDecodeFeatures * kChunkRowBytes;   // codes + scales: one bulk copy
+    static constexpr int kHalf = half_bytes(kCodeBytes);             // codes + scales: one bulk copy
+    static_assert(kHalf == kDecodeFeatures * kChunkRowBytes, "one record per 64-row half");
 };
 
 template <int PREC, bool GATED>
@@ -90,10 +90,10 @@ template <int PREC>
 __device__ __forceinline__ void decode_row_block(const uint8_t *codes, float sc, int row, int s, int q, uint32_t *o) {
     using DL = DecodeLayout<PREC>;
     if (PREC == GTMOE_INT8) {
-        const uint32_t w = *reinterpret_cast<const uint32_t *>(codes + row * DL::kCodeBytes + 16 * s + 4 * q);
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(codes + half_code_off(row, 16 * s + 4 * q));
         int8_decode4_f16(w, pack_f16(sc, sc), o);
     } else {
-        const uint32_t w = *reinterpret_cast<const uint16_t *>(codes + row * DL::kCodeBytes + 8 * s + 2 * q);
+        const uint32_t w = *reinterpret_cast<const uint16_t *>(codes + half_code_off(row, 8 * s + 2 * q));
         const Fp4Tables t = fp4_tables_f16(sc);
         uint32_t v[4];
         fp4_decode8(w, t, v);
@@ -127,7 +127,6 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     const int blocks = n_out / kDecodeFeatures;
     const int which = GATED ? 0 : 2;
     const int xpitch = decode_x_pitch(K);
-    const int64_t chunk_bytes = (int64_t)128 * DL::kChunkRowBytes;
     const __nv_bfloat16 *xin = (const __nv_bfloat16 *)(GATED ? a.xp : a.hp);
     __nv_bfloat16 *out = (__nv_bfloat16 *)(GATED ? a.hp : a.yp);
     const int64_t units = __ldg(a.tile_prefix + a.n_groups) * blocks;
@@ -166,8 +165,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
         if (warp == kComputeWarps) {
             // ---- producer
             const int nt = fb >> 1, half = fb & 1;
-            const uint8_t *w0 = L.tiled[which] + (int64_t)nt * KB * chunk_bytes + half * DL::kHalf;
-            const uint8_t *w1 = GATED ? L.tiled[1] + (int64_t)nt * KB * chunk_bytes + half * DL::kHalf : nullptr;
+            // the 64-row block (2 nt + half) of each layer, its k-block records consecutive
+            const uint8_t *w0 = L.tiled[which] + (int64_t)(2 * nt + half) * KB * DL::kHalf;
+            const uint8_t *w1 = GATED ? L.tiled[1] + (int64_t)(2 * nt + half) * KB * DL::kHalf : nullptr;
             const uint8_t *xrow0 = (const uint8_t *)(xin + ((GATED ? grp.x_row0 : grp.h_row0) + r0) * (int64_t)K);
             if (nu > 0 && !*abort_p) mbar_wait(&xempty, (nu - 1) & 1, abort_p, a.err, 13);
             if (lane == 0) mbar_arrive_expect_tx(&xfull, (uint32_t)m * K * 2);
@@ -181,8 +181,8 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
                 if (lane == 0) {
                     uint8_t *st = ring + slot * ST::kBytes;
                     mbar_arrive_expect_tx(&full[slot], ST::kBytes);
-                    bulk_copy(st, w0 + kb * chunk_bytes, DL::kHalf, &full[slot]);
-                    if (GATED) bulk_copy(st + DL::kHalf, w1 + kb * chunk_bytes, DL::kHalf, &full[slot]);
+                    bulk_copy(st, w0 + (int64_t)kb * DL::kHalf, DL::kHalf, &full[slot]);
+                    if (GATED) bulk_copy(st + DL::kHalf, w1 + (int64_t)kb * DL::kHalf, DL::kHalf, &full[slot]);
                 }
                 __syncwarp();
             }
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             float4 sc[2];
 #pragma unroll
             for (int l = 0; l < ST::kLayers; l++)
-                sc[l] = *reinterpret_cast<const float4 *>(st + l * DL::kHalf + DL::kCodes + row * 16);
+                sc[l] = *reinterpret_cast<const float4 *>(st + l * DL::kHalf + half_scale_off(row, DL::kCodeBytes));
 #pragma unroll
             for (int s = 0; s < 4; s++) {
                 const uint8_t *xa = xrow + kb * 128 + 32 * s;

@@ -14,13 +14,24 @@ namespace gtmoe {
 // [64][code_bytes] then block scales [64][4 floats], so that a half is one
 // contiguous bulk copy.  Int8 codes are stored biased, as the bytes q + 128
 // (the decoders place them straight into a float or half mantissa).
-constexpr int kChunkHalfRows = 64;
-__host__ __device__ __forceinline__ int chunk_code_off(int r, int code_bytes) {
-    return (r / kChunkHalfRows) * kChunkHalfRows * (code_bytes + 16) + (r % kChunkHalfRows) * code_bytes;
+// Tile-chunk layout of an Int8/FP4 layer for the tensor-core and decode
+// kernels (built at set time by tc.cu's relayout): the rows in blocks of 64
+// ("halves"), each half's k-blocks (64 inputs) consecutive, so that the
+// records of one half over consecutive k-blocks are one contiguous copy.  A
+// (half, k-block) record holds the codes column-group major -- 16-byte group
+// j of all 64 rows, then group j+1 -- followed by the scales [64 rows][4].
+// A lane that reads "its" row's group then touches consecutive 16-byte words
+// across the warp (no bank conflicts).  Int8 codes are stored biased (q + 128)
+// for the decoders' float/half magic-number conversions.
+constexpr int kHalfRows = 64;
+__host__ __device__ __forceinline__ constexpr int half_bytes(int code_bytes) { return kHalfRows * (code_bytes + 16); }
+// byte `byte` of row r's codes within a record
+__host__ __device__ __forceinline__ constexpr int half_code_off(int r, int byte) {
+    return (byte >> 4) * (kHalfRows * 16) + r * 16 + (byte & 15);
 }
-__host__ __device__ __forceinline__ int chunk_scale_off(int r, int code_bytes) {
-    return (r / kChunkHalfRows) * kChunkHalfRows * (code_bytes + 16) + kChunkHalfRows * code_bytes +
-           (r % kChunkHalfRows) * 16;
+// row r's four block scales (float4) within a record
+__host__ __device__ __forceinline__ constexpr int half_scale_off(int r, int code_bytes) {
+    return kHalfRows * code_bytes + r * 16;
 }
 
 // prmt with the sign-replicating selector mode (msb of a selector nibble set)

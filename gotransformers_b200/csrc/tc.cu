@@ -5,36 +5,46 @@
 //   kernel 1 (GATED):  H = act_g(X Wg^T + bg) * act_u(X Wu^T + bu)  -> bf16
 //   kernel 2 (DOWN):   Y = H Wd^T + bd                               -> bf16
 // X / H rows of every expert are contiguous (the dispatch's expert-sorted
-// buffer).  A tile is 256 rows x 128 columns computed by two M=128 UMMAs that
-// share one weight tile, so every dequantised weight feeds 256 rows of MMA
-// work.  For kernel 1 the 128 columns are 64 gate features and the same 64
-// up features, so each epilogue thread holds both operands of its SwiGLU
-// products in registers.
+// buffer).
 //
-// The Int8/FP4 weights stay compressed in HBM: the bytes of the
+// The products are computed transposed, D = W X^T.  The dequantised weights
+// are the MMA's A operand and go from the dequantisation warps' registers
+// straight into tensor memory (tcgen05.st); the token rows are the B operand,
+// staged in shared memory by TMA.  The bf16 weight tile therefore never
+// passes through shared memory: writing it there and reading it back for the
+// MMA was the shared-memory traffic that bounded the previous form of this
+// kernel.  The Int8/FP4 weights stay compressed in HBM: the bytes of the
 // lowprecision.Rows snapshot (codes, one float32 scale per 16 values of a
-// row; lowprecision/rows.go:38-79) are only permuted at set time into chunks
-// of (row tile, 64-wide k-block), codes then scales, so that one bulk async
-// copy moves the raw weights of one pipeline stage into shared memory.
-// Dequantisation warps turn them into bf16(code * scale) (Rows.Row semantics,
-// rows.go:87-119) straight in the UMMA canonical K-major SWIZZLE_128B layout;
-// activations arrive by TMA in the same layout.  One elected thread issues
-// tcgen05.mma kind::f16 (bf16 x bf16 -> f32 in TMEM); four epilogue warps read
-// TMEM with tcgen05.ld.
+// row; lowprecision/rows.go:38-79) are only permuted at set time into
+// 64-row records (dequant.cuh), and the dequantisation is Rows.Row's
+// bf16(code * scale) (rows.go:87-119).
+//
+// A CTA pair (cluster of 2, tcgen05.mma.cta_group::2, M = 256, N = 192)
+// computes 256 weight rows x 192 tokens: each CTA holds 128 weight rows in
+// its TMEM lanes and 96 of the tokens in shared memory, and accumulates its
+// 128 rows x 192 tokens in its own TMEM.  In kernel 1 a CTA's 128 weight rows
+// are 64 gate features and the same 64 up features, so one pair tile yields
+// 128 hidden features; in kernel 2 they are 128 consecutive output features.
+// One pipeline step covers 128 inputs: 8 MMAs between one pair of barrier
+// waits and one commit, which keeps the single issuing thread ahead of the
+// tensor pipe.
 //
 // Persistent kernel, one CTA per SM, warp roles:
-//   warp 0      TMA / bulk-copy producer (activation tile + raw weight chunks)
+//   warp 0      TMA / bulk-copy producer (token tiles + raw weight records)
 //   warp 1      TMEM allocator and MMA issuer
-//   warps 2-5   epilogue (TMEM -> bias, SwiGLU -> bf16 -> global)
-//   warps 6-13  dequantisation of the weight tile
-// A ring of shared-memory stages (activations 32 KB, bf16 weights 16 KB, raw
-// weights 6 KB FP4 / 10 KB Int8 each) and two TMEM accumulators of 256
-// columns (the epilogue of one tile overlaps the main loop of the next).
+//   warps 2-5   epilogue (TMEM -> bias, SwiGLU -> bf16 -> shared-memory
+//               transpose -> coalesced global rows)
+//   warps 6-13  dequantisation, two groups of four (one per TMEM lane
+//               quadrant) taking alternate steps
+//   warps 14-17 expert parallel only (kernel 2): finished rows to their
+//               tokens' ranks
+// TMEM: two accumulators of 192 columns (the epilogue of one tile overlaps
+// the main loop of the next) and a two-stage ring of 64-column A stages.
 //
 // Every mbarrier wait is bounded (kWaitLimitNs of %globaltimer).  On expiry
 // the kernel records an error code in *err, raises a CTA-wide abort flag so
-// every role leaves its loop, lets in-flight copies land, frees TMEM and
-// returns; the host reports GTMOE_ETIMEOUT.
+// every role leaves its loop, lets in-flight copies and MMAs finish, frees
+// TMEM and returns; the host reports GTMOE_ETIMEOUT.
 #include <stdlib.h>
 #include <string.h>
 
@@ -47,38 +57,61 @@ namespace gtmoe {
 
 namespace {
 
-constexpr int kBK = 64;              // K elements per stage (128 bytes of bf16)
-constexpr int kCtaRows = 128;        // token rows per CTA (UMMA M=256 over the pair)
-constexpr int kTileM = 2 * kCtaRows; // rows per cluster tile
-constexpr int kTileN = 256;          // B rows (output columns) per cluster tile, 128 per CTA
-constexpr int kChunkRows = 128;      // weight rows per raw chunk = one CTA's half of B
-static_assert(kChunkRows == 2 * kChunkHalfRows, "a chunk is two halves");
-constexpr int kNumDequantWarps = 8;
-constexpr int kDequantThreads = kNumDequantWarps * 32;
-constexpr int kNumThreads = (6 + kNumDequantWarps) * 32;  // 448
-// Expert parallel: two more warps in the down kernel copy finished output
-// rows to their tokens' ranks (coalesced 512-byte row segments).
+constexpr int kBK = 64;                 // inputs per k-block (one raw record)
+constexpr int kStepK = 128;             // inputs per pipeline step
+constexpr int kStepKB = kStepK / kBK;   // k-blocks per step
+constexpr int kCtaTok = 96;             // token rows per CTA (its half of B)
+constexpr int kTileTok = 2 * kCtaTok;   // tokens per pair tile (UMMA N)
+constexpr int kCtaW = 2 * kHalfRows;    // weight rows per CTA (TMEM lanes; UMMA M = 256 over the pair)
+constexpr int kGatedFeat = 2 * kHalfRows;  // kernel 1: hidden features per pair tile
+constexpr int kDownFeat = 2 * kCtaW;       // kernel 2: output features per pair tile
+constexpr int kNumWriterWarps = 8;      // dequantisation: 2 groups x 4 lane quadrants
+constexpr int kEpiWarps = 4;
+constexpr int kNumThreads = (2 + kEpiWarps + kNumWriterWarps) * 32;  // 448
+// Expert parallel: four more warps in the down kernel copy finished output
+// rows to their tokens' ranks.
 constexpr int kReturnWarps = 4;
-constexpr int kMaxThreads = kNumThreads + kReturnWarps * 32;
+constexpr int kMaxThreads = kNumThreads + kReturnWarps * 32;  // 576
 constexpr int kTmemCols = 512;
-constexpr int kATileBytes = kCtaRows * kBK * 2;    // 16 KB per CTA
-constexpr int kBTileBytes = kChunkRows * kBK * 2;  // 16 KB per CTA
-constexpr int kItems = kChunkRows * 4 / kDequantThreads;  // (row, 16-value block) items per dequant thread
-constexpr int kPrefixCache = 2048;  // m-tile prefix entries cached in shared memory
-// instruction descriptor: D f32, A bf16, B bf16, both K-major, N=256, M=256 (2-SM)
+constexpr int kAccCols = kTileTok;          // f32 accumulator columns
+constexpr int kRingCol = 2 * kAccCols;      // first column of the A ring
+constexpr int kAStageCols = kStepK / 2;     // bf16 pairs per lane per step
+static_assert(kRingCol + 2 * kAStageCols <= kTmemCols, "tensor memory");
+constexpr int kBSubBytes = kCtaTok * 128;   // one k-block of this CTA's tokens (SWIZZLE_128B rows)
+constexpr int kBStageBytes = kStepKB * kBSubBytes;
+static_assert(kBSubBytes % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+constexpr int kEpiChunk = 32;               // tokens per epilogue round
+// Epilogue staging, f32 [32 tokens][pitch]: kernel 1 the gate and the up
+// values of the CTA's 64 features (pitch 68 each), kernel 2 its 128 output
+// features (pitch 132).  Pitches of 4 mod 32 words keep both the column
+// writes (lanes = features) and the row reads (lanes = tokens) free of bank
+// conflicts.
+constexpr int kGatePitch = 68;
+constexpr int kDownPitch = 132;
+constexpr int kEpiBytes = 2 * kEpiChunk * kGatePitch * 4;  // 17408
+static_assert(kEpiChunk * kDownPitch * 4 <= kEpiBytes, "epilogue staging");
+constexpr int kPrefixCache = 2048;          // m-tile prefix entries cached in shared memory
+// instruction descriptor: D f32, A bf16, B bf16, both K-major, N = 192, M = 256 (2-SM)
 constexpr uint32_t kIdesc =
-    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileN >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileTok >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+static_assert(kTileTok % 16 == 0 && kTileTok <= 256, "UMMA N for M = 256");
 
-// Raw chunk geometry: code bytes per row per k-block, stage bytes.
+// Raw record geometry and the shared-memory plan of one precision: a ring of
+// token tiles (released when the step's MMAs complete) and a separate ring of
+// raw weight records (released as soon as the dequantisation warps have
+// decoded them, so that weight loads run further ahead).
+constexpr int kBStages = 5;
 template <int PREC>
 struct Raw {
-    static constexpr int kCodeBytes = PREC == GTMOE_INT8 ? 64 : 32;
-    static constexpr int kRowBytes = kCodeBytes + 16;  // codes + 4 float scales
-    static constexpr int kStageBytes = kChunkRows * kRowBytes;
-    static constexpr int kStages = 5;
-    static constexpr int kSmemBytes =
-        kStages * (kATileBytes + kBTileBytes + kStageBytes) + 1024 + 256 + kPrefixCache * 4;
+    static constexpr int kCodeBytes = PREC == GTMOE_INT8 ? 64 : 32;  // per row and k-block
+    static constexpr int kHalfBytes = half_bytes(kCodeBytes);        // one (64-row, k-block) record
+    static constexpr int kStageBytes = 2 * kStepKB * kHalfBytes;     // two halves x the step's k-blocks
+    static constexpr int kStages = 4;
+    static constexpr int kBarBytes = 256;
+    static constexpr int kSmemBytes = 1024 + kBStages * kBStageBytes + kStages * kStageBytes + kEpiBytes +
+                                      kBarBytes + kPrefixCache * 4;
 };
+static_assert(Raw<GTMOE_INT8>::kSmemBytes <= 232448, "shared memory per CTA");
 
 struct TcKernelArgs {
     const Group *groups;
@@ -106,6 +139,22 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory"); }
+// Barrier of the epilogue warps that also ANDs their verdicts, so that all
+// of them take a tile (and its named barriers) or all of them stop.
+__device__ __forceinline__ bool epi_vote(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)ok), "n"(kEpiWarps * 32)
+        : "memory");
+    return r != 0;
 }
 
 // Bounded wait of the 2-SM kernel: on expiry it records `code`, raises the
@@ -165,68 +214,66 @@ struct UnitDecoder {
     }
 };
 
-// Dequantises one stage of this CTA's 128 B rows: item (r, b) = 16 values of
-// row r, k-block quarter b.  The raw stage is one chunk (two 64-row halves of
-// codes then scales, chunk_code_off / chunk_scale_off).
+// One weight row of one step (128 inputs = two k-block records of the row's
+// half) -> 64 bf16 pairs in K order: the A columns of this lane.
 template <int PREC>
-__device__ __forceinline__ void dequant_stage(const uint8_t *raw, uint8_t *btile, int tid) {
+__device__ __forceinline__ void dequant_row(const uint8_t *half_rec, int hr, uint32_t (&v)[64]) {
     using R = Raw<PREC>;
 #pragma unroll
-    for (int i = 0; i < kItems; i++) {
-        const int item = tid + i * kDequantThreads;
-        const int r = item >> 2;
-        const int b = item & 3;
-        const float s = *reinterpret_cast<const float *>(raw + chunk_scale_off(r, R::kCodeBytes) + b * 4);
-        uint32_t w[8];
+    for (int kb = 0; kb < kStepKB; kb++) {
+        const uint8_t *rec = half_rec + kb * R::kHalfBytes;
+        const float4 sc = *reinterpret_cast<const float4 *>(rec + half_scale_off(hr, R::kCodeBytes));
+        const float s4[4] = {sc.x, sc.y, sc.z, sc.w};
+        uint32_t *o = v + kb * 32;
         if (PREC == GTMOE_INT8) {
-            const uint4 c = *reinterpret_cast<const uint4 *>(raw + chunk_code_off(r, R::kCodeBytes) + b * 16);
-            int8_decode4(c.x, s, w);
-            int8_decode4(c.y, s, w + 2);
-            int8_decode4(c.z, s, w + 4);
-            int8_decode4(c.w, s, w + 6);
+#pragma unroll
+            for (int b = 0; b < 4; b++) {  // 16-byte group b = block b (16 codes)
+                const uint4 c = *reinterpret_cast<const uint4 *>(rec + half_code_off(hr, 16 * b));
+                int8_decode4(c.x, s4[b], o + 8 * b);
+                int8_decode4(c.y, s4[b], o + 8 * b + 2);
+                int8_decode4(c.z, s4[b], o + 8 * b + 4);
+                int8_decode4(c.w, s4[b], o + 8 * b + 6);
+            }
         } else {
-            const uint2 c = *reinterpret_cast<const uint2 *>(raw + chunk_code_off(r, R::kCodeBytes) + b * 8);
-            const Fp4Tables t = fp4_tables(s);
-            fp4_decode8(c.x, t, w);
-            fp4_decode8(c.y, t, w + 4);
+#pragma unroll
+            for (int gi = 0; gi < 2; gi++) {  // 16-byte group gi = blocks 2gi, 2gi+1
+                const uint4 c = *reinterpret_cast<const uint4 *>(rec + half_code_off(hr, 16 * gi));
+                const Fp4Tables t0 = fp4_tables(s4[2 * gi]);
+                fp4_decode8(c.x, t0, o + 16 * gi);
+                fp4_decode8(c.y, t0, o + 16 * gi + 4);
+                const Fp4Tables t1 = fp4_tables(s4[2 * gi + 1]);
+                fp4_decode8(c.z, t1, o + 16 * gi + 8);
+                fp4_decode8(c.w, t1, o + 16 * gi + 12);
+            }
         }
-        // 16 values = logical 16-byte chunks 2b, 2b+1 of row r, placed at
-        // chunk ^ (r & 7) (SWIZZLE_128B)
-        uint8_t *row = btile + r * 128;
-        const int c0 = (2 * b) ^ (r & 7), c1 = (2 * b + 1) ^ (r & 7);
-        *reinterpret_cast<uint4 *>(row + c0 * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4 *>(row + c1 * 16) = make_uint4(w[4], w[5], w[6], w[7]);
     }
 }
 
-// Grouped SwiGLU GEMM on a CTA pair (cluster of 2, tcgen05.mma.cta_group::2):
-// the pair computes a 256-row x 256-column tile, CTA rank r holding A rows
-// r*128..r*128+127 and B rows r*128..r*128+127 in its own shared memory and
-// D rows r*128.. in its own TMEM.  For kernel 1 the pair's B rows are 128
-// gate features (rank 0) and the same 128 up features (rank 1), so D columns
-// 0..127 / 128..255 of each TMEM lane are the gate / up values of one
-// (token, feature).  Rank 0 (the leader) issues the MMAs.
+// Grouped SwiGLU GEMM on a CTA pair; see the file comment for the roles.
+// Rank 0 (the leader) issues the MMAs.
 template <int PREC, bool GATED>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     grouped_tc_kernel(const __grid_constant__ CUtensorMap amap, const TcKernelArgs a) {
     using R = Raw<PREC>;
-    constexpr int S = R::kStages;
+    constexpr int SB = kBStages, SR = R::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *a_tiles = smem;
-    uint8_t *b_tiles = smem + S * kATileBytes;
-    uint8_t *raw_tiles = b_tiles + S * kBTileBytes;
-    uint64_t *bars = (uint64_t *)(raw_tiles + S * R::kStageBytes);
-    uint64_t *full_a = bars;                  // [S] both activation tiles landed (leader)
-    uint64_t *full_raw = bars + S;            // [S] this CTA's raw weights landed
-    uint64_t *full_b = bars + 2 * S;          // [S] both bf16 weight halves written (leader)
-    uint64_t *empty = bars + 3 * S;           // [S] MMAs of the stage done (both CTAs)
-    uint64_t *tmem_full = bars + 4 * S;       // [2] accumulator ready (both CTAs)
-    uint64_t *tmem_empty = bars + 4 * S + 2;  // [2] both epilogues done (leader)
-    uint32_t *tmem_slot = (uint32_t *)(bars + 4 * S + 4);
+    uint8_t *b_tiles = smem;                               // [SB] this CTA's tokens, 2 SW128 k-blocks
+    uint8_t *raw_tiles = b_tiles + SB * kBStageBytes;      // [SR] this CTA's raw weight records
+    uint8_t *epi = raw_tiles + SR * R::kStageBytes;        // epilogue staging
+    uint64_t *bars = (uint64_t *)(epi + kEpiBytes);
+    uint64_t *full_b = bars;                          // [SB] both token tiles landed (leader)
+    uint64_t *b_empty = bars + SB;                    // [SB] MMAs of the step done (both CTAs)
+    uint64_t *full_raw = bars + 2 * SB;               // [SR] this CTA's raw weights landed
+    uint64_t *raw_empty = bars + 2 * SB + SR;         // [SR] raw records decoded (this CTA)
+    uint64_t *a_full = bars + 2 * SB + 2 * SR;        // [2] both CTAs' A stage written (leader)
+    uint64_t *tmem_full = a_full + 2;                 // [2] accumulator ready (both CTAs)
+    uint64_t *tmem_empty = a_full + 4;                // [2] both epilogues done (leader)
+    uint32_t *tmem_slot = (uint32_t *)(a_full + 6);
     volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
     volatile int *tiles_out = (volatile int *)(tmem_slot + 2);  // epilogue warps' finished tiles (x4)
-    int *prefix_s = (int *)(smem + S * (kATileBytes + kBTileBytes + R::kStageBytes) + 256);
+    int *prefix_s = (int *)((uint8_t *)bars + R::kBarBytes);
+    static_assert((2 * SB + 2 * SR + 6) * 8 + 12 <= R::kBarBytes, "barrier area");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -234,22 +281,25 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const bool leader = rank == 0;
     const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
     const uint32_t peer_abort = mapa_shared(smem_u32((const void *)abort_flag), rank ^ 1u);
-    // kernel 1: 128 gate + the same 128 up features per tile; kernel 2: 256 features
-    const int n_tiles = GATED ? a.n_out / kChunkRows : a.n_out / kTileN;
+    const int n_tiles = GATED ? a.n_out / kGatedFeat : a.n_out / kDownFeat;
     const int64_t total = __ldg(a.tile_prefix + a.n_groups) * n_tiles;
     const int KB = a.K / kBK;
+    const int KS = a.K / kStepK;
     for (int i = threadIdx.x; i <= a.n_groups; i += blockDim.x) prefix_s[i] = (int)__ldg(a.tile_prefix + i);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; s++) {
-            mbar_init(&full_a[s], 1);
+        for (int s = 0; s < SB; s++) {
+            mbar_init(&full_b[s], 1);
+            mbar_init(&b_empty[s], 1);
+        }
+        for (int s = 0; s < SR; s++) {
             mbar_init(&full_raw[s], 1);
-            mbar_init(&full_b[s], 2 * kNumDequantWarps);
-            mbar_init(&empty[s], 1);
+            mbar_init(&raw_empty[s], 4);
         }
         for (int b = 0; b < 2; b++) {
+            mbar_init(&a_full[b], 2 * 4);
             mbar_init(&tmem_full[b], 1);
-            mbar_init(&tmem_empty[b], 2 * 4);
+            mbar_init(&tmem_empty[b], 2 * kEpiWarps);
         }
         *abort_flag = 0;
         *tiles_out = 0;
@@ -267,36 +317,47 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- producer: activation tile (TMA, counted on the leader) + raw weight chunk (bulk)
+        // ---------------- producer: token tiles (TMA, counted on the leader) + raw weight records (bulk)
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&amap) : "memory");
-            int stage = 0;
-            uint32_t phase = 0;
-            constexpr uint32_t chunk_bytes = R::kStageBytes;
+            int64_t j = 0;  // steps issued by this CTA
             UnitDecoder dec{prefix_s, a.groups, a.n_groups, n_tiles};
-            const uint8_t *src = nullptr;
+            const uint8_t *src0 = nullptr, *src1 = nullptr;
             for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
                 Unit w;
                 if (dec.advance(u, w)) {
                     const ExpertLayers &L = a.experts[dec.grp.expert];
-                    src = GATED ? L.tiled[rank] : L.tiled[2];
+                    src0 = GATED ? L.tiled[0] : L.tiled[2];
+                    src1 = GATED ? L.tiled[1] : L.tiled[2];
                 }
                 const Group &grp = dec.grp;
-                const int row0 = (int)((GATED ? grp.x_row0 : grp.h_row0) + w.mt * kTileM + rank * kCtaRows);
-                // chunk (t, k-block) of a layer sits at (t * KB + kb) * chunk_bytes
-                const int64_t chunk = GATED ? w.nt : 2 * w.nt + rank;
-                for (int kb = 0; kb < KB; kb++) {
-                    if (!pair_wait<false>(&empty[stage], phase ^ 1, abort_flag, peer_abort, a.err, 1)) break;
-                    if (leader) mbar_arrive_expect_tx(&full_a[stage], 2 * kATileBytes);
-                    tma_load_2d_pair(a_tiles + stage * kATileBytes, &amap, kb * kBK, row0,
-                                     mapa_shared(smem_u32(&full_a[stage]), 0));
-                    mbar_arrive_expect_tx(&full_raw[stage], chunk_bytes);
-                    bulk_load(raw_tiles + stage * R::kStageBytes, src + ((size_t)chunk * KB + kb) * chunk_bytes,
-                              chunk_bytes, &full_raw[stage]);
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
+                const int row0 = (int)((GATED ? grp.x_row0 : grp.h_row0) + w.mt * kTileTok + rank * kCtaTok);
+                // this CTA's two 64-row weight blocks: kernel 1 the gate and the up
+                // block of its 64 features, kernel 2 two consecutive blocks
+                const int64_t hb0 = GATED ? 2 * w.nt + rank : 4 * w.nt + 2 * rank;
+                const int64_t hb1 = GATED ? hb0 : hb0 + 1;
+                const uint8_t *p0 = src0 + hb0 * KB * R::kHalfBytes;
+                const uint8_t *p1 = src1 + hb1 * KB * R::kHalfBytes;
+                for (int s = 0; s < KS; s++, j++) {
+                    // raw weights first: the dequantisation needs them two steps before the MMAs
+                    const int sr = (int)(j % SR), sb = (int)(j % SB);
+                    if (!pair_wait<false>(&raw_empty[sr], ((uint32_t)(j / SR) & 1) ^ 1, abort_flag, peer_abort, a.err,
+                                          1))
+                        break;
+                    uint8_t *rs = raw_tiles + sr * R::kStageBytes;
+                    const int64_t off = (int64_t)s * kStepKB * R::kHalfBytes;
+                    mbar_arrive_expect_tx(&full_raw[sr], R::kStageBytes);
+                    bulk_load(rs, p0 + off, kStepKB * R::kHalfBytes, &full_raw[sr]);
+                    bulk_load(rs + kStepKB * R::kHalfBytes, p1 + off, kStepKB * R::kHalfBytes, &full_raw[sr]);
+                    if (!pair_wait<false>(&b_empty[sb], ((uint32_t)(j / SB) & 1) ^ 1, abort_flag, peer_abort, a.err,
+                                          1))
+                        break;
+                    if (leader) mbar_arrive_expect_tx(&full_b[sb], 2 * kBStageBytes);
+                    uint8_t *bt = b_tiles + sb * kBStageBytes;
+#pragma unroll
+                    for (int i = 0; i < kStepKB; i++)
+                        tma_load_2d_pair(bt + i * kBSubBytes, &amap, (s * kStepKB + i) * kBK, row0,
+                                         mapa_shared(smem_u32(&full_b[sb]), 0));
                 }
             }
             if (*abort_flag) {
@@ -309,33 +370,30 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader CTA)
         if (leader && lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
+            uint32_t j = 0;  // steps issued (A ring stage j & 1, use j >> 1; token stage j % SB)
             int acc = 0;
             uint32_t acc_phase = 0;
             for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
                 if (!pair_wait<false>(&tmem_empty[acc], acc_phase ^ 1, abort_flag, peer_abort, a.err, 2)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kTileN);
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kAccCols);
                 bool ok = true;
-                for (int kb = 0; kb < KB; kb++) {
-                    if (!pair_wait<false>(&full_a[stage], phase, abort_flag, peer_abort, a.err, 3) ||
-                        !pair_wait<false>(&full_b[stage], phase, abort_flag, peer_abort, a.err, 4)) {
+                for (int s = 0; s < KS; s++, j++) {
+                    const int sb = (int)(j % SB);
+                    if (!pair_wait<false>(&full_b[sb], (j / SB) & 1, abort_flag, peer_abort, a.err, 3) ||
+                        !pair_wait<false>(&a_full[j & 1], (j >> 1) & 1, abort_flag, peer_abort, a.err, 4)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t adesc = sw128_desc(smem_u32(a_tiles + stage * kATileBytes));
-                    const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + stage * kBTileBytes));
+                    const uint32_t b_addr = smem_u32(b_tiles + sb * kBStageBytes);
+                    const uint32_t a_tmem = tmem_base + (uint32_t)(kRingCol + (j & 1) * kAStageCols);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; k++)
-                        umma2_bf16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
-                                   (kb | k) != 0);
-                    umma2_commit_mc(&empty[stage], 0x3);
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1;
+                    for (int k = 0; k < kStepK / 16; k++) {
+                        const uint64_t bdesc = sw128_desc(b_addr + (k >> 2) * kBSubBytes) + (uint64_t)(2 * (k & 3));
+                        umma2_ts_bf16(d_tmem, a_tmem + 8 * k, bdesc, kIdesc, (s | k) != 0);
                     }
+                    umma2_commit_mc(&b_empty[sb], 0x3);
                 }
                 if (!ok) break;
                 umma2_commit_mc(&tmem_full[acc], 0x3);
@@ -344,16 +402,30 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     acc_phase ^= 1;
                 }
             }
+            if (*abort_flag) {
+                // let MMAs already issued finish before TMEM is freed
+                const uint64_t t0 = global_timer_ns();
+                while (global_timer_ns() - t0 < 1000000ull) {
+                }
+            }
         }
-    } else if (warp < 6) {
-        // ---------------- epilogue: TMEM -> registers -> global (both CTAs)
-        const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+    } else if (warp < 2 + kEpiWarps) {
+        // ---------------- epilogue: TMEM -> registers -> shared memory -> global rows (both CTAs)
+        // Per 32-token chunk every warp first parks its lanes' bias-added
+        // values in shared memory (lanes = features); after a barrier the
+        // four warps take 32 tokens each (lanes = tokens), do the activation
+        // work evenly and write 16-byte pieces of the output rows.
+        const int quad = warp & 3;         // TMEM lanes 32*quad .. 32*quad+31
+        const int ew = warp - 2;           // 0..3: this warp's feature slice in the second phase
         const uint32_t tmem_empty_leader0 = mapa_shared(smem_u32(&tmem_empty[0]), 0);
+        float *stage_f = reinterpret_cast<float *>(epi);
         int acc = 0;
         uint32_t acc_phase = 0;
         UnitDecoder dec{prefix_s, a.groups, a.n_groups, n_tiles};
         const float *b0 = nullptr, *b1 = nullptr;
-        for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
+        // (no abort test in the loop condition: the vote below is the one place
+        // where the four warps decide together to stop)
+        for (int64_t u = cluster; u < total; u += n_clusters) {
             Unit w;
             if (dec.advance(u, w)) {
                 const ExpertLayers &L = a.experts[dec.grp.expert];
@@ -361,87 +433,110 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 b1 = L.b32[1];
             }
             const Group &grp = dec.grp;
-            if (!pair_wait<false>(&tmem_full[acc], acc_phase, abort_flag, peer_abort, a.err, 5)) break;
+            const bool ready = pair_wait<false>(&tmem_full[acc], acc_phase, abort_flag, peer_abort, a.err, 5);
+            if (!epi_vote(ready)) break;
             tc_fence_after();
-            const int row_in_tile = (int)rank * kCtaRows + quad * 32 + lane;
-            const bool valid = row_in_tile < grp.m - w.mt * kTileM;
-            const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * kTileN);
-            __nv_bfloat16 *dst = a.out + (grp.h_row0 + w.mt * kTileM + row_in_tile) * (int64_t)a.n_out;
+            const int64_t left = grp.m - w.mt * kTileTok;
+            const int n_valid = left < kTileTok ? (int)left : kTileTok;
+            const int n_chunks = (n_valid + kEpiChunk - 1) / kEpiChunk;
+            const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * kAccCols);
+            const int64_t row0 = grp.h_row0 + w.mt * kTileTok;
             if (GATED) {
-                const int f0 = w.nt * kChunkRows;
-                const float *bg = b0;
-                const float *bu = b1;
+                // TMEM lanes 0-63 gate, 64-127 up of the CTA's 64 features
+                const int f0 = w.nt * kGatedFeat + (int)rank * kHalfRows;
+                const int fl = (quad & 1) * 32 + lane;
+                const float *bp = quad < 2 ? b0 : b1;
+                const float bias = bp ? __ldg(bp + f0 + fl) : 0.f;
+                float *col = stage_f + (quad < 2 ? 0 : kEpiChunk * kGatePitch) + fl;
+                const float *gate_row = stage_f + lane * kGatePitch + ew * 16;
+                const float *up_row = gate_row + kEpiChunk * kGatePitch;
+                __nv_bfloat16 *dst = a.out + (row0 + lane) * (int64_t)a.n_out + f0 + ew * 16;
 #pragma unroll 1
-                for (int c = 0; c < kChunkRows; c += 16) {
-                    uint32_t g[16], up[16];
-                    tmem_ld16(t_row + c, g);
-                    tmem_ld16(t_row + kChunkRows + c, up);
+                for (int c = 0; c < n_chunks; c++) {
+                    uint32_t v[32];
+                    tmem_ld16(t_row + c * kEpiChunk, *reinterpret_cast<uint32_t(*)[16]>(v));
+                    tmem_ld16(t_row + c * kEpiChunk + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
                     tmem_ld_wait();
-                    uint32_t o[8];
 #pragma unroll
-                    for (int j = 0; j < 16; j += 2) {
-                        float hv[2];
+                    for (int i = 0; i < kEpiChunk; i++) col[i * kGatePitch] = __uint_as_float(v[i]) + bias;
+                    epi_bar();
+                    if (c * kEpiChunk + lane < n_valid) {
+                        uint32_t o[8];
 #pragma unroll
-                        for (int q = 0; q < 2; q++) {
-                            float gv = __uint_as_float(g[j + q]) + (bg ? __ldg(bg + f0 + c + j + q) : 0.f);
-                            float uv = __uint_as_float(up[j + q]) + (bu ? __ldg(bu + f0 + c + j + q) : 0.f);
-                            hv[q] = gate_act<float>(gv, a.clamped, a.clamp_limit) *
-                                    up_act<float>(uv, a.clamped, a.clamp_limit);
+                        for (int q = 0; q < 4; q++) {
+                            const float4 gv = *reinterpret_cast<const float4 *>(gate_row + 4 * q);
+                            const float4 uv = *reinterpret_cast<const float4 *>(up_row + 4 * q);
+                            const float h0 = gate_act<float>(gv.x, a.clamped, a.clamp_limit) *
+                                             up_act<float>(uv.x, a.clamped, a.clamp_limit);
+                            const float h1 = gate_act<float>(gv.y, a.clamped, a.clamp_limit) *
+                                             up_act<float>(uv.y, a.clamped, a.clamp_limit);
+                            const float h2 = gate_act<float>(gv.z, a.clamped, a.clamp_limit) *
+                                             up_act<float>(uv.z, a.clamped, a.clamp_limit);
+                            const float h3 = gate_act<float>(gv.w, a.clamped, a.clamp_limit) *
+                                             up_act<float>(uv.w, a.clamped, a.clamp_limit);
+                            o[2 * q] = pack_bf16(h0, h1);
+                            o[2 * q + 1] = pack_bf16(h2, h3);
                         }
-                        o[j / 2] = pack_bf16(hv[0], hv[1]);
-                    }
-                    if (valid) {
-                        uint4 *p = reinterpret_cast<uint4 *>(dst + f0 + c);
+                        uint4 *p = reinterpret_cast<uint4 *>(dst + (int64_t)(c * kEpiChunk) * a.n_out);
                         p[0] = make_uint4(o[0], o[1], o[2], o[3]);
                         p[1] = make_uint4(o[4], o[5], o[6], o[7]);
                     }
+                    epi_bar();
                 }
             } else {
-                const int f0 = w.nt * kTileN;
-                const float *bd = b0;
+                const int f0 = w.nt * kDownFeat + (int)rank * kCtaW;
+                const int fl = quad * 32 + lane;
+                const float bias = b0 ? __ldg(b0 + f0 + fl) : 0.f;
+                float *col = stage_f + fl;
+                const float *row = stage_f + lane * kDownPitch + ew * 32;
+                __nv_bfloat16 *dst = a.out + (row0 + lane) * (int64_t)a.n_out + f0 + ew * 32;
 #pragma unroll 1
-                for (int c = 0; c < kTileN; c += 16) {
-                    uint32_t y[16];
-                    tmem_ld16(t_row + c, y);
+                for (int c = 0; c < n_chunks; c++) {
+                    uint32_t v[32];
+                    tmem_ld16(t_row + c * kEpiChunk, *reinterpret_cast<uint32_t(*)[16]>(v));
+                    tmem_ld16(t_row + c * kEpiChunk + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
                     tmem_ld_wait();
-                    uint32_t o[8];
 #pragma unroll
-                    for (int j = 0; j < 16; j += 2) {
-                        float y0 = __uint_as_float(y[j]) + (bd ? __ldg(bd + f0 + c + j) : 0.f);
-                        float y1 = __uint_as_float(y[j + 1]) + (bd ? __ldg(bd + f0 + c + j + 1) : 0.f);
-                        o[j / 2] = pack_bf16(y0, y1);
+                    for (int i = 0; i < kEpiChunk; i++) col[i * kDownPitch] = __uint_as_float(v[i]) + bias;
+                    epi_bar();
+                    if (c * kEpiChunk + lane < n_valid) {
+                        uint4 *p = reinterpret_cast<uint4 *>(dst + (int64_t)(c * kEpiChunk) * a.n_out);
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            const float4 y0 = *reinterpret_cast<const float4 *>(row + 8 * q);
+                            const float4 y1 = *reinterpret_cast<const float4 *>(row + 8 * q + 4);
+                            p[q] = make_uint4(pack_bf16(y0.x, y0.y), pack_bf16(y0.z, y0.w), pack_bf16(y1.x, y1.y),
+                                              pack_bf16(y1.z, y1.w));
+                        }
                     }
-                    if (valid) {
-                        uint4 *p = reinterpret_cast<uint4 *>(dst + f0 + c);
-                        p[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                        p[1] = make_uint4(o[4], o[5], o[6], o[7]);
-                    }
+                    epi_bar();
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(tmem_empty_leader0 + (uint32_t)(acc * sizeof(uint64_t)));
-            if (!GATED && a.ret_ranks > 0 && lane == 0) {
+            if (!GATED && a.ret_ranks > 0) {
                 // the tile's rows are in global memory: hand them to the return warps
                 __threadfence_block();
-                atomicAdd((int *)tiles_out, 1);
+                __syncwarp();
+                if (lane == 0) atomicAdd((int *)tiles_out, 1);
             }
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
             }
         }
-    } else if (warp >= 6 + kNumDequantWarps) {
+    } else if (warp >= 2 + kEpiWarps + kNumWriterWarps) {
         // ---------------- expert parallel (down kernel): finished output rows
         // of routed experts to their tokens' ranks, one tile behind the epilogue
-        const int rw = warp - (6 + kNumDequantWarps);
+        const int rw = warp - (2 + kEpiWarps + kNumWriterWarps);
         UnitDecoder dec{prefix_s, a.groups, a.n_groups, n_tiles};
         int done = 0;
         for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
             Unit w;
             dec.advance(u, w);
             const Group &grp = dec.grp;
-            done += 4;
+            done += kEpiWarps;
             if (*tiles_out < done) {
                 const uint64_t t0 = global_timer_ns();
                 bool ok = true;
@@ -461,51 +556,71 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 if (!ok) break;
             }
             __threadfence_block();
-            const int f0 = w.nt * kTileN;  // this tile's 256 output features: 512 bytes per row
-            const int64_t row_base = grp.h_row0 + w.mt * kTileM + (int64_t)rank * kCtaRows;
-            const int64_t left = grp.m - w.mt * kTileM - (int64_t)rank * kCtaRows;
-            const int n_valid = left < kCtaRows ? (int)left : kCtaRows;
-            const int r0 = rw * (kCtaRows / kReturnWarps);
-            const int r1 = min(n_valid, r0 + kCtaRows / kReturnWarps);
+            // this CTA's 128 output features of the tile: 256 bytes per token row
+            const int f0 = w.nt * kDownFeat + (int)rank * kCtaW;
+            const int64_t row_base = grp.h_row0 + w.mt * kTileTok;
+            const int64_t left = grp.m - w.mt * kTileTok;
+            const int n_valid = left < kTileTok ? (int)left : kTileTok;
+            const int per = kTileTok / kReturnWarps;
+            const int r0 = rw * per;
+            const int r1 = min(n_valid, r0 + per);
+            const int sg = lane & 15;
             for (int r = r0; r < r1; r += 8) {
-                uint4 v[8];
-                uint4 *dst[8];
+                uint4 v[4];
+                uint4 *dst[4];
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const int64_t out_row = row_base + r + j;
-                    dst[j] = nullptr;
-                    if (r + j < r1 && out_row >= a.ret_row0) {
+                for (int q = 0; q < 4; q++) {
+                    const int rr = r + 2 * q + (lane >> 4);
+                    const int64_t out_row = row_base + rr;
+                    dst[q] = nullptr;
+                    if (rr < r1 && out_row >= a.ret_row0) {
                         const int64_t route = __ldg(a.ret_route + (out_row - a.ret_row0));
-                        dst[j] = reinterpret_cast<uint4 *>((__nv_bfloat16 *)a.ret_peers[route >> 48] +
+                        dst[q] = reinterpret_cast<uint4 *>((__nv_bfloat16 *)a.ret_peers[route >> 48] +
                                                            (route & 0xFFFFFFFFFFFFll) * (int64_t)a.n_out + f0) +
-                                 lane;
-                        v[j] = __ldcg(reinterpret_cast<const uint4 *>(a.out + out_row * (int64_t)a.n_out + f0) + lane);
+                                 sg;
+                        v[q] = __ldcg(reinterpret_cast<const uint4 *>(a.out + out_row * (int64_t)a.n_out + f0) + sg);
                     }
                 }
 #pragma unroll
-                for (int j = 0; j < 8; j++)
-                    if (dst[j]) *dst[j] = v[j];
+                for (int q = 0; q < 4; q++)
+                    if (dst[q]) *dst[q] = v[q];
             }
         }
         __threadfence_system();  // rows on other GPUs visible before the arrival below
     } else {
-        // ---------------- dequantisation of this CTA's half of the weight tile
-        const int tid = threadIdx.x - 6 * 32;
-        const uint32_t full_b_leader0 = mapa_shared(smem_u32(&full_b[0]), 0);
-        int stage = 0;
-        uint32_t phase = 0;
+        // ---------------- dequantisation: group g fills the A stage g of steps g, g+2, ...
+        const int g = (warp - (2 + kEpiWarps)) >> 2;
+        const int quad = warp & 3;              // TMEM lanes 32*quad .. 32*quad+31
+        const int lr = quad * 32 + lane;        // this lane's weight row in the CTA
+        const int half = lr / kHalfRows, hr = lr % kHalfRows;
+        const uint32_t a_full_leader = mapa_shared(smem_u32(&a_full[g]), 0);
+        const uint32_t t_dst = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(kRingCol + g * kAStageCols);
         const int64_t units = cluster < total ? (total - cluster + n_clusters - 1) / n_clusters : 0;
-        const int64_t steps = units * KB;  // stages this CTA runs
-        for (int64_t j = 0; j < steps && !*abort_flag; j++) {
-            if (!pair_wait<false>(&full_raw[stage], phase, abort_flag, peer_abort, a.err, 6)) break;
-            dequant_stage<PREC>(raw_tiles + stage * R::kStageBytes, b_tiles + stage * kBTileBytes, tid);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const int64_t steps = units * KS;  // steps this CTA runs
+        // every decision to stop is taken by the whole warp (__all_sync): the
+        // tensor-memory stores below are warp-collective
+        for (int64_t j = g; j < steps; j += 2) {
+            const int sr = (int)(j % SR);
+            bool ok = pair_wait<false>(&full_raw[sr], (uint32_t)(j / SR) & 1, abort_flag, peer_abort, a.err, 6);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            uint32_t v[64];
+            dequant_row<PREC>(raw_tiles + sr * R::kStageBytes + half * kStepKB * R::kHalfBytes, hr, v);
             __syncwarp();
-            if (lane == 0) mbar_arrive_remote(full_b_leader0 + (uint32_t)(stage * sizeof(uint64_t)));
-            if (++stage == S) {
-                stage = 0;
-                phase ^= 1;
+            if (lane == 0) mbar_arrive(&raw_empty[sr]);
+            // the A stage is free once the MMAs of step j - 2 are done (this
+            // group's previous wait saw step j - 4's, so the parity is not stale)
+            if (j >= 2) {
+                ok = pair_wait<false>(&b_empty[(j - 2) % SB], (uint32_t)((j - 2) / SB) & 1, abort_flag, peer_abort,
+                                      a.err, 7);
+                if (!__all_sync(0xffffffffu, ok)) break;
             }
+            tc_fence_after();
+#pragma unroll
+            for (int i = 0; i < 4; i++) tmem_st16(t_dst + 16 * i, v + 16 * i);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(a_full_leader);
         }
     }
 
@@ -529,20 +644,20 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     }
 }
 
-// Re-lays one Int8/FP4 layer (rows x K, reference snapshot layout) into
-// chunks of (chunk_rows rows, 64-wide k-block), each two 64-row halves of
-// codes [64][code bytes] then scales [64][4].  One thread per (row, k-block).
+// Re-lays one Int8/FP4 layer (rows x K, reference snapshot layout) into the
+// records of dequant.cuh: record (row / 64) * KB + kb holds the row's codes
+// of k-block kb column-group major and its four block scales.  One thread
+// per (row, k-block).
 __global__ void relayout_kernel(const uint8_t *__restrict__ codes, const float *__restrict__ scales, int rows, int K,
-                                int code_bytes, int chunk_rows, uint8_t *__restrict__ out) {
+                                int code_bytes, uint8_t *__restrict__ out) {
     const int KB = K / kBK;
     const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (item >= (int64_t)rows * KB) return;
     const int row = (int)(item / KB), kb = (int)(item % KB);
-    const int nt = row / chunk_rows, lr = row % chunk_rows;
-    const int row_bytes = code_bytes + 16;
-    uint8_t *chunk = out + ((int64_t)nt * KB + kb) * chunk_rows * row_bytes;
+    const int hr = row % kHalfRows;
+    uint8_t *rec = out + ((int64_t)(row / kHalfRows) * KB + kb) * half_bytes(code_bytes);
     const int64_t src_row = (int64_t)row * KB * code_bytes + (int64_t)kb * code_bytes;
-    // Int8 codes biased to q + 128 (see chunk_code_off)
+    // Int8 codes biased to q + 128
     const uint32_t bias = code_bytes == 64 ? 0x80808080u : 0u;
     for (int i = 0; i < code_bytes; i += 16) {
         uint4 c = *reinterpret_cast<const uint4 *>(codes + src_row + i);
@@ -550,10 +665,10 @@ __global__ void relayout_kernel(const uint8_t *__restrict__ codes, const float *
         c.y ^= bias;
         c.z ^= bias;
         c.w ^= bias;
-        *reinterpret_cast<uint4 *>(chunk + chunk_code_off(lr, code_bytes) + i) = c;
+        *reinterpret_cast<uint4 *>(rec + half_code_off(hr, i)) = c;
     }
     const float4 s = *reinterpret_cast<const float4 *>(scales + (int64_t)row * (K / 16) + kb * 4);
-    *reinterpret_cast<float4 *>(chunk + chunk_scale_off(lr, code_bytes)) = s;
+    *reinterpret_cast<float4 *>(rec + half_scale_off(hr, code_bytes)) = s;
 }
 
 template <int PREC, bool GATED>
@@ -598,10 +713,10 @@ int launch_one(const CUtensorMap &map, const TcKernelArgs &ka, int sms, cudaStre
 }
 
 bool shapes_ok(const gtmoe_config &c) {
-    // gate/up tiles hold 128 features of each, down tiles 256; K in steps of
-    // 64; the group prefix fits the shared-memory cache
-    return c.hidden % kChunkRows == 0 && c.d_model % kTileN == 0 && c.d_model % kBK == 0 && c.hidden % kBK == 0 &&
-           c.n_shared + c.n_routed + 1 <= kPrefixCache;
+    // kernel 1 tiles 128 hidden features, kernel 2 256 output features; K in
+    // steps of 128; the group prefix fits the shared-memory cache
+    return c.hidden % kGatedFeat == 0 && c.d_model % kDownFeat == 0 && c.d_model % kStepK == 0 &&
+           c.hidden % kStepK == 0 && c.n_shared + c.n_routed + 1 <= kPrefixCache;
 }
 
 }  // namespace
@@ -620,12 +735,12 @@ int tc_relayout_layer(gtmoe_handle *h, LayerDev &L, int which) {
     if (c.weight_precision != GTMOE_INT8 && c.weight_precision != GTMOE_FP4) return 0;
     if (!shapes_ok(c)) return 0;
     const int code_bytes = c.weight_precision == GTMOE_INT8 ? 64 : 32;
-    const int chunk_rows = kChunkRows;
     (void)which;
+    if (L.rows % kHalfRows != 0 || L.width % kBK != 0) return fail(GTMOE_EINVAL, "layer shape does not tile");
     const int64_t items = (int64_t)L.rows * (L.width / kBK);
     GT_CHECK(L.tiled.ensure((size_t)items * (code_bytes + 16)));
     relayout_kernel<<<(unsigned)((items + 255) / 256), 256, 0, h->stream>>>(
-        (const uint8_t *)L.w.p, L.s.as<float>(), L.rows, L.width, code_bytes, chunk_rows, L.tiled.as<uint8_t>());
+        (const uint8_t *)L.w.p, L.s.as<float>(), L.rows, L.width, code_bytes, L.tiled.as<uint8_t>());
     GT_CUDA(cudaGetLastError());
     return 0;
 }
@@ -643,7 +758,7 @@ int tc_prepare(gtmoe_handle *h, TcWeights &w) {
     return 0;
 }
 
-int tc_tile_rows(TcWeights &) { return kTileM; }
+int tc_tile_rows(TcWeights &) { return kTileTok; }
 
 int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, cudaStream_t st) {
     const gtmoe_config &c = h->cfg;
@@ -662,8 +777,8 @@ int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &ta, cudaStrea
     ka.clamp_limit = (float)c.clamp_limit;
     ka.err = w.err;
     CUtensorMap xmap, hmap;
-    GT_CHECK(encode_bf16_2d(&xmap, ta.xp, c.d_model, ta.rows_x, kBK, kCtaRows));
-    GT_CHECK(encode_bf16_2d(&hmap, ta.hp, c.hidden, ta.rows_h, kBK, kCtaRows));
+    GT_CHECK(encode_bf16_2d(&xmap, ta.xp, c.d_model, ta.rows_x, kBK, kCtaTok));
+    GT_CHECK(encode_bf16_2d(&hmap, ta.hp, c.hidden, ta.rows_h, kBK, kCtaTok));
     const int prec = c.weight_precision;
 
     GT_CHECK(h->phase_begin(3));
