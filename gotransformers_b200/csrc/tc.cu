@@ -141,6 +141,33 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
+// The eight MMAs of one step (K = 128): A columns a_tmem + 8k, B k-blocks at
+// bdesc (inputs 0-63) and bdesc + kBSubBytes (64-127), 32 bytes of K per MMA
+// (+2 in the descriptor's 16-byte address units).  Only the first may start
+// a fresh accumulation.
+__device__ __forceinline__ void umma2_ts_step(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, bool accumulate) {
+    constexpr uint64_t kSub = kBSubBytes >> 4;
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t"
+        "setp.ne.b32 p, %10, 0;\n\t"
+        "setp.eq.b32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %9, p;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%3], %4, %9, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %6, %9, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %8, %9, t;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(a_tmem + 8), "l"(bdesc + 2), "r"(a_tmem + 16), "l"(bdesc + 4), "r"(a_tmem + 24),
+        "l"(bdesc + 6), "r"(kIdesc), "r"((uint32_t)accumulate));
+    asm volatile(
+        "{\n\t.reg .pred t;\n\t"
+        "setp.eq.b32 t, 0, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %9, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%3], %4, %9, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %6, %9, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %8, %9, t;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem + 32), "l"(bdesc + kSub), "r"(a_tmem + 40), "l"(bdesc + kSub + 2), "r"(a_tmem + 48),
+        "l"(bdesc + kSub + 4), "r"(a_tmem + 56), "l"(bdesc + kSub + 6), "r"(kIdesc));
+}
+
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory"); }
 // Barrier of the epilogue warps that also ANDs their verdicts, so that all
 // of them take a tile (and its named barriers) or all of them stop.
@@ -262,18 +289,21 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     uint8_t *raw_tiles = b_tiles + SB * kBStageBytes;      // [SR] this CTA's raw weight records
     uint8_t *epi = raw_tiles + SR * R::kStageBytes;        // epilogue staging
     uint64_t *bars = (uint64_t *)(epi + kEpiBytes);
-    uint64_t *full_b = bars;                          // [SB] both token tiles landed (leader)
+    // step j uses token stage j % SB, raw stage j % SR and A stage j & 1; its
+    // MMAs wait for one barrier, full[j % SB] on the leader, which counts the
+    // leader producer's arrival (with both CTAs' token bytes) and the eight
+    // dequantisation warps of the pair that wrote the A stage
+    uint64_t *full = bars;                            // [SB] step ready (leader)
     uint64_t *b_empty = bars + SB;                    // [SB] MMAs of the step done (both CTAs)
     uint64_t *full_raw = bars + 2 * SB;               // [SR] this CTA's raw weights landed
     uint64_t *raw_empty = bars + 2 * SB + SR;         // [SR] raw records decoded (this CTA)
-    uint64_t *a_full = bars + 2 * SB + 2 * SR;        // [2] both CTAs' A stage written (leader)
-    uint64_t *tmem_full = a_full + 2;                 // [2] accumulator ready (both CTAs)
-    uint64_t *tmem_empty = a_full + 4;                // [2] both epilogues done (leader)
-    uint32_t *tmem_slot = (uint32_t *)(a_full + 6);
+    uint64_t *tmem_full = bars + 2 * SB + 2 * SR;     // [2] accumulator ready (both CTAs)
+    uint64_t *tmem_empty = tmem_full + 2;             // [2] both epilogues done (leader)
+    uint32_t *tmem_slot = (uint32_t *)(tmem_full + 4);
     volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
     volatile int *tiles_out = (volatile int *)(tmem_slot + 2);  // epilogue warps' finished tiles (x4)
     int *prefix_s = (int *)((uint8_t *)bars + R::kBarBytes);
-    static_assert((2 * SB + 2 * SR + 6) * 8 + 12 <= R::kBarBytes, "barrier area");
+    static_assert((2 * SB + 2 * SR + 4) * 8 + 12 <= R::kBarBytes, "barrier area");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -289,7 +319,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SB; s++) {
-            mbar_init(&full_b[s], 1);
+            mbar_init(&full[s], 1 + 2 * 4);
             mbar_init(&b_empty[s], 1);
         }
         for (int s = 0; s < SR; s++) {
@@ -297,7 +327,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             mbar_init(&raw_empty[s], 4);
         }
         for (int b = 0; b < 2; b++) {
-            mbar_init(&a_full[b], 2 * 4);
             mbar_init(&tmem_full[b], 1);
             mbar_init(&tmem_empty[b], 2 * kEpiWarps);
         }
@@ -352,12 +381,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     if (!pair_wait<false>(&b_empty[sb], ((uint32_t)(j / SB) & 1) ^ 1, abort_flag, peer_abort, a.err,
                                           1))
                         break;
-                    if (leader) mbar_arrive_expect_tx(&full_b[sb], 2 * kBStageBytes);
+                    if (leader) mbar_arrive_expect_tx(&full[sb], 2 * kBStageBytes);
                     uint8_t *bt = b_tiles + sb * kBStageBytes;
 #pragma unroll
                     for (int i = 0; i < kStepKB; i++)
                         tma_load_2d_pair(bt + i * kBSubBytes, &amap, (s * kStepKB + i) * kBK, row0,
-                                         mapa_shared(smem_u32(&full_b[sb]), 0));
+                                         mapa_shared(smem_u32(&full[sb]), 0));
                 }
             }
             if (*abort_flag) {
@@ -380,19 +409,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 bool ok = true;
                 for (int s = 0; s < KS; s++, j++) {
                     const int sb = (int)(j % SB);
-                    if (!pair_wait<false>(&full_b[sb], (j / SB) & 1, abort_flag, peer_abort, a.err, 3) ||
-                        !pair_wait<false>(&a_full[j & 1], (j >> 1) & 1, abort_flag, peer_abort, a.err, 4)) {
+                    if (!pair_wait<false>(&full[sb], (j / SB) & 1, abort_flag, peer_abort, a.err, 3)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t b_addr = smem_u32(b_tiles + sb * kBStageBytes);
-                    const uint32_t a_tmem = tmem_base + (uint32_t)(kRingCol + (j & 1) * kAStageCols);
-#pragma unroll
-                    for (int k = 0; k < kStepK / 16; k++) {
-                        const uint64_t bdesc = sw128_desc(b_addr + (k >> 2) * kBSubBytes) + (uint64_t)(2 * (k & 3));
-                        umma2_ts_bf16(d_tmem, a_tmem + 8 * k, bdesc, kIdesc, (s | k) != 0);
-                    }
+                    umma2_ts_step(d_tmem, tmem_base + (uint32_t)(kRingCol + (j & 1) * kAStageCols),
+                                  sw128_desc(smem_u32(b_tiles + sb * kBStageBytes)), s != 0);
                     umma2_commit_mc(&b_empty[sb], 0x3);
                 }
                 if (!ok) break;
@@ -593,7 +616,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const int quad = warp & 3;              // TMEM lanes 32*quad .. 32*quad+31
         const int lr = quad * 32 + lane;        // this lane's weight row in the CTA
         const int half = lr / kHalfRows, hr = lr % kHalfRows;
-        const uint32_t a_full_leader = mapa_shared(smem_u32(&a_full[g]), 0);
+        const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
         const uint32_t t_dst = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(kRingCol + g * kAStageCols);
         const int64_t units = cluster < total ? (total - cluster + n_clusters - 1) / n_clusters : 0;
         const int64_t steps = units * KS;  // steps this CTA runs
@@ -620,7 +643,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_remote(a_full_leader);
+            if (lane == 0) mbar_arrive_remote(full_leader0 + (uint32_t)((j % SB) * sizeof(uint64_t)));
         }
     }
 
