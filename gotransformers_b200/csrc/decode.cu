@@ -6,8 +6,8 @@
 // bytes of the expert weights (feedforward/gatedfeedforward.go:49-57 over
 // lowprecision rows, rows.go:207-257), not by tensor throughput.  These
 // kernels stream each touched expert's Int8/FP4 weight rows once, in the
-// tile-chunk layout the tensor-core kernels use (128 rows x 64 inputs: codes
-// then block scales), dequantise them in registers straight into mma.sync
+// record layout the tensor-core kernels use (dequant.cuh: 64 rows x 64
+// inputs, codes then block scales), dequantise them in registers straight into mma.sync
 // B fragments (no shared-memory round trip for the decoded weights) and run
 // them against the few token rows (16 per m-tile).
 //
@@ -24,8 +24,9 @@
 // 64-row half of a weight chunk).  A CTA of eight compute warps and one
 // producer warp runs a unit.  The producer copies the tile's token rows once
 // per unit (one bulk copy per row, all inputs; padded rows: conflict-free
-// fragment loads) and keeps a 4-stage ring of weight steps, one contiguous
-// bulk copy per layer per 64-input step (gate and up for kernel 1): the TMA
+// fragment loads) and keeps a 2-stage ring of weight steps, one contiguous
+// bulk copy per layer per 128-input step (gate and up for kernel 1; the
+// records of consecutive k-blocks of a 64-row half are adjacent): the TMA
 // engine's rate per CTA grows with the size of each copy, so few large copies
 // replace many small ones.  "full" mbarriers carry the transaction counts,
 // "empty" ones are released by each compute warp; no CTA-wide barrier.  The
@@ -46,7 +47,8 @@ namespace {
 constexpr int kComputeWarps = 8;                          // 8 features each
 constexpr int kDecodeThreads = (kComputeWarps + 1) * 32;  // + one producer warp
 constexpr int kDecodeFeatures = kHalfRows;               // output features per unit
-constexpr int kDecodeStages = 4;
+constexpr int kDecodeStepKB = 2;                          // 64-input k-blocks per weight step
+constexpr int kDecodeStages = 2;
 
 template <int PREC>
 struct DecodeLayout {
@@ -56,10 +58,13 @@ struct DecodeLayout {
     static_assert(kHalf == kDecodeFeatures * kChunkRowBytes, "one record per 64-row half");
 };
 
+// One weight step: per layer the half's records of kDecodeStepKB consecutive
+// k-blocks, contiguous in the layer's buffer, so one bulk copy per layer.
 template <int PREC, bool GATED>
 struct DecodeStage {
     static constexpr int kLayers = GATED ? 2 : 1;
-    static constexpr int kBytes = kLayers * DecodeLayout<PREC>::kHalf;
+    static constexpr int kLayerBytes = kDecodeStepKB * DecodeLayout<PREC>::kHalf;
+    static constexpr int kBytes = kLayers * kLayerBytes;
 };
 
 // Token-row pitch in shared memory for K inputs: 32 bytes of padding make
@@ -173,7 +178,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             if (lane == 0) mbar_arrive_expect_tx(&xfull, (uint32_t)m * K * 2);
             __syncwarp();
             for (int r = lane; r < m; r += 32) bulk_copy(xs + r * xpitch, xrow0 + (int64_t)r * K * 2, K * 2, &xfull);
-            for (int kb = 0; kb < KB; kb++, n++) {
+            for (int kb = 0; kb < KB; kb += kDecodeStepKB, n++) {
                 const uint32_t slot = n % kDecodeStages;
                 if (n >= kDecodeStages && !*abort_p)
                     mbar_wait(&empty[slot], ((n / kDecodeStages) - 1) & 1, abort_p, a.err, 10);
@@ -181,8 +186,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
                 if (lane == 0) {
                     uint8_t *st = ring + slot * ST::kBytes;
                     mbar_arrive_expect_tx(&full[slot], ST::kBytes);
-                    bulk_copy(st, w0 + (int64_t)kb * DL::kHalf, DL::kHalf, &full[slot]);
-                    if (GATED) bulk_copy(st + DL::kHalf, w1 + (int64_t)kb * DL::kHalf, DL::kHalf, &full[slot]);
+                    bulk_copy(st, w0 + (int64_t)kb * DL::kHalf, ST::kLayerBytes, &full[slot]);
+                    if (GATED)
+                        bulk_copy(st + ST::kLayerBytes, w1 + (int64_t)kb * DL::kHalf, ST::kLayerBytes, &full[slot]);
                 }
                 __syncwarp();
             }
@@ -224,27 +230,32 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
         const uint8_t *xrow = xs + g8 * xpitch + 8 * q;
-        for (int kb = 0; kb < KB; kb++, n++) {
+        for (int kb0 = 0; kb0 < KB; kb0 += kDecodeStepKB, n++) {
             const uint32_t slot = n % kDecodeStages;
             if (!*abort_p) mbar_wait(&full[slot], (n / kDecodeStages) & 1, abort_p, a.err, 9);
             if (*abort_p) break;
             const uint8_t *st = ring + slot * ST::kBytes;
-            float4 sc[2];
 #pragma unroll
-            for (int l = 0; l < ST::kLayers; l++)
-                sc[l] = *reinterpret_cast<const float4 *>(st + l * DL::kHalf + half_scale_off(row, DL::kCodeBytes));
+            for (int sub = 0; sub < kDecodeStepKB; sub++) {
+                const int kb = kb0 + sub;
+                float4 sc[2];
 #pragma unroll
-            for (int s = 0; s < 4; s++) {
-                const uint8_t *xa = xrow + kb * 128 + 32 * s;
-                const uint2 lo = *reinterpret_cast<const uint2 *>(xa);
-                const uint2 hi = *reinterpret_cast<const uint2 *>(xa + 8 * xpitch);
-                const uint32_t af[4] = {lo.x, hi.x, lo.y, hi.y};
+                for (int l = 0; l < ST::kLayers; l++)
+                    sc[l] = *reinterpret_cast<const float4 *>(st + l * ST::kLayerBytes + sub * DL::kHalf +
+                                                              half_scale_off(row, DL::kCodeBytes));
 #pragma unroll
-                for (int l = 0; l < ST::kLayers; l++) {
-                    const float scl = s == 0 ? sc[l].x : s == 1 ? sc[l].y : s == 2 ? sc[l].z : sc[l].w;
-                    uint32_t bw[2];
-                    decode_row_block<PREC>(st + l * DL::kHalf, scl, row, s, q, bw);
-                    mma_f16_16816(acc[l], af, bw[0], bw[1]);
+                for (int s = 0; s < 4; s++) {
+                    const uint8_t *xa = xrow + kb * 128 + 32 * s;
+                    const uint2 lo = *reinterpret_cast<const uint2 *>(xa);
+                    const uint2 hi = *reinterpret_cast<const uint2 *>(xa + 8 * xpitch);
+                    const uint32_t af[4] = {lo.x, hi.x, lo.y, hi.y};
+#pragma unroll
+                    for (int l = 0; l < ST::kLayers; l++) {
+                        const float scl = s == 0 ? sc[l].x : s == 1 ? sc[l].y : s == 2 ? sc[l].z : sc[l].w;
+                        uint32_t bw[2];
+                        decode_row_block<PREC>(st + l * ST::kLayerBytes + sub * DL::kHalf, scl, row, s, q, bw);
+                        mma_f16_16816(acc[l], af, bw[0], bw[1]);
+                    }
                 }
             }
             __syncwarp();
@@ -314,8 +325,9 @@ bool decode_usable(int precision, int d, int h, int64_t T) {
     // the token tile of a unit (16 rows x all inputs) and the weight ring fit in shared memory
     const int kmax = d > h ? d : h;
     const int smem = kDecodeTileRows * decode_x_pitch(kmax) + kDecodeStages * DecodeStage<GTMOE_INT8, true>::kBytes;
-    return (precision == GTMOE_INT8 || precision == GTMOE_FP4) && T <= kDecodeMaxRows && d % 128 == 0 &&
-           h % 128 == 0 && smem <= 200 * 1024;
+    return (precision == GTMOE_INT8 || precision == GTMOE_FP4) && T <= kDecodeMaxRows &&
+           d % (64 * kDecodeStepKB) == 0 && h % (64 * kDecodeStepKB) == 0 && d % 128 == 0 && h % 128 == 0 &&
+           smem <= 200 * 1024;
 }
 
 int launch_decode(const DecodeArgs &a, int which, cudaStream_t st) {
