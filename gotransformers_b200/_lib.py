@@ -55,6 +55,8 @@ EXPORTS = [
     "gtmoe_route_noalloc",
     "gtmoe_set_norm",
     "gtmoe_forward_block",
+    "gtmoe_set_training",
+    "gtmoe_backward",
     "gtmoe_weightfile_open",
     "gtmoe_weightfile_close",
     "gtmoe_weightfile_count",
@@ -127,6 +129,8 @@ def lib():
             L.gtmoe_fill_normal.argtypes = [vp, i32, i64, ctypes.c_uint64, ctypes.c_uint64, i64, d]
             L.gtmoe_set_norm.argtypes = [vp, vp, d]
             L.gtmoe_forward_block.argtypes = [vp, vp, i32, i64, vp, vp, i32, vp, vp, vp, vp]
+            L.gtmoe_set_training.argtypes = [vp, i32]
+            L.gtmoe_backward.argtypes = [vp, vp, i32, vp, i32, vp, vp]
             L.gtmoe_weightfile_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(vp)]
             L.gtmoe_weightfile_close.argtypes = [vp]
             L.gtmoe_weightfile_close.restype = None

@@ -38,7 +38,7 @@ static std::atomic<int64_t> g_launches{0};
 void note_launches(int n) { g_launches += n; }
 int64_t launches_so_far() { return g_launches.load(); }
 
-static bool is_device_ptr(const void *p) {
+bool is_device_ptr(const void *p) {
     if (!p) return false;
     cudaPointerAttributes at;
     cudaError_t e = cudaPointerGetAttributes(&at, p);
@@ -166,7 +166,7 @@ int create_handle(const gtmoe_config *cfg, int device, int n_ranks, int rank, gt
     return 0;
 }
 
-static int upload(DevBuf &dst, const void *src, size_t bytes, cudaStream_t st) {
+int upload(DevBuf &dst, const void *src, size_t bytes, cudaStream_t st) {
     GT_CHECK(dst.ensure(bytes));
     if (bytes) GT_CUDA(cudaMemcpyAsync(dst.p, src, bytes, cudaMemcpyDefault, st));
     return 0;
@@ -612,6 +612,7 @@ void gtmoe_destroy(gtmoe_t h) {
                           &h->res_dev, &h->fixups, &h->flagged, &h->x_pipe[0], &h->x_pipe[1], &h->out_pipe[0],
                           &h->out_pipe[1], &h->load_acc, &h->norm_w, &h->block_x, &h->block_xn};
         for (DevBuf *b : bufs) b->release();
+        release_training_state(h);
         for (cudaEvent_t e : h->pipe_ev)
             if (e) cudaEventDestroy(e);
         if (h->h2d_stream) cudaStreamDestroy(h->h2d_stream);
@@ -819,8 +820,9 @@ int forward_locked(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64
 
     // a large batch in host memory runs as chunks whose copies overlap compute
     // (not with timing, a host residual, or the whole-batch permutation asked for)
-    const bool pipelined = T >= kPipelineMinRows && !h->timing && !perm && !is_device_ptr(x) &&
+    const bool pipelined = T >= kPipelineMinRows && !h->timing && !perm && !h->training && !is_device_ptr(x) &&
                            !is_device_ptr(out) && (!residual || is_device_ptr(residual));
+    h->tr_valid = 0;  // a backward refers to the last Forward only
 
     const void *x_dev = x;
     if (T > 0 && !pipelined && !is_device_ptr(x)) {
@@ -858,6 +860,7 @@ int forward_locked(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64
     // device pointers only, no host round trip inside: the forward may be replayed as a CUDA graph
     const bool graphable = !c.hash_routing && x_dev == x && out_dev == out && res_dev == residual;
     GT_CHECK(run_forward(h, graphable, x_dev, x_dtype, T, ids_dev, res_dev, out_dev, out_dtype));
+    if (h->training) GT_CHECK(save_training_state(h, x_dev, x_dtype, T));
 
     bool sync = out_host;
     const int64_t TK = T * k;

@@ -1,0 +1,486 @@
+// backward.cu -- MixtureOfExperts.Backward (mixtureofexperts.go:227-285) on
+// the GPU, in float64, for the last Forward of a handle in training mode.
+//
+// The reference's pieces, restated:
+// * every shared expert's GatedFeedForward.Backward on the output gradients,
+//   summed (AddMatrices) in expert order; then for each routed expert in
+//   ascending order the backward of its rows with the output gradient rows
+//   scaled by the token's gate, added into the token's row (:235-257);
+// * GatedFeedForward.Backward (feedforward/gatedfeedforward.go:59-66):
+//   dH = Down.Backward(dY); gate' = dH * up outputs; up' = dH * gate outputs;
+//   dX = Gate.Backward(gate') + Up.Backward(up');
+// * perceptron.Layer.Backward for compressed rows (layer.go:164-207): the
+//   pre-activation gradient g * act'(pre) per (example, neuron); the expert
+//   layers are compressed, so frozen (no weight gradients, :165-167, 184);
+//   the input gradients add every neuron's scaled row in ascending neuron
+//   order, skipping zero gradients (adapter.go:108-120 ->
+//   Rows.AddScaledRowTo, lowprecision/rows.go:285-324: Float64 g * w,
+//   Float32 g * float64(w), Int8 (g * scale) * q, FP4 (g * scale) * value);
+// * the router term (:262-284): per token, gate gradient i = dout . y_i (the
+//   expert's output row), then (gate gradient i - sum_j gate gradient j *
+//   gate j) / sum of the chosen affinities, times affinityDerivative
+//   (softplus'(logit) / (2 affinity), :84-86), as the gradient of logit i;
+//   RouterLayer.Backward on these logit gradients: bias gradients added per
+//   example, weight gradients as TransposedTimesMatrix (tokens ascending,
+//   vectormath/backend.go:139-158) added after, input gradients through the
+//   dense weights (MatrixTimesWeights, backend.go:84-112: experts ascending,
+//   zeros skipped); dx = expert input gradients + router input gradients.
+//
+// The gate/up pre-activations, hidden values and expert outputs the reference
+// keeps from Forward are recomputed here from the saved float64 input rows
+// with the layers' DotRow (rows.go:207-257: per 16-value block a partial sum
+// of x * code, times float64(scale)).  Sums run in the reference's order.
+// Work rows: r < S*T are (shared expert r / T, token r % T); after them
+// (token t, slot i) for t*k + i, one CTA each.
+#include "handle.h"
+
+namespace gtmoe {
+namespace {
+
+constexpr int kBwdThreads = 256;
+
+// Rows.DotRow of one layer row against float64 inputs (shared memory).
+__device__ double dot_row_f64(const void *w, const float *s, int prec, int width, int row, const double *x) {
+    const int64_t base = (int64_t)row * width;
+    double total = 0;
+    if (prec == GTMOE_FLOAT64) {
+        const double *v = (const double *)w + base;
+        for (int i = 0; i < width; i++) total += x[i] * v[i];
+    } else if (prec == GTMOE_FLOAT32) {
+        const float *v = (const float *)w + base;
+        for (int i = 0; i < width; i++) total += x[i] * (double)v[i];
+    } else {
+        const int nb = scale_blocks(width);
+        for (int b = 0; b < nb; b++) {
+            const int i1 = min(width, (b + 1) * kValuesPerScale);
+            double partial = 0;
+            if (prec == GTMOE_INT8) {
+                const int8_t *q = (const int8_t *)w + base;
+                for (int i = b * kValuesPerScale; i < i1; i++) partial += x[i] * (double)q[i];
+            } else {
+                const uint8_t *p = (const uint8_t *)w + (int64_t)row * fp4_row_bytes(width);
+                for (int i = b * kValuesPerScale; i < i1; i++) {
+                    const uint8_t byte = p[i / 2];
+                    const uint32_t code = (i & 1) ? (byte >> 4) : (byte & 15u);
+                    partial += x[i] * (double)fp4_value(code);
+                }
+            }
+            total += partial * (double)s[(int64_t)row * nb + b];
+        }
+    }
+    return total;
+}
+
+// One term of Rows.AddScaledRowTo(row, g, target)[col].
+__device__ __forceinline__ double scaled_weight(const void *w, const float *s, int prec, int width, int row, int col,
+                                                double g) {
+    if (prec == GTMOE_FLOAT64) return g * ((const double *)w)[(int64_t)row * width + col];
+    if (prec == GTMOE_FLOAT32) return g * (double)((const float *)w)[(int64_t)row * width + col];
+    const double sc = (double)s[(int64_t)row * scale_blocks(width) + col / kValuesPerScale];
+    if (prec == GTMOE_INT8) return (g * sc) * (double)((const int8_t *)w)[(int64_t)row * width + col];
+    const uint8_t byte = ((const uint8_t *)w)[(int64_t)row * fp4_row_bytes(width) + col / 2];
+    const uint32_t code = (col & 1) ? (byte >> 4) : (byte & 15u);
+    return (g * sc) * (double)fp4_value(code);
+}
+
+__device__ __forceinline__ double sigmoid_d(double x) { return 1.0 / (1.0 + exp(-x)); }
+
+// Derivatives of the expert activations, taking the pre-activation: SiLU
+// s + x s (1 - s) (activationfunction.go:106-109), Linear 1 (:162-164), and
+// the clamped variants, 0 where the forward clamps
+// (moreactivationfunctions.go:207-243).
+__device__ __forceinline__ double gate_deriv(double x, int clamped, double limit) {
+    if (clamped && x > limit) return 0.0;
+    const double s = sigmoid_d(x);
+    return s + x * s * (1 - s);
+}
+__device__ __forceinline__ double up_deriv(double x, int clamped, double limit) {
+    if (clamped && (x > limit || x < -limit)) return 0.0;
+    return 1.0;
+}
+
+// The router's softplus (moreactivationfunctions.go:8-16).
+__device__ __forceinline__ double softplus_d(double x) {
+    if (x > 20) return x;
+    if (x < -20) return exp(x);
+    return log1p(exp(x));
+}
+
+struct BwdArgs {
+    const ExpertLayers *experts;
+    int prec;
+    int S, k, d, h;
+    int clamped;
+    double limit;
+    int64_t T;
+    const double *x;        // T x d, the Forward's input rows
+    const int32_t *chosen;  // T x k, ascending per token
+    const double *gates;    // T x k
+    const double *dout;     // T x d
+    double *rows_dx;        // (S*T + T*k) x d: input gradients of each work row
+    double *rows_y;         // T*k x d: routed experts' output rows
+};
+
+// One work row per iteration: recompute the expert's gate/up pre-activations,
+// hidden values and (routed rows) output, then its backward to the input
+// gradients.
+__global__ void __launch_bounds__(kBwdThreads) bwd_rows_kernel(const BwdArgs a) {
+    extern __shared__ double bsm[];
+    const int d = a.d, h = a.h;
+    double *sx = bsm;        // d  input row
+    double *sdy = sx + d;    // d  the expert's output gradients (gate-scaled for routed rows)
+    double *spg = sdy + d;   // h  gate pre-activations
+    double *spu = spg + h;   // h  up pre-activations
+    double *shid = spu + h;  // h  hidden values, then the gate pre-activation gradients
+    double *sdh = shid + h;  // h  up pre-activation gradients
+    const int64_t n_shared_rows = (int64_t)a.S * a.T;
+    const int64_t n_rows = n_shared_rows + a.T * a.k;
+    for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
+        int64_t t, slot = -1;
+        int e;
+        double gate = 1.0;
+        if (r < n_shared_rows) {
+            e = (int)(r / a.T);
+            t = r % a.T;
+        } else {
+            slot = r - n_shared_rows;
+            t = slot / a.k;
+            e = a.S + a.chosen[slot];
+            gate = a.gates[slot];
+        }
+        const ExpertLayers &L = a.experts[e];
+        for (int i = threadIdx.x; i < d; i += blockDim.x) {
+            sx[i] = a.x[t * d + i];
+            const double g = a.dout[t * d + i];
+            sdy[i] = slot >= 0 ? g * gate : g;  // vectormath.Scale for routed rows
+        }
+        __syncthreads();
+        // forward recompute: gate and up layers (d -> h), hidden = act_g * act_u
+        for (int j = threadIdx.x; j < h; j += blockDim.x) {
+            const double pg = dot_row_f64(L.w[0], L.s[0], a.prec, d, j, sx) + (L.b64[0] ? L.b64[0][j] : 0.0);
+            const double pu = dot_row_f64(L.w[1], L.s[1], a.prec, d, j, sx) + (L.b64[1] ? L.b64[1][j] : 0.0);
+            spg[j] = pg;
+            spu[j] = pu;
+            shid[j] = gate_act<double>(pg, a.clamped, a.limit) * up_act<double>(pu, a.clamped, a.limit);
+        }
+        __syncthreads();
+        // routed rows: the expert's output row (down layer, linear), for the router term
+        if (slot >= 0)
+            for (int o = threadIdx.x; o < d; o += blockDim.x)
+                a.rows_y[slot * d + o] =
+                    dot_row_f64(L.w[2], L.s[2], a.prec, h, o, shid) + (L.b64[2] ? L.b64[2][o] : 0.0);
+        __syncthreads();
+        // Down.Backward: dH[j] = sum over output neurons o (ascending, zeros
+        // skipped) of the scaled row term; the linear derivative is 1.  Then
+        // the gate / up pre-activation gradients.
+        for (int j = threadIdx.x; j < h; j += blockDim.x) {
+            double dh = 0;
+            for (int o = 0; o < d; o++) {
+                const double g = sdy[o] * 1.0;
+                if (g != 0) dh += scaled_weight(L.w[2], L.s[2], a.prec, h, o, j, g);
+            }
+            const double pg = spg[j], pu = spu[j];
+            const double go = gate_act<double>(pg, a.clamped, a.limit);
+            const double uo = up_act<double>(pu, a.clamped, a.limit);
+            shid[j] = (dh * uo) * gate_deriv(pg, a.clamped, a.limit);
+            sdh[j] = (dh * go) * up_deriv(pu, a.clamped, a.limit);
+        }
+        __syncthreads();
+        // Gate.Backward + Up.Backward input gradients (neurons ascending, zeros skipped)
+        double *dst = a.rows_dx + r * d;
+        for (int c = threadIdx.x; c < d; c += blockDim.x) {
+            double dg = 0, du = 0;
+            for (int j = 0; j < h; j++) {
+                const double gg = shid[j], gu = sdh[j];
+                if (gg != 0) dg += scaled_weight(L.w[0], L.s[0], a.prec, d, j, c, gg);
+                if (gu != 0) du += scaled_weight(L.w[1], L.s[1], a.prec, d, j, c, gu);
+            }
+            dst[c] = dg + du;
+        }
+        __syncthreads();
+    }
+}
+
+// Per token, the chosen experts' router logits in float64 (DotProduct,
+// inputs ascending, then the bias), their affinities and the gates as
+// Forward forms them (mixtureofexperts.go:154-169): the affinity total over
+// the chosen experts in order, gate i = affinity i / total.  (The forward's
+// gates come from tensor-core logits, exact only where the selection needed
+// it; the backward uses the reference's values.)
+__global__ void bwd_gates_kernel(const double *__restrict__ x, const double *__restrict__ wr,
+                                 const double *__restrict__ br, const int32_t *__restrict__ chosen, int64_t T, int d,
+                                 int k, double *__restrict__ logit, double *__restrict__ aff,
+                                 double *__restrict__ gate) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    const double *xr = x + t * d;
+    double total = 0;
+    for (int i = 0; i < k; i++) {
+        const int e = chosen[t * k + i];
+        double z = 0;
+        for (int c = 0; c < d; c++) z += xr[c] * wr[(int64_t)e * d + c];
+        z += br[e];
+        const double a = sqrt(softplus_d(z));
+        logit[t * k + i] = z;
+        aff[t * k + i] = a;
+        total += a;
+    }
+    for (int i = 0; i < k; i++) gate[t * k + i] = aff[t * k + i] / total;
+}
+
+// Router term per token: the gate gradients and the logit gradients (T x k).
+__global__ void bwd_router_kernel(const double *__restrict__ logit, const double *__restrict__ aff,
+                                  const double *__restrict__ gates, const double *__restrict__ dout,
+                                  const double *__restrict__ rows_y, int64_t T, int d, int k,
+                                  double *__restrict__ lg) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    const double *gr = dout + t * d;
+    double gate_grad[kMaxTopK];
+    double weighted = 0, total = 0;
+    for (int i = 0; i < k; i++) {
+        const double *yr = rows_y + (t * k + i) * d;
+        double gg = 0;
+        for (int c = 0; c < d; c++) gg += gr[c] * yr[c];
+        gate_grad[i] = gg;
+        weighted += gg * gates[t * k + i];
+        total += aff[t * k + i];
+    }
+    for (int i = 0; i < k; i++) {
+        const double ag = (gate_grad[i] - weighted) / total;
+        lg[t * k + i] = ag * (sigmoid_d(logit[t * k + i]) / (2 * aff[t * k + i]));
+    }
+}
+
+// dx per (token, input): shared experts' rows summed in order from zero, the
+// routed rows added in ascending expert order, then the router's input
+// gradient (experts ascending; only chosen experts have nonzero logit
+// gradients) added to the total.
+template <typename OT>
+__global__ void bwd_dx_kernel(const double *__restrict__ rows_dx, const double *__restrict__ lg,
+                              const int32_t *__restrict__ chosen, const double *__restrict__ wr, int64_t T, int d,
+                              int S, int k, int router, OT *__restrict__ dx) {
+    const int64_t n = T * d;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = p / d;
+        const int c = (int)(p % d);
+        double v = 0;
+        for (int s = 0; s < S; s++) v = v + rows_dx[((int64_t)s * T + t) * d + c];
+        for (int i = 0; i < k; i++) v += rows_dx[((int64_t)S * T + t * k + i) * d + c];
+        if (router) {
+            double rg = 0;
+            for (int i = 0; i < k; i++) {
+                const double g = lg[t * k + i];
+                if (g != 0) rg += g * wr[(int64_t)chosen[t * k + i] * d + c];
+            }
+            v = v + rg;
+        }
+        dx[p] = from_double<OT>(v);
+    }
+}
+
+// RouterLayer.Backward parameter gradients: bias[e] += each token's logit
+// gradient in token order; weight[e][c] += (sum over tokens ascending of
+// logit gradient * x[t][c]), the tokens of expert e from the Forward's
+// expert-sorted lists (token-ascending).
+__global__ void bwd_router_params_kernel(const double *__restrict__ lg, const double *__restrict__ x,
+                                         const int32_t *__restrict__ chosen, const int32_t *__restrict__ perm,
+                                         const int64_t *__restrict__ offsets, int E, int d, int k,
+                                         double *__restrict__ wgrad, double *__restrict__ bgrad) {
+    const int64_t n = (int64_t)E * d;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += (int64_t)gridDim.x * blockDim.x) {
+        const int e = (int)(p / d);
+        const int c = (int)(p % d);
+        double acc = 0, bacc = bgrad ? bgrad[e] : 0.0;
+        for (int64_t q = offsets[e]; q < offsets[e + 1]; q++) {
+            const int64_t t = perm[q];
+            int i = 0;
+            while (i < k && chosen[t * k + i] != e) i++;
+            const double g = lg[t * k + i];
+            if (c == 0) bacc += g;
+            if (g != 0) acc += g * x[t * d + c];
+        }
+        if (wgrad) wgrad[p] += acc;
+        if (c == 0 && bgrad) bgrad[e] = bacc;
+    }
+}
+
+__global__ void to_f64_kernel(const void *__restrict__ src, int dtype, int64_t n, double *__restrict__ dst) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = load_as_double(src, dtype, i);
+}
+
+unsigned grid_for(int64_t n, int threads) {
+    const int64_t b = (n + threads - 1) / threads;
+    return (unsigned)(b < 1 ? 1 : b > 65535 ? 65535 : b);
+}
+
+}  // namespace
+
+int save_training_state(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T) {
+    const gtmoe_config &c = h->cfg;
+    cudaStream_t st = h->stream;
+    const int d = c.d_model, k = c.experts_per_token, E = c.n_routed;
+    h->tr_valid = 0;
+    h->tr_T = T;
+    if (T > 0) {
+        GT_CHECK(h->tr_x.ensure(sizeof(double) * (size_t)T * d));
+        GT_CHECK(h->tr_chosen.ensure(sizeof(int32_t) * (size_t)T * k));
+        GT_CHECK(h->tr_gates.ensure(sizeof(double) * (size_t)T * k));
+        GT_CHECK(h->tr_perm.ensure(sizeof(int32_t) * (size_t)T * k));
+        GT_CHECK(h->tr_offsets.ensure(sizeof(int64_t) * (E + 1)));
+        to_f64_kernel<<<grid_for(T * d, 256), 256, 0, st>>>(x_dev, x_dtype, T * d, h->tr_x.as<double>());
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+        GT_CUDA(cudaMemcpyAsync(h->tr_chosen.p, h->chosen.p, sizeof(int32_t) * T * k, cudaMemcpyDeviceToDevice, st));
+        GT_CUDA(cudaMemcpyAsync(h->tr_gates.p, h->gates64.p, sizeof(double) * T * k, cudaMemcpyDeviceToDevice, st));
+        GT_CUDA(cudaMemcpyAsync(h->tr_perm.p, h->perm.p, sizeof(int32_t) * T * k, cudaMemcpyDeviceToDevice, st));
+        GT_CUDA(cudaMemcpyAsync(h->tr_offsets.p, h->offsets.p, sizeof(int64_t) * (E + 1), cudaMemcpyDeviceToDevice,
+                                st));
+    }
+    h->tr_valid = 1;
+    return 0;
+}
+
+void release_training_state(gtmoe_handle *h) {
+    DevBuf *bufs[] = {&h->tr_x,    &h->tr_chosen, &h->tr_gates, &h->tr_perm, &h->tr_offsets, &h->bw_in,
+                      &h->bw_dout, &h->bw_dx,     &h->bw_rows,  &h->bw_y,    &h->bw_lg,      &h->bw_zag,
+                      &h->bw_rw,   &h->bw_rb};
+    for (DevBuf *b : bufs) b->release();
+    h->tr_valid = 0;
+}
+
+}  // namespace gtmoe
+
+using namespace gtmoe;
+
+extern "C" {
+
+int gtmoe_set_training(gtmoe_t h, int on) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    if (on && h->n_ranks > 1) return fail(GTMOE_EINVAL, "training state is kept on one GPU (not expert parallel)");
+    h->training = on ? 1 : 0;
+    if (!on) h->tr_valid = 0;
+    return 0;
+}
+
+int gtmoe_backward(gtmoe_t h, const void *dout, int dout_dtype, void *dx, int dx_dtype, double *router_weight_grad,
+                   double *router_bias_grad) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    if (h->n_ranks > 1) return fail(GTMOE_EINVAL, "gtmoe_backward runs on one GPU");
+    if (!h->training || !h->tr_valid)
+        return fail(GTMOE_ENOTREADY, "mixture of experts: call Forward (with training on) before Backward");
+    if (dout_dtype < GTMOE_DTYPE_F64 || dout_dtype > GTMOE_DTYPE_BF16 || dx_dtype < GTMOE_DTYPE_F64 ||
+        dx_dtype > GTMOE_DTYPE_BF16)
+        return fail(GTMOE_EINVAL, "unknown dtype");
+    const gtmoe_config &c = h->cfg;
+    const int64_t T = h->tr_T;
+    const int d = c.d_model, hd = c.hidden, k = c.experts_per_token, E = c.n_routed, S = c.n_shared;
+    if (T > 0 && (!dout || !dx)) return fail(GTMOE_EINVAL, "mixture of experts: dout and dx must be given");
+    if (T == 0) return 0;
+    GT_CUDA(cudaSetDevice(h->device));
+    GT_CHECK(refresh_table(h));
+    cudaStream_t st = h->stream;
+    const bool router = !c.hash_routing;
+
+    // output gradients as float64 on the device
+    const size_t in_bytes = dtype_size(dout_dtype) * (size_t)T * d;
+    const void *dout_dev = dout;
+    if (!is_device_ptr(dout)) {
+        GT_CHECK(upload(h->bw_in, dout, in_bytes, st));
+        dout_dev = h->bw_in.p;
+    }
+    GT_CHECK(h->bw_dout.ensure(sizeof(double) * (size_t)T * d));
+    to_f64_kernel<<<grid_for(T * d, 256), 256, 0, st>>>(dout_dev, dout_dtype, T * d, h->bw_dout.as<double>());
+    GT_CUDA(cudaGetLastError());
+
+    const int64_t n_rows = (int64_t)S * T + T * k;
+    GT_CHECK(h->bw_rows.ensure(sizeof(double) * (size_t)n_rows * d));
+    GT_CHECK(h->bw_y.ensure(sizeof(double) * (size_t)T * k * d));
+    GT_CHECK(h->bw_lg.ensure(sizeof(double) * (size_t)T * k));
+    GT_CHECK(h->bw_zag.ensure(3 * sizeof(double) * (size_t)T * k));
+    double *zl = h->bw_zag.as<double>(), *za = zl + T * k, *zg = za + T * k;
+    if (router) {
+        bwd_gates_kernel<<<grid_for(T, 128), 128, 0, st>>>(h->tr_x.as<double>(), h->wr64.as<double>(),
+                                                            h->br.as<double>(), h->tr_chosen.as<int32_t>(), T, d, k,
+                                                            zl, za, zg);
+        GT_CUDA(cudaGetLastError());
+    }
+
+    BwdArgs a;
+    a.experts = h->table.as<ExpertLayers>();
+    a.prec = c.weight_precision;
+    a.S = S;
+    a.k = k;
+    a.d = d;
+    a.h = hd;
+    a.clamped = c.clamped;
+    a.limit = c.clamp_limit;
+    a.T = T;
+    a.x = h->tr_x.as<double>();
+    a.chosen = h->tr_chosen.as<int32_t>();
+    a.gates = router ? zg : h->tr_gates.as<double>();  // hash routing: 1/k from Forward
+    a.dout = h->bw_dout.as<double>();
+    a.rows_dx = h->bw_rows.as<double>();
+    a.rows_y = h->bw_y.as<double>();
+    const size_t smem = sizeof(double) * (2 * (size_t)d + 4 * (size_t)hd);
+    if (smem > 220 * 1024) return fail(GTMOE_EINVAL, "backward: d_model and hidden too large for one work row");
+    GT_CUDA(cudaFuncSetAttribute(bwd_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    bwd_rows_kernel<<<grid_for(n_rows, 1), kBwdThreads, smem, st>>>(a);
+    GT_CUDA(cudaGetLastError());
+    if (router) {
+        bwd_router_kernel<<<grid_for(T, 128), 128, 0, st>>>(zl, za, zg, a.dout, a.rows_y, T, d, k,
+                                                             h->bw_lg.as<double>());
+        GT_CUDA(cudaGetLastError());
+    }
+
+    // dx (device, in dx_dtype)
+    const size_t out_bytes = dtype_size(dx_dtype) * (size_t)T * d;
+    void *dx_dev = dx;
+    const bool dx_host = !is_device_ptr(dx);
+    if (dx_host) {
+        GT_CHECK(h->bw_dx.ensure(out_bytes));
+        dx_dev = h->bw_dx.p;
+    }
+    const unsigned gdx = grid_for(T * d, 256);
+    const double *lg = h->bw_lg.as<double>();
+    const double *wr = h->wr64.as<double>();
+    if (dx_dtype == GTMOE_DTYPE_F64)
+        bwd_dx_kernel<double><<<gdx, 256, 0, st>>>(a.rows_dx, lg, a.chosen, wr, T, d, S, k, router, (double *)dx_dev);
+    else if (dx_dtype == GTMOE_DTYPE_F32)
+        bwd_dx_kernel<float><<<gdx, 256, 0, st>>>(a.rows_dx, lg, a.chosen, wr, T, d, S, k, router, (float *)dx_dev);
+    else
+        bwd_dx_kernel<__nv_bfloat16><<<gdx, 256, 0, st>>>(a.rows_dx, lg, a.chosen, wr, T, d, S, k, router,
+                                                           (__nv_bfloat16 *)dx_dev);
+    GT_CUDA(cudaGetLastError());
+    note_launches(router ? 6 : 4);
+
+    // router parameter gradients, added to the caller's
+    if (router && (router_weight_grad || router_bias_grad)) {
+        double *wg = router_weight_grad, *bg = router_bias_grad;
+        const bool wg_host = wg && !is_device_ptr(wg), bg_host = bg && !is_device_ptr(bg);
+        if (wg_host) {
+            GT_CHECK(upload(h->bw_rw, wg, sizeof(double) * (size_t)E * d, st));
+            wg = h->bw_rw.as<double>();
+        }
+        if (bg_host) {
+            GT_CHECK(upload(h->bw_rb, bg, sizeof(double) * E, st));
+            bg = h->bw_rb.as<double>();
+        }
+        bwd_router_params_kernel<<<grid_for((int64_t)E * d, 256), 256, 0, st>>>(
+            lg, a.x, a.chosen, h->tr_perm.as<int32_t>(), h->tr_offsets.as<int64_t>(), E, d, k, wg, bg);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+        if (wg_host)
+            GT_CUDA(cudaMemcpyAsync(router_weight_grad, wg, sizeof(double) * (size_t)E * d, cudaMemcpyDeviceToHost,
+                                    st));
+        if (bg_host) GT_CUDA(cudaMemcpyAsync(router_bias_grad, bg, sizeof(double) * E, cudaMemcpyDeviceToHost, st));
+    }
+    if (dx_host) GT_CUDA(cudaMemcpyAsync(dx, dx_dev, out_bytes, cudaMemcpyDeviceToHost, st));
+    GT_CUDA(cudaStreamSynchronize(st));
+    return 0;
+}
+
+}  // extern "C"

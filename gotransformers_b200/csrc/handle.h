@@ -100,6 +100,15 @@ struct gtmoe_handle {
     double norm_eps = 0;
     int norm_set = 0;
 
+    // training (backward.cu): what gtmoe_backward needs from the last Forward
+    // (its input rows as float64, chosen experts, gates, the expert-sorted
+    // token lists) and the backward's workspace
+    int training = 0;
+    int tr_valid = 0;
+    int64_t tr_T = 0;
+    DevBuf tr_x, tr_chosen, tr_gates, tr_perm, tr_offsets;
+    DevBuf bw_in, bw_dout, bw_dx, bw_rows, bw_y, bw_lg, bw_zag, bw_rw, bw_rb;
+
     // host-buffer forwards of large batches: chunks whose copies overlap the
     // compute of their neighbours (api.cu, forward_pipelined)
     DevBuf x_pipe[2], out_pipe[2], load_acc;
@@ -136,6 +145,11 @@ int create_handle(const gtmoe_config *cfg, int device, int n_ranks, int rank, gt
 // expert parallelism (ep.cu)
 void ep_destroy(gtmoe_handle *h);
 // gtmoe_forward with the handle's lock already held
+bool is_device_ptr(const void *p);  // device or managed memory
+int upload(DevBuf &dst, const void *src, size_t bytes, cudaStream_t st);  // ensure + async copy
+// After a successful single-GPU Forward with training on: keep its state (backward.cu).
+int save_training_state(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T);
+void release_training_state(gtmoe_handle *h);
 int forward_locked(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,
                    void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm, int64_t *load);
 int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,

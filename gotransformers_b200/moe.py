@@ -262,6 +262,35 @@ class MixtureOfExperts:
             self.last_rows_for_expert = perm
         return out
 
+    # -- training
+    def set_training(self, on: bool = True):
+        """Keep, from every later forward, what backward() needs."""
+        check(_lib.lib().gtmoe_set_training(self._h, int(on)))
+
+    def backward(self, output_gradients, input_gradients=None, router_weight_grad=None, router_bias_grad=None):
+        """MixtureOfExperts.Backward (mixtureofexperts.go:227-285) of the last
+        forward: returns the input gradients (T x d, the output gradients'
+        dtype unless input_gradients is given).  router_weight_grad (E x d) and
+        router_bias_grad (E), float64, have the router's gradients added."""
+        g = output_gradients
+        if g.ndim != 2 or g.shape[1] != self.cfg.d_model:
+            raise ValueError(f"output gradients have {g.shape[-1]} values per row but the layer has {self.cfg.d_model}")
+        if input_gradients is None:
+            if isinstance(g, np.ndarray):
+                input_gradients = np.empty_like(g)
+            else:
+                import torch
+
+                input_gradients = torch.empty_like(g)
+        for a, shape in ((router_weight_grad, (self.cfg.n_routed, self.cfg.d_model)),
+                         (router_bias_grad, (self.cfg.n_routed,))):
+            if a is not None and (tuple(a.shape) != shape or _dtype_code(a) != DTYPE_F64):
+                raise ValueError(f"router gradients must be float64 of shape {shape}")
+        check(_lib.lib().gtmoe_backward(self._h, _addr(g), _dtype_code(g), _addr(input_gradients),
+                                        _dtype_code(input_gradients), _addr(router_weight_grad),
+                                        _addr(router_bias_grad)))
+        return input_gradients
+
     def last_expert_load(self) -> np.ndarray:
         out = np.empty(self.cfg.n_routed, np.int64)
         check(_lib.lib().gtmoe_last_expert_load(self._h, _addr(out)))

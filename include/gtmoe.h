@@ -119,6 +119,25 @@ GTMOE_API int gtmoe_forward_block(gtmoe_t h, const void *x, int x_dtype, int64_t
                                   void *out, int out_dtype, int32_t *chosen, double *gates, int32_t *perm,
                                   int64_t *load);
 
+/* MixtureOfExperts.Backward (mixtureofexperts.go:227-285) for the last
+ * Forward.  gtmoe_set_training(h, 1) makes every later Forward keep what the
+ * backward needs (its input rows as float64, the chosen experts, the gates
+ * and the expert-sorted token lists; a host-buffer batch then runs unchunked).
+ * gtmoe_backward takes the output gradients dout (T x d_model, the last
+ * Forward's T) and writes the input gradients dx (T x d_model); when
+ * router_weight_grad (n_routed x d_model) / router_bias_grad (n_routed) are
+ * given, the router's gradients are ADDED to them, as the reference's
+ * RouterLayer.Backward accumulates into its gradient storage
+ * (perceptron/layer.go:184-195).  The expert layers are compressed rows and
+ * take part as frozen layers (layer.go:165-167, 184: no weight gradients;
+ * input gradients through the rows, adapter.go:108-120).  Computed in float64
+ * on the GPU; the gate/up/down values are recomputed from the saved input.
+ * Hash routing: no router term (:258-260).  GTMOE_ENOTREADY without a
+ * Forward since training was switched on; one GPU (not expert parallel). */
+GTMOE_API int gtmoe_set_training(gtmoe_t h, int on);
+GTMOE_API int gtmoe_backward(gtmoe_t h, const void *dout, int dout_dtype, void *dx, int dx_dtype,
+                             double *router_weight_grad, double *router_bias_grad);
+
 /* GoTransformers binary weights files (weightfile/binaryfile.go): a saved
  * model's parameters read straight into a handle.  gtmoe_weightfile_open maps
  * the file, checks its marker (GOTRANSFORMERS-WEIGHTS-1 or -2,

@@ -324,3 +324,104 @@ def rmsnorm(x: np.ndarray, weights: np.ndarray, epsilon: float) -> np.ndarray:
         rms = math.sqrt(s / d + epsilon)
         out[t] = [v / rms * float(w) for v, w in zip(row, weights)]
     return out
+
+
+def _sigmoid(x):
+    return 1.0 / (1.0 + np.exp(-x))
+
+
+def _gate_act(x, spec):
+    """SiLU / ClampedSiLU (activationfunction.go:102-105, moreactivationfunctions.go:207-223)."""
+    if spec.clamped:
+        x = np.minimum(x, spec.clamp_limit)
+    return x * _sigmoid(x)
+
+
+def _up_act(x, spec):
+    """Linear / ClampedLinear (activationfunction.go:158-160, moreactivationfunctions.go:225-244)."""
+    return np.clip(x, -spec.clamp_limit, spec.clamp_limit) if spec.clamped else x
+
+
+def _gate_deriv(x, spec):
+    """siluDerivative s + x s (1 - s) (activationfunction.go:106-109); 0 above the clamp."""
+    s = _sigmoid(x)
+    dv = s + x * s * (1 - s)
+    return np.where(x > spec.clamp_limit, 0.0, dv) if spec.clamped else dv
+
+
+def _up_deriv(x, spec):
+    """linearDerivative 1 (activationfunction.go:162-164); 0 outside the clamp."""
+    if spec.clamped:
+        return np.where((x > spec.clamp_limit) | (x < -spec.clamp_limit), 0.0, 1.0)
+    return np.ones_like(x)
+
+
+def _layer_weights(layer: Layer):
+    w = decode_rows(layer)
+    b = np.zeros(layer.rows) if layer.bias is None else np.asarray(layer.bias, np.float64)
+    return w, b
+
+
+def _expert_backward(spec: MoESpec, expert: int, xr: np.ndarray, dy: np.ndarray):
+    """GatedFeedForward.Backward (feedforward/gatedfeedforward.go:59-66) with
+    frozen compressed layers (perceptron/layer.go:164-207: pre-activation
+    gradients g * act'(pre), input gradients through the rows).  The forward
+    values it uses (gatedfeedforward.go:49-57) are recomputed.  Returns the
+    input gradients and the expert's output rows."""
+    gate, up, down = spec.experts[expert]
+    wg, bg = _layer_weights(gate)
+    wu, bu = _layer_weights(up)
+    wd, bd = _layer_weights(down)
+    pre_g = xr @ wg.T + bg
+    pre_u = xr @ wu.T + bu
+    go, uo = _gate_act(pre_g, spec), _up_act(pre_u, spec)
+    y = (go * uo) @ wd.T + bd
+    dh = dy @ wd  # Down.Backward, linear: derivative 1
+    pg = (dh * uo) * _gate_deriv(pre_g, spec)
+    pu = (dh * go) * _up_deriv(pre_u, spec)
+    return pg @ wg + pu @ wu, y
+
+
+def moe_backward(spec: MoESpec, x: np.ndarray, dout: np.ndarray, token_ids=None) -> dict:
+    """MixtureOfExperts.Backward (mixtureofexperts.go:227-285) after Forward on
+    x, in float64 numpy, the expert layers taking part as frozen compressed
+    layers.  Returns dict(dx, router_weight_grad, router_bias_grad) -- the
+    router's gradients of this call alone (RouterLayer.Backward, layer.go:
+    184-195, adds them to its storage), None with hash routing."""
+    x = np.ascontiguousarray(x, np.float64)
+    dout = np.ascontiguousarray(dout, np.float64)
+    T, d = x.shape
+    E, k, S = spec.n_routed, spec.k, spec.n_shared
+    fwd = moe_forward(spec, x, token_ids)
+    chosen, gates = fwd["chosen"], fwd["gates"]
+    dx = np.zeros((T, d))
+    for s in range(S):  # shared experts on the unscaled output gradients (:235-237)
+        dxs, _ = _expert_backward(spec, s, x, dout)
+        dx = dx + dxs
+    ys = {}
+    for e in range(E):  # routed experts, ascending (:239-256)
+        rows = [t for t in range(T) if e in chosen[t]]
+        if not rows:
+            continue
+        slots = [int(np.nonzero(chosen[t] == e)[0][0]) for t in rows]
+        g = np.array([gates[t, i] for t, i in zip(rows, slots)])
+        dxe, y = _expert_backward(spec, S + e, x[rows], dout[rows] * g[:, None])
+        for j, t in enumerate(rows):
+            dx[t] += dxe[j]
+            ys[(t, e)] = y[j]
+    if spec.hash_routing:
+        return dict(dx=dx, router_weight_grad=None, router_bias_grad=None)
+    wr, br = _layer_weights(spec.router)
+    logits = x @ wr.T + br
+    lg = np.zeros((T, E))
+    for t in range(T):  # :262-283
+        gg = np.array([float(dout[t] @ ys[(t, e)]) for e in chosen[t]])
+        weighted = float(np.sum(gg * gates[t]))
+        aff = np.array([affinity(float(logits[t, e])) for e in chosen[t]])
+        total = float(np.sum(aff))
+        for i, e in enumerate(chosen[t]):
+            z = float(logits[t, e])
+            # affinityDerivative: softplus'(z) / (2 affinity) (:84-86)
+            lg[t, e] = (gg[i] - weighted) / total * (1.0 / (1.0 + math.exp(-z)) / (2 * aff[i]))
+    # RouterLayer.Backward, linear (layer.go:174-202)
+    return dict(dx=dx + lg @ wr, router_weight_grad=lg.T @ x, router_bias_grad=lg.sum(axis=0))
