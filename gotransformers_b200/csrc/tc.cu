@@ -91,6 +91,7 @@ constexpr int kDownPitch = 132;
 constexpr int kEpiBytes = 2 * kEpiChunk * kGatePitch * 4;  // 17408
 static_assert(kEpiChunk * kDownPitch * 4 <= kEpiBytes, "epilogue staging");
 constexpr int kPrefixCache = 2048;          // m-tile prefix entries cached in shared memory
+constexpr int kBandTiles = 16;              // m-tiles per band of the unit order (UnitDecoder)
 // instruction descriptor: D f32, A bf16, B bf16, both K-major, N = 192, M = 256 (2-SM)
 constexpr uint32_t kIdesc =
     (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileTok >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
@@ -205,11 +206,14 @@ __device__ __forceinline__ bool pair_wait(uint64_t *bar, uint32_t parity, volati
     }
 }
 
-// Work unit u -> (group, n-tile, m-tile); m-tiles innermost so that
-// neighbouring clusters share one weight tile in L2.  Each role walks its
-// units in increasing order, so the group index only moves forward: the
-// decoder keeps it and the group's record, and reads the m-tile prefix from
-// shared memory.
+// Work unit u -> (group, n-tile, m-tile).  Within a group the m-tiles run
+// in bands of kBandTiles: a band's units are n-tile major, m-tiles innermost,
+// so the clusters working at one time share each weight tile and, for a
+// large group (the shared expert sees every token), re-read each token tile
+// for the next n-tiles from L2 instead of HBM.  A group of at most
+// kBandTiles m-tiles is one band.  Each role walks its units in increasing
+// order, so the group index only moves forward: the decoder keeps it and the
+// group's record, and reads the m-tile prefix from shared memory.
 struct Unit {
     int g;
     int nt;
@@ -234,9 +238,18 @@ struct UnitDecoder {
         if (changed) grp = groups[g];
         const int64_t mt_g = prefix[g + 1] - prefix[g];
         const int64_t r = u - (int64_t)prefix[g] * n_tiles;
+        const int64_t full = mt_g / kBandTiles;  // complete bands
+        const int64_t band_units = (int64_t)kBandTiles * n_tiles;
         w.g = g;
-        w.nt = (int)(r / mt_g);
-        w.mt = r % mt_g;
+        if (r < full * band_units) {
+            const int64_t q = r % band_units;
+            w.nt = (int)(q / kBandTiles);
+            w.mt = (r / band_units) * kBandTiles + q % kBandTiles;
+        } else {
+            const int64_t rest = mt_g - full * kBandTiles, q = r - full * band_units;
+            w.nt = (int)(q / rest);
+            w.mt = full * kBandTiles + q % rest;
+        }
         return changed;
     }
 };
