@@ -255,6 +255,7 @@ int refresh_table(gtmoe_handle *h) {
 static int forward_prepare(gtmoe_handle *h, int64_t T);
 // Host-buffer batches from this many rows on are pipelined in chunks.
 constexpr int64_t kPipelineMinRows = 16384;
+constexpr int kMaxPipeChunks = 4;
 
 __global__ void add_load_kernel(int64_t *__restrict__ acc, const int64_t *__restrict__ load, int E) {
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < E; e += gridDim.x * blockDim.x) acc[e] += load[e];
@@ -271,7 +272,18 @@ static int forward_pipelined(gtmoe_handle *h, const void *x, int x_dtype, int64_
     const int d = c.d_model, k = c.experts_per_token, E = c.n_routed;
     cudaStream_t st = h->stream;
     const size_t xrow = dtype_size(x_dtype) * d, orow = dtype_size(out_dtype) * d;
-    const int64_t Tc = (T + nc - 1) / nc;
+    // chunk bounds: the first and the last chunk are the smaller ones (a
+    // quarter of the batch each for 3 chunks, an eighth for 4), since only
+    // their copies are not hidden behind another chunk's compute
+    int64_t bound[kMaxPipeChunks + 1];
+    nc = nc < 2 ? 2 : nc > kMaxPipeChunks ? kMaxPipeChunks : nc;
+    const int64_t edge = nc == 2 ? (T + 1) / 2 : T / (nc == 3 ? 4 : 8);
+    bound[0] = 0;
+    bound[nc] = T;
+    for (int ci = 1; ci < nc; ci++)
+        bound[ci] = ci == 1 ? edge : ci == nc - 1 ? T - edge : edge + (T - 2 * edge) * (ci - 1) / (nc - 2);
+    int64_t Tc = 0;
+    for (int ci = 0; ci < nc; ci++) Tc = bound[ci + 1] - bound[ci] > Tc ? bound[ci + 1] - bound[ci] : Tc;
     if (!h->h2d_stream) GT_CUDA(cudaStreamCreateWithFlags(&h->h2d_stream, cudaStreamNonBlocking));
     if (!h->d2h_stream) GT_CUDA(cudaStreamCreateWithFlags(&h->d2h_stream, cudaStreamNonBlocking));
     for (cudaEvent_t &e : h->pipe_ev)
@@ -290,9 +302,9 @@ static int forward_pipelined(gtmoe_handle *h, const void *x, int x_dtype, int64_
     GT_CUDA(cudaStreamWaitEvent(h->h2d_stream, x_free[0], 0));
     GT_CUDA(cudaStreamWaitEvent(h->d2h_stream, x_free[0], 0));
     for (int ci = 0; ci < nc; ci++) {
-        const int64_t t0 = (int64_t)ci * Tc;
-        const int64_t n = T - t0 < Tc ? T - t0 : Tc;
-        if (n <= 0) break;
+        const int64_t t0 = bound[ci];
+        const int64_t n = bound[ci + 1] - t0;
+        if (n <= 0) continue;
         const int s = ci & 1;
         if (ci >= 2) GT_CUDA(cudaStreamWaitEvent(h->h2d_stream, x_free[s], 0));
         GT_CUDA(cudaMemcpyAsync(h->x_pipe[s].p, (const char *)x + t0 * xrow, n * xrow, cudaMemcpyHostToDevice,
@@ -855,7 +867,7 @@ int forward_locked(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64
     if (pipelined) {
         h->drop_graph();
         return forward_pipelined(h, x, x_dtype, T, ids_dev, res_dev, out, out_dtype, chosen, gates, load,
-                                 T >= 4 * kPipelineMinRows ? 4 : 2);
+                                 T >= 4 * kPipelineMinRows ? 4 : 3);
     }
     // device pointers only, no host round trip inside: the forward may be replayed as a CUDA graph
     const bool graphable = !c.hash_routing && x_dev == x && out_dev == out && res_dev == residual;
