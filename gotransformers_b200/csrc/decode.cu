@@ -158,7 +158,10 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     uint32_t n = 0;      // weight steps of this CTA so far: slot = n % S, parity = (n / S) & 1
     uint32_t nu = 0;     // units of this CTA so far (token-row buffer parity)
 
-    for (int64_t u = blockIdx.x; u < units && !*abort_p; u += gridDim.x, nu++) {
+    // Every warp walks all of this CTA's units, also after an abort (its
+    // waits then return at once): the compute warps' named barrier is
+    // reached by all eight of them, whatever each one saw of the flag.
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x, nu++) {
         const int64_t tile = u / blocks;
         const int fb = (int)(u % blocks);
         const int gi = unit_group(a.tile_prefix, a.n_groups, tile);
@@ -175,6 +178,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             const uint8_t *w1 = GATED ? L.tiled[1] + (int64_t)(2 * nt + half) * KB * DL::kHalf : nullptr;
             const uint8_t *xrow0 = (const uint8_t *)(xin + ((GATED ? grp.x_row0 : grp.h_row0) + r0) * (int64_t)K);
             if (nu > 0 && !*abort_p) mbar_wait(&xempty, (nu - 1) & 1, abort_p, a.err, 13);
+            if (*abort_p) continue;  // no new copies once a wait has given up
             if (lane == 0) mbar_arrive_expect_tx(&xfull, (uint32_t)m * K * 2);
             __syncwarp();
             for (int r = lane; r < m; r += 32) bulk_copy(xs + r * xpitch, xrow0 + (int64_t)r * K * 2, K * 2, &xfull);
@@ -293,8 +297,13 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             *reinterpret_cast<uint32_t *>(out + (grp.h_row0 + r0 + t) * (int64_t)n_out + f) = pack_bf16(v0, v1);
         }
     }
-    // every copy the producer issued was waited for by the compute warps
-    // (or a wait gave up), so no copy lands after the CTA has exited
+    // every copy the producer issued was waited for by the compute warps;
+    // after an abort some may not have been: let them land before the CTA exits
+    if (warp == kComputeWarps && *abort_p) {
+        const uint64_t t0 = global_timer_ns();
+        while (global_timer_ns() - t0 < 1000000ull) {
+        }
+    }
 }
 
 template <int PREC, bool GATED>
