@@ -417,8 +417,9 @@ def l2_note(cfg) -> str:
 
 def profiled_traffic(kernel: str, config: str, T_local: int):
     """DRAM bytes per launch of `kernel` from the committed ncu summary
-    (profiles/traffic.json), scaled by tokens when captured on a smaller
-    case; None when no capture exists."""
+    (profiles/traffic.json) when it was captured on this run's token count;
+    None otherwise (no capture, or an expert-parallel rank, whose launches
+    hold other rows than a single-GPU run's)."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(path):
         return None
@@ -427,7 +428,9 @@ def profiled_traffic(kernel: str, config: str, T_local: int):
     ent = j.get(f"{kernel}:{config}")
     if not ent:
         return None
-    return int(ent["bytes_per_launch"] * T_local / ent["tokens"])
+    if int(ent["tokens"]) != int(T_local):
+        return None
+    return int(ent["bytes_per_launch"])
 
 
 def run_reference(args, cfg, rank, world, local_rank, metric):
