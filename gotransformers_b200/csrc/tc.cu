@@ -142,12 +142,15 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
-// The eight MMAs of one step (K = 128): A columns a_tmem + 8k, B k-blocks at
-// bdesc (inputs 0-63) and bdesc + kBSubBytes (64-127), 32 bytes of K per MMA
-// (+2 in the descriptor's 16-byte address units).  Only the first may start
-// a fresh accumulation.
-__device__ __forceinline__ void umma2_ts_step(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, bool accumulate) {
-    constexpr uint64_t kSub = kBSubBytes >> 4;
+// Half of the MMAs of one step (K = 128; half 0: inputs 0-63, half 1:
+// 64-127): A columns a_tmem + 8k, B k-blocks at bdesc (inputs 0-63) and
+// bdesc + kBSubBytes (64-127), 32 bytes of K per MMA (+2 in the descriptor's
+// 16-byte address units).  Only the step's first MMA may start a fresh
+// accumulation.
+template <int HALF>
+__device__ __forceinline__ void umma2_ts_half(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, bool accumulate) {
+    constexpr uint64_t kSub = HALF ? (kBSubBytes >> 4) : 0;
+    const uint32_t a0 = a_tmem + HALF * 32;
     asm volatile(
         "{\n\t.reg .pred p, t;\n\t"
         "setp.ne.b32 p, %10, 0;\n\t"
@@ -156,17 +159,8 @@ __device__ __forceinline__ void umma2_ts_step(uint32_t d_tmem, uint32_t a_tmem, 
         "tcgen05.mma.cta_group::2.kind::f16 [%0], [%3], %4, %9, t;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %6, %9, t;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %8, %9, t;\n\t}\n" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(a_tmem + 8), "l"(bdesc + 2), "r"(a_tmem + 16), "l"(bdesc + 4), "r"(a_tmem + 24),
-        "l"(bdesc + 6), "r"(kIdesc), "r"((uint32_t)accumulate));
-    asm volatile(
-        "{\n\t.reg .pred t;\n\t"
-        "setp.eq.b32 t, 0, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %9, t;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%3], %4, %9, t;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %6, %9, t;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %8, %9, t;\n\t}\n" ::"r"(d_tmem),
-        "r"(a_tmem + 32), "l"(bdesc + kSub), "r"(a_tmem + 40), "l"(bdesc + kSub + 2), "r"(a_tmem + 48),
-        "l"(bdesc + kSub + 4), "r"(a_tmem + 56), "l"(bdesc + kSub + 6), "r"(kIdesc));
+        "r"(a0), "l"(bdesc + kSub), "r"(a0 + 8), "l"(bdesc + kSub + 2), "r"(a0 + 16), "l"(bdesc + kSub + 4),
+        "r"(a0 + 24), "l"(bdesc + kSub + 6), "r"(kIdesc), "r"((uint32_t)(HALF || accumulate)));
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory"); }
@@ -420,15 +414,22 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kAccCols);
                 bool ok = true;
+                bool seen = false;  // this step's barrier was already seen complete by the probe below
                 for (int s = 0; s < KS; s++, j++) {
                     const int sb = (int)(j % SB);
-                    if (!pair_wait<false>(&full[sb], (j / SB) & 1, abort_flag, peer_abort, a.err, 3)) {
+                    if (!seen && !pair_wait<false>(&full[sb], (j / SB) & 1, abort_flag, peer_abort, a.err, 3)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    umma2_ts_step(d_tmem, tmem_base + (uint32_t)(kRingCol + (j & 1) * kAStageCols),
-                                  sw128_desc(smem_u32(b_tiles + sb * kBStageBytes)), s != 0);
+                    const uint32_t a_tmem = tmem_base + (uint32_t)(kRingCol + (j & 1) * kAStageCols);
+                    const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + sb * kBStageBytes));
+                    umma2_ts_half<0>(d_tmem, a_tmem, bdesc, s != 0);
+                    // probe the next step's barrier between the two halves, so that its
+                    // latency overlaps the MMA issue (that phase cannot complete twice
+                    // before the next step's MMAs are issued)
+                    seen = s + 1 < KS && mbar_try_wait(&full[(j + 1) % SB], ((j + 1) / SB) & 1);
+                    umma2_ts_half<1>(d_tmem, a_tmem, bdesc, true);
                     umma2_commit_mc(&b_empty[sb], 0x3);
                 }
                 if (!ok) break;
