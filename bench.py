@@ -48,7 +48,13 @@ def parse_args():
     p.add_argument("--config", default="c5")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--mode", default="auto", choices=["auto", "ep", "replicas"],
-                   help="multi-GPU mode: expert parallel (NCCL all-to-all) or token-sharded replicas")
+                   help="multi-GPU mode: expert parallel (routed experts sharded by index; token rows exchanged "
+                        "by peer stores over NVLink, per-expert counts by an NCCL all-gather) or token-sharded "
+                        "replicas of the whole layer")
+    p.add_argument("--replicas", default="auto",
+                   help="expert parallel: hot experts held on every rank ('auto': chosen from the config's expected "
+                        "expert popularity, '0': none -- routed experts purely owned by index, or a number: the "
+                        "hottest experts chosen the same way, at most that many)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     return p.parse_args()
@@ -209,6 +215,9 @@ def main():
         dist.broadcast_object_list(obj, src=0)
         moe = M.MixtureOfExperts(cfg.d, cfg.h, cfg.n_shared, cfg.n_routed, cfg.k, weight_precision=cfg.precision,
                                  device=local_rank, ep_ranks=world, ep_rank=rank, nccl_id=obj[0])
+        reps = bench_replicas(args, cfg, world)
+        if reps:
+            moe.set_replicas(reps)
     else:
         moe = M.MixtureOfExperts(cfg.d, cfg.h, cfg.n_shared, cfg.n_routed, cfg.k, weight_precision=cfg.precision,
                                  device=local_rank)
@@ -306,15 +315,26 @@ def main():
 
     # expert rows this rank ran: its tokens through the shared experts plus the
     # rows routed to the experts it owns
+    sent_bytes = recv_bytes = 0
     if world > 1 and mode == "ep":
-        # each rank's load counts its own tokens; the owned experts' rows come from all ranks
-        load = torch.from_numpy(moe.last_expert_load()).to(dev)
+        # each rank's load counts its own tokens; an owned expert's rows come
+        # from all ranks, a replicated expert's only from this rank's tokens
+        own = moe.last_expert_load()
+        load = torch.from_numpy(own).to(dev)
         dist.all_reduce(load)
+        glob = load.cpu().numpy()
         el = cfg.n_routed // world
-        my_rows = cfg.n_shared * T_local + int(load[rank * el:(rank + 1) * el].sum())
+        rep = set(getattr(moe, "replicas", ()))
+        mine = [e for e in range(rank * el, (rank + 1) * el) if e not in rep]
+        my_rows = cfg.n_shared * T_local + int(glob[mine].sum()) + int(sum(own[e] for e in rep))
+        # token rows (and the same number of output rows back) that crossed NVLink
+        row_b = cfg.d * 2
+        sent_bytes = row_b * int(sum(own[e] for e in range(cfg.n_routed) if e not in rep and e // el != rank))
+        recv_bytes = row_b * int(sum(glob[e] - own[e] for e in mine))
     else:
         my_rows = (cfg.n_shared + cfg.k) * T_local
-    per_rank = [[ms, e2e_ms, float(my_rows)] + [phases[n] for n in _lib.PHASES]]
+    per_rank = [[ms, e2e_ms, float(my_rows), float(sent_bytes), float(recv_bytes)] + [phases[n] for n in _lib.PHASES]]
+    NP = 5  # per-rank values before the phases
     if world > 1:
         t = torch.tensor(per_rank[0], dtype=torch.float64, device=dev)
         allv = [torch.empty_like(t) for _ in range(world)]
@@ -322,12 +342,12 @@ def main():
         per_rank = [v.tolist() for v in allv]
         ms = max(v[0] for v in per_rank)
         e2e_ms = max(v[1] for v in per_rank)
-        phases = {n: max(v[3 + i] for v in per_rank) for i, n in enumerate(_lib.PHASES)}
+        phases = {n: max(v[NP + i] for v in per_rank) for i, n in enumerate(_lib.PHASES)}
 
     peaks = measured_peaks()
     # dominant kernel: the grouped gate/up GEMM (2/3 of the expert FLOPs and
     # weight bytes), on the rank where it took longest, with its own rows
-    ig, idn = 3 + _lib.PHASES.index("expert_gate_up"), 3 + _lib.PHASES.index("expert_down")
+    ig, idn = NP + _lib.PHASES.index("expert_gate_up"), NP + _lib.PHASES.index("expert_down")
     kname, col = max((("expert_gate_up", ig), ("expert_down", idn)), key=lambda kv: phases[kv[0]])
     slow = max(per_rank, key=lambda v: v[col])
     kms, rows = slow[col], slow[2]
@@ -372,20 +392,15 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 activations, N(0,1/fan_in) weights quantised by the reference "
                     "quantiser, Zipf router bias)",
-            "config": {"workload": f"BASELINE {cfg.name}: {cfg.T} tokens x d {cfg.d}, {cfg.n_routed} routed + "
-                                   f"{cfg.n_shared} shared SwiGLU experts (hidden {cfg.h}), top-{cfg.k}, "
-                                   f"{['Float64', 'Float32', 'Int8', 'FP4'][cfg.precision]} experts",
-                       "tokens": cfg.T, "d_model": cfg.d, "hidden": cfg.h, "n_routed": cfg.n_routed,
-                       "n_shared": cfg.n_shared, "top_k": cfg.k,
-                       "parallelism": f"{mode}{world}" if world > 1 else "single",
-                       "l2": l2_note(cfg)},
+            "config": workload_config(cfg, world, mode, getattr(moe, "replicas", [])),
             "e2e": {"value": round(T_total / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(T_local * cfg.d * 2), "d2h_bytes_per_step": int(T_local * cfg.d * 2)},
             "roofline": roofline,
             "cpu_baseline": cpu_baseline,
             "phases_ms": {k: round(v, 4) for k, v in phases.items()},
-            **({"ranks": [{"ms": round(v[0], 4), "expert_rows": int(v[2]),
-                           "phases_ms": {n: round(v[3 + i], 4) for i, n in enumerate(_lib.PHASES)}}
+            **({"ranks": [{"ms": round(v[0], 4), "expert_rows": int(v[2]), "push_bytes": int(v[3]),
+                           "received_bytes": int(v[4]), "return_bytes": int(v[4]),
+                           "phases_ms": {n: round(v[NP + i], 4) for i, n in enumerate(_lib.PHASES)}}
                           for v in per_rank]} if world > 1 else {}),
             "gpu_launches": int(launches.value),
             "clocks": clocks,
@@ -395,6 +410,30 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def bench_replicas(args, cfg, world: int) -> list:
+    """Hot experts held on every expert-parallel rank (--replicas)."""
+    from gotransformers_b200 import synthetic
+
+    if world < 2 or args.replicas == "0" or args.mode == "replicas":
+        return []
+    cap = 16 if args.replicas == "auto" else int(args.replicas)
+    return synthetic.choose_replicas(cfg, world, max_replicas=cap)
+
+
+def workload_config(cfg, world: int, mode: str, replicas=()) -> dict:
+    """The `config` object of both arms' JSON lines."""
+    prec = ["Float64", "Float32", "Int8", "FP4"][cfg.precision]
+    return {"workload": f"{cfg.name}: {cfg.T} tokens x d {cfg.d}, {cfg.n_routed} routed + {cfg.n_shared} shared "
+                        f"SwiGLU experts (hidden {cfg.h}), top-{cfg.k}, {prec} experts, "
+                        f"{'bf16' if cfg.x_bf16 else 'float64'} activations",
+            "tokens": cfg.T, "d_model": cfg.d, "hidden": cfg.h, "n_routed": cfg.n_routed,
+            "n_shared": cfg.n_shared, "top_k": cfg.k, "precision": prec,
+            "parallelism": (f"{mode}{world}" + (f" + {len(replicas)} hot-expert replicas" if replicas else "")
+                            if world > 1 else "single"),
+            **({"replicated_experts": list(replicas)} if replicas else {}),
+            "l2": l2_note(cfg)}
 
 
 def decode_shaped(cfg) -> bool:
@@ -433,55 +472,77 @@ def profiled_traffic(kernel: str, config: str, T_local: int):
     return int(ent["bytes_per_launch"])
 
 
+def host_spec_and_sample(cfg, n_tokens: int, threads: int, seed: int = 7):
+    """The config's router and expert weights made on the host by the
+    oracle's restatement of the seeded generator and the reference quantiser
+    (no GPU library), and the activations of a seeded sample of n_tokens
+    tokens.  Returns (spec, x_sample float64, token indices)."""
+    from gotransformers_b200 import synthetic
+    from oracle import oracle as O
+
+    E, S, d, h = cfg.n_routed, cfg.n_shared, cfg.d, cfg.h
+    rb = synthetic.zipf_router_bias(E, cfg.k, cfg.zipf_s, cfg.weight_seed) if cfg.zipf_s else np.zeros(E)
+    wr = O.synth_rows(O.FLOAT64, E, d, cfg.weight_seed, synthetic.STREAM_ROUTER, 1.0 / np.sqrt(d), threads)
+    router = O.Layer(O.FLOAT64, E, d, wr.values, None, np.ascontiguousarray(rb, np.float64))
+    experts = []
+    for e in range(S + E):
+        experts.append(tuple(
+            O.synth_rows(cfg.precision, rows, width, cfg.weight_seed, synthetic.expert_stream(e, which),
+                         1.0 / np.sqrt(width), threads)
+            for which, (rows, width) in enumerate([(h, d), (h, d), (d, h)])))
+    spec = O.MoESpec(d=d, h=h, n_shared=S, n_routed=E, k=cfg.k, router=router, experts=experts)
+    rng = np.random.default_rng(seed)
+    tokens = np.sort(rng.choice(cfg.T, size=min(n_tokens, cfg.T), replace=False))
+    x = np.stack([synthetic.normal(cfg.act_seed, synthetic.STREAM_X, d, offset=int(t) * d) for t in tokens])
+    if cfg.x_bf16:
+        x = synthetic.bf16_round(x)
+    return spec, np.ascontiguousarray(x), tokens
+
+
 def run_reference(args, cfg, rank, world, local_rank, metric):
     """The reference's CPU algorithm (the C float64 oracle port; the Go
-    reference has no toolchain here) on the host cores, rank 0 only.  Inputs
-    are the same seeded weights and activations as the GPU arm, generated with
-    the library's GPU generator and quantiser (input preparation only, not
-    timed)."""
+    reference has no toolchain here) on all host cores, rank 0 only, on the
+    same config as the GPU arm.  Its inputs are made on the host by the
+    oracle (seeded generator + reference quantiser); neither the GPU library
+    nor the GPU is used.  Each step runs a bounded seeded token sample (row
+    independence, mixtureofexperts_test.go:83-100, makes a sample valid)."""
     if rank != 0:
         return
-    import torch
-
-    from gotransformers_b200 import moe as M
-    from gotransformers_b200 import synthetic
-
-    torch.cuda.set_device(local_rank)
-    moe = M.MixtureOfExperts(cfg.d, cfg.h, cfg.n_shared, cfg.n_routed, cfg.k, weight_precision=cfg.precision,
-                             device=local_rank)
-    host = synthetic.load_config_on_gpu(cfg, moe, keep_host=True, device=local_rank)
-    x = synthetic.make_x_on_gpu(cfg, device=local_rank).to(torch.float64).cpu().numpy()
-    moe.close()
-    spec = oracle_spec(cfg, host)
     from oracle import oracle as O
 
     threads = os.cpu_count() or 1
-    rng = np.random.default_rng(7)
-    # size each step for ~ (a few minutes / steps)
-    probe = np.sort(rng.choice(cfg.T, size=2, replace=False))
     t0 = time.perf_counter()
-    O.moe_forward(spec, x[probe], probe.astype(np.int64), threads=threads)
+    spec, x_all, tokens = host_spec_and_sample(cfg, min(cfg.T, 4096), threads)
+    prep_s = time.perf_counter() - t0
+    # size each step for ~ (two minutes / steps)
+    t0 = time.perf_counter()
+    O.moe_forward(spec, x_all[:2], tokens[:2].astype(np.int64), threads=threads)
     per_tok = max((time.perf_counter() - t0) / 2, 1e-6)
     budget = 120.0 / max(args.steps + args.warmup, 1)
-    n = int(min(cfg.T, max(2, budget / per_tok)))
-    sample = np.sort(rng.choice(cfg.T, size=n, replace=False))
+    n = int(min(len(tokens), max(2, budget / per_tok)))
+    xs, ids = x_all[:n], tokens[:n].astype(np.int64)
     for _ in range(args.warmup):
-        O.moe_forward(spec, x[sample], sample.astype(np.int64), threads=threads)
+        O.moe_forward(spec, xs, ids, threads=threads)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        O.moe_forward(spec, x[sample], sample.astype(np.int64), threads=threads)
+        O.moe_forward(spec, xs, ids, threads=threads)
         times.append(time.perf_counter() - t0)
     ms = 1e3 * sum(times) / len(times)
     value = n / (ms * 1e-3)
+    mode = args.mode if args.mode != "auto" else ("ep" if world > 1 else "replicas")
+    config = workload_config(cfg, world, mode, bench_replicas(args, cfg, world) if mode == "ep" else [])
+    config["sample_tokens"] = n
     line = {
         "impl": "reference", "metric": metric, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"BASELINE {cfg.name}", "tokens_per_step": n},
+        "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (the GPU arm's seeded generator and reference quantiser, run on the host by the oracle)",
+        "config": config,
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{n} seeded tokens of {cfg.name} per step; C float64 restatement of the "
-                                   f"reference CPU path (no Go toolchain on this image)"},
+                                   f"reference CPU path (no Go toolchain on this image); inputs made on the host "
+                                   f"in {prep_s:.0f} s (not timed)"},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -38,6 +38,7 @@ EXPORTS = [
     "gtmoe_create",
     "gtmoe_ep_unique_id",
     "gtmoe_create_ep",
+    "gtmoe_ep_set_replicas",
     "gtmoe_destroy",
     "gtmoe_set_stream",
     "gtmoe_set_graphs",
@@ -111,6 +112,7 @@ def lib():
             L.gtmoe_create.argtypes = [ctypes.POINTER(Config), i32, ctypes.POINTER(vp)]
             L.gtmoe_ep_unique_id.argtypes = [vp]
             L.gtmoe_create_ep.argtypes = [ctypes.POINTER(Config), i32, i32, i32, vp, ctypes.POINTER(vp)]
+            L.gtmoe_ep_set_replicas.argtypes = [vp, i32, vp]
             L.gtmoe_destroy.argtypes = [vp]
             L.gtmoe_destroy.restype = None
             L.gtmoe_set_stream.argtypes = [vp, vp]

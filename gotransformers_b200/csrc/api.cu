@@ -85,9 +85,8 @@ int gtmoe_handle::phase_end(int p) {
 namespace gtmoe {
 
 int layer_index(const gtmoe_handle *h, int kind, int index, int which) {
-    int S = h->cfg.n_shared;
     if (kind == GTMOE_SHARED) return 3 * index + which;
-    return 3 * (S + index - h->e_begin) + which;
+    return 3 * h->slot_of[index] + which;
 }
 
 static int validate_config(const gtmoe_config *c) {
@@ -149,6 +148,18 @@ int create_handle(const gtmoe_config *cfg, int device, int n_ranks, int rank, gt
     h->e_local = cfg->n_routed / n_ranks;
     h->e_begin = rank * h->e_local;
     h->layers.resize((size_t)3 * (cfg->n_shared + h->e_local));
+    h->slot_of.assign(cfg->n_routed, -1);
+    h->routed_of_slot.assign(cfg->n_shared + h->e_local, -1);
+    h->replicated.assign(cfg->n_routed, 0);
+    for (int i = 0; i < h->e_local; i++) {
+        h->slot_of[h->e_begin + i] = cfg->n_shared + i;
+        h->routed_of_slot[cfg->n_shared + i] = h->e_begin + i;
+    }
+    // test switches, read once per handle: GTMOE_DISABLE_TC sends every batch
+    // to the SIMT kernels and the float32 router, GTMOE_DISABLE_DECODE sends
+    // small batches to the prefill kernels (the parity tests compare paths)
+    h->no_tc = getenv("GTMOE_DISABLE_TC") != nullptr;
+    h->no_decode = getenv("GTMOE_DISABLE_DECODE") != nullptr;
     h->h_bal.assign(cfg->n_routed, 0.0);
     cudaError_t e = cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
@@ -225,7 +236,7 @@ static int all_layers_set(const gtmoe_handle *h) {
             int e = (int)(i / 3);
             const char *which = (i % 3 == 0) ? "gate" : (i % 3 == 1) ? "up" : "down";
             if (e < S) return fail(GTMOE_ENOTREADY, "shared expert %d %s layer is not set", e, which);
-            return fail(GTMOE_ENOTREADY, "routed expert %d %s layer is not set", e - S + h->e_begin, which);
+            return fail(GTMOE_ENOTREADY, "routed expert %d %s layer is not set", h->routed_of_slot[e], which);
         }
     if (!h->cfg.hash_routing && !h->router_set) return fail(GTMOE_ENOTREADY, "router weights are not set");
     return 0;
@@ -233,7 +244,7 @@ static int all_layers_set(const gtmoe_handle *h) {
 
 int refresh_table(gtmoe_handle *h) {
     if (!h->table_dirty) return 0;
-    int n = h->cfg.n_shared + h->e_local;
+    int n = (int)(h->layers.size() / 3);
     std::vector<ExpertLayers> t(n);
     for (int e = 0; e < n; e++)
         for (int w = 0; w < 3; w++) {
@@ -378,7 +389,7 @@ static std::vector<uint64_t> graph_key(gtmoe_handle *h, const void *x, int x_dty
     memcpy(&wbits, &h->wmax, sizeof(wbits));
     const bool use_tc = tc_supported(h, T);
     const bool use_decode = use_tc && decode_usable(h->cfg.weight_precision, h->cfg.d_model, h->cfg.hidden, T) &&
-                            !getenv("GTMOE_DISABLE_DECODE");
+                            !h->no_decode;
     std::vector<uint64_t> k = {(uint64_t)(uintptr_t)x, (uint64_t)x_dtype, (uint64_t)T, (uint64_t)(uintptr_t)res,
                                (uint64_t)(uintptr_t)out, (uint64_t)out_dtype, (uint64_t)(uintptr_t)h->stream, wbits,
                                (uint64_t)h->e_pad, (uint64_t)use_tc, (uint64_t)use_decode,
@@ -447,7 +458,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     const bool use_tc = tc_supported(h, T);
     // few rows per expert: stream the weights (decode.cu) instead of 256-row tiles
     const bool use_decode =
-        use_tc && decode_usable(c.weight_precision, d, hd, T) && !getenv("GTMOE_DISABLE_DECODE");
+        use_tc && decode_usable(c.weight_precision, d, hd, T) && !h->no_decode;
     const int compute = c.weight_precision == GTMOE_FLOAT64 ? GTMOE_DTYPE_F64
                         : use_tc                            ? GTMOE_DTYPE_BF16
                                                             : GTMOE_DTYPE_F32;
@@ -471,7 +482,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     ra.w64 = h->wr64.as<double>();
     ra.bias = h->br.as<double>();
     ra.balance = h->bal.as<double>();
-    ra.use_tc = !c.hash_routing && h->wr3.p && router_tc_usable(x_dev, x_dtype, T, d);
+    ra.use_tc = !c.hash_routing && h->wr3.p && !h->no_tc && router_tc_usable(x_dev, x_dtype, T, d);
     ra.thresh_scale = (ra.use_tc ? kRouterTcErr : kRouterSimtErr) * h->wmax;
     ra.w3 = h->wr3.p;
     ra.e_pad = h->e_pad;
@@ -742,9 +753,9 @@ int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, int precis
     } else if (kind == GTMOE_ROUTED) {
         if (index < 0 || index >= c.n_routed)
             return fail(GTMOE_EINVAL, "routed expert %d does not exist (%d routed)", index, c.n_routed);
-        if (index < h->e_begin || index >= h->e_begin + h->e_local)
-            return fail(GTMOE_EINVAL, "routed expert %d is not owned by rank %d (owns %d..%d)", index, h->rank,
-                        h->e_begin, h->e_begin + h->e_local - 1);
+        if (h->slot_of[index] < 0)
+            return fail(GTMOE_EINVAL, "routed expert %d is not owned by rank %d (owns %d..%d) nor replicated on it",
+                        index, h->rank, h->e_begin, h->e_begin + h->e_local - 1);
     } else {
         return fail(GTMOE_EINVAL, "kind must be GTMOE_SHARED or GTMOE_ROUTED, got %d", kind);
     }

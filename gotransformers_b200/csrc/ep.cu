@@ -19,6 +19,13 @@
 //   5. the return kernel copies every output row straight into its token's
 //      rank, at the (token, slot) position, where combine.cu adds them in the
 //      reference's order.
+// Hot-expert replicas (gtmoe_ep_set_replicas, opt-in): a routed expert that
+// every rank holds is computed on each token's own rank, like the shared
+// experts -- its rows are copied into this rank's own GEMM input and its
+// outputs stored into this rank's own return buffer, and never cross NVLink.
+// Under a skewed router (a few experts chosen by nearly every token) this
+// takes the hottest experts' rows off the ranks that own them.  Every other
+// routed expert stays owned by index.
 // A kernel that pushed rows fences them (system scope) and then increments
 // an arrival counter on every rank, once per CTA; the receiver's wait kernel
 // spins (bounded) until all G sources' CTAs of this step have arrived.
@@ -129,12 +136,13 @@ __device__ __forceinline__ void signal_ranks(const PeerSigs &sig, int G, int whi
     }
 }
 
-// Rows of this rank's (token, slot) pairs, in dispatch order, to the owning
-// ranks; then (copy_shared) all T token rows to this rank's own buffer after
-// its received rows, for the shared experts.
+// Rows of this rank's (token, slot) pairs, in dispatch order, to the ranks
+// that compute them (dst_base[e] = (rank << 48) | first row of this rank's
+// rows of expert e there); then (copy_shared) all T token rows to this rank's
+// own buffer after its received rows, for the shared experts.
 __global__ void __launch_bounds__(kPushThreads) ep_push_kernel(
     const uint4 *__restrict__ x, int vec_per_row, const int32_t *__restrict__ perm, int64_t TK,
-    const int64_t *__restrict__ offsets, int E, int El, const int64_t *__restrict__ dst_base, int64_t T,
+    const int64_t *__restrict__ offsets, int E, const int64_t *__restrict__ dst_base, int64_t T,
     int copy_shared, int64_t shared_row0, int rank, const __grid_constant__ PeerRows rows,
     const __grid_constant__ PeerSigs sig, int G, unsigned int *done) {
     extern __shared__ int64_t off_s[];  // E + 1 exclusive prefix of this rank's per-expert counts
@@ -151,8 +159,9 @@ __global__ void __launch_bounds__(kPushThreads) ep_push_kernel(
                 if (off_s[mid] <= w) lo = mid;
                 else hi = mid;
             }
-            const int q = lo / El;
-            const int64_t dst = dst_base[lo] + (w - off_s[lo]);
+            const int64_t code = dst_base[lo];
+            const int q = (int)(code >> 48);
+            const int64_t dst = (code & 0xFFFFFFFFFFFFll) + (w - off_s[lo]);
             copy_row((uint4 *)rows.p[q] + dst * vec_per_row, x + (int64_t)perm[w] * vec_per_row, vec_per_row, lane);
         } else {
             const int64_t t = w - TK;
@@ -500,7 +509,7 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     ra.w64 = h->wr64.as<double>();
     ra.bias = h->br.as<double>();
     ra.balance = h->bal.as<double>();
-    ra.use_tc = !c.hash_routing && h->wr3.p && router_tc_usable(x_dev, x_dtype, T, d);
+    ra.use_tc = !c.hash_routing && h->wr3.p && !h->no_tc && router_tc_usable(x_dev, x_dtype, T, d);
     ra.thresh_scale = (ra.use_tc ? kRouterTcErr : kRouterSimtErr) * h->wmax;
     ra.w3 = h->wr3.p;
     ra.e_pad = h->e_pad;
@@ -550,13 +559,25 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     for (int s = 0; s < G; s++)
         if (Tof(s) < 0)
             return fail(GTMOE_EINVAL, "expert-parallel rank %d refused its Forward arguments; no rank ran this step", s);
-    // eoff[e]: first row of expert e in its owner's received block (expert-major)
-    std::vector<int64_t> eoff(E, 0), n_recv(G, 0);
+    // Rows of expert e that rank q computes: a replicated expert's rows of
+    // q's own tokens, an owned expert's rows from every rank, else none.
+    const std::vector<char> &rep = h->replicated;
+    auto held_rows = [&](int q, int e) -> int64_t {
+        if (rep[e]) return L(q, e);
+        if (e / El != q) return 0;
+        int64_t n = 0;
+        for (int s = 0; s < G; s++) n += L(s, e);
+        return n;
+    };
+    auto held = [&](int q, int e) { return rep[e] || e / El == q; };
+    // eoff[q*E + e]: first row of expert e in rank q's GEMM input (expert-major,
+    // experts ascending, sources ascending inside an expert)
+    std::vector<int64_t> eoff((size_t)G * E, 0), n_recv(G, 0);
     for (int q = 0; q < G; q++) {
         int64_t run = 0;
-        for (int e = q * El; e < (q + 1) * El; e++) {
-            eoff[e] = run;
-            for (int s = 0; s < G; s++) run += L(s, e);
+        for (int e = 0; e < E; e++) {
+            eoff[(size_t)q * E + e] = run;
+            run += held_rows(q, e);
         }
         n_recv[q] = run;
     }
@@ -567,46 +588,50 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     }
     GT_CHECK(ep_ensure_buffers(h, ep, need_x, need_y));
 
-    // where this rank's rows for expert e start in the owner's block
+    // where this rank's rows for expert e go: (rank << 48) | first row there
     std::vector<int64_t> dst_base(E);
     for (int e = 0; e < E; e++) {
-        int64_t b = eoff[e];
-        for (int s = 0; s < r; s++) b += L(s, e);
-        dst_base[e] = b;
+        const int q = rep[e] ? r : e / El;
+        int64_t b = eoff[(size_t)q * E + e];
+        if (!rep[e])
+            for (int s = 0; s < r; s++) b += L(s, e);
+        dst_base[e] = ((int64_t)q << 48) | b;
     }
-    // this rank's group table: owned experts on the received rows, shared
-    // experts on its own tokens (after the received rows)
+    // this rank's group table: shared experts on its own tokens (after the
+    // received rows), then every expert it holds, ascending
     const int64_t nr = n_recv[r];
     const int64_t rows_x = nr + (S > 0 ? T : 0);
     const int64_t rows_h = (int64_t)S * T + nr;
-    std::vector<Group> groups(S + El);
-    std::vector<int64_t> prefix(S + El + 1, 0);
+    std::vector<Group> groups;
     const int bm = use_tc ? tc_tile_rows(h->tc) : kSimtBM;
-    for (int s = 0; s < S; s++) groups[s] = Group{nr, (int64_t)s * T, T, s, 0};
-    std::vector<int64_t> tot(El, 0);
-    for (int el = 0; el < El; el++) {
-        for (int s = 0; s < G; s++) tot[el] += L(s, r * El + el);
-        groups[S + el] = Group{eoff[r * El + el], (int64_t)S * T + eoff[r * El + el], tot[el], S + el, 0};
-    }
-    for (int g = 0; g < S + El; g++) prefix[g + 1] = prefix[g] + (groups[g].m + bm - 1) / bm;
-    // output rows back: (owned expert, source) runs to the source's (token, slot) positions
+    for (int s = 0; s < S; s++) groups.push_back(Group{nr, (int64_t)s * T, T, s, 0});
+    for (int e = 0; e < E; e++)
+        if (held(r, e)) {
+            const int64_t o = eoff[(size_t)r * E + e];
+            groups.push_back(Group{o, (int64_t)S * T + o, held_rows(r, e), h->slot_of[e], 0});
+        }
+    const int n_groups = (int)groups.size();
+    std::vector<int64_t> prefix(n_groups + 1, 0);
+    for (int g = 0; g < n_groups; g++) prefix[g + 1] = prefix[g] + (groups[g].m + bm - 1) / bm;
+    // output rows back: (held expert, source) runs to the source's (token,
+    // slot) positions, which follow the source's dispatch order
+    std::vector<int64_t> slot0((size_t)G * E, 0);  // exclusive prefix of each rank's counts
+    for (int s = 0; s < G; s++)
+        for (int e = 1; e < E; e++) slot0[(size_t)s * E + e] = slot0[(size_t)s * E + e - 1] + L(s, e - 1);
     std::vector<RetSeg> back;
-    for (int el = 0; el < El; el++) {
-        const int e = r * El + el;
-        int64_t src = (int64_t)S * T + eoff[e];
+    for (int e = 0; e < E; e++) {
+        if (!held(r, e)) continue;
+        int64_t src = (int64_t)S * T + eoff[(size_t)r * E + e];
         for (int s = 0; s < G; s++) {
+            if (rep[e] && s != r) continue;
             const int64_t n = L(s, e);
-            if (n > 0) {
-                int64_t slot = 0;  // exclusive prefix of rank s's counts
-                for (int e2 = 0; e2 < e; e2++) slot += L(s, e2);
-                back.push_back(RetSeg{src, slot, n, s});
-            }
+            if (n > 0) back.push_back(RetSeg{src, slot0[(size_t)s * E + e], n, s});
             src += n;
         }
     }
     GT_CUDA(cudaMemcpyAsync(ep->dst_base.p, dst_base.data(), sizeof(int64_t) * E, cudaMemcpyHostToDevice, st));
-    GT_CUDA(cudaMemcpyAsync(h->groups.p, groups.data(), sizeof(Group) * (S + El), cudaMemcpyHostToDevice, st));
-    GT_CUDA(cudaMemcpyAsync(h->tile_prefix.p, prefix.data(), sizeof(int64_t) * (S + El + 1), cudaMemcpyHostToDevice,
+    GT_CUDA(cudaMemcpyAsync(h->groups.p, groups.data(), sizeof(Group) * n_groups, cudaMemcpyHostToDevice, st));
+    GT_CUDA(cudaMemcpyAsync(h->tile_prefix.p, prefix.data(), sizeof(int64_t) * (n_groups + 1), cudaMemcpyHostToDevice,
                             st));
     if (!back.empty()) {
         GT_CHECK(ep->ret_segs.ensure(sizeof(RetSeg) * back.size()));
@@ -630,8 +655,8 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     ep->epoch++;
     const unsigned long long arrivals = ep->epoch * (unsigned long long)G;  // one per source rank and step
     ep_push_kernel<<<kPushCtas, kPushThreads, sizeof(int64_t) * (E + 1), st>>>(
-        (const uint4 *)xrows, vec, da.perm, TK, da.offsets, E, El, ep->dst_base.as<int64_t>(), T, S > 0 ? 1 : 0, nr,
-        r, px, sg, G, ep->done + 0);
+        (const uint4 *)xrows, vec, da.perm, TK, da.offsets, E, ep->dst_base.as<int64_t>(), T, S > 0 ? 1 : 0, nr, r,
+        px, sg, G, ep->done + 0);
     GT_CUDA(cudaGetLastError());
     ep_wait_kernel<<<1, 32, 0, st>>>((unsigned long long *)ep->sig_local + kSigForward, arrivals, ep->err, 1);
     GT_CUDA(cudaGetLastError());
@@ -659,7 +684,7 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     if (rows_h > 0) {
         if (use_tc) {
             TcArgs ta;
-            ta.n_groups = S + El;
+            ta.n_groups = n_groups;
             ta.groups = h->groups.as<Group>();
             ta.tile_prefix = h->tile_prefix.as<int64_t>();
             ta.rows_x = rows_x;
@@ -678,7 +703,7 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
             GroupedArgs ga;
             ga.precision = c.weight_precision;
             ga.compute = compute;
-            ga.n_groups = S + El;
+            ga.n_groups = n_groups;
             ga.groups = h->groups.as<Group>();
             ga.tile_prefix = h->tile_prefix.as<int64_t>();
             ga.experts = h->table.as<ExpertLayers>();
@@ -762,6 +787,51 @@ int gtmoe_ep_unique_id(void *nccl_id_128) {
     ncclUniqueId id;
     GT_NCCL(g_nccl.GetUniqueId(&id));
     memcpy(nccl_id_128, &id, sizeof(id));
+    return 0;
+}
+
+int gtmoe_ep_set_replicas(gtmoe_t h, int n, const int32_t *experts) {
+    if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
+    std::lock_guard<std::mutex> lock(h->mu);
+    EpState *ep = ep_of(h);
+    if (!ep) return fail(GTMOE_EINVAL, "hot-expert replicas are for expert-parallel handles");
+    if (ep->have_gathered || ep->epoch > 0)
+        return fail(GTMOE_EINVAL, "hot-expert replicas must be set before the first Forward");
+    const int E = h->cfg.n_routed, S = h->cfg.n_shared, El = h->e_local;
+    if (n < 0 || n > E || (n > 0 && !experts))
+        return fail(GTMOE_EINVAL, "gtmoe_ep_set_replicas: %d experts of %d", n, E);
+    std::vector<char> rep(E, 0);
+    for (int i = 0; i < n; i++) {
+        const int e = experts[i];
+        if (e < 0 || e >= E) return fail(GTMOE_EINVAL, "routed expert %d does not exist (%d routed)", e, E);
+        if (rep[e]) return fail(GTMOE_EINVAL, "routed expert %d is listed twice", e);
+        rep[e] = 1;
+    }
+    // the owned experts keep their slots; replicas owned by other ranks get
+    // new, unset slots after them (slots of an earlier list are dropped)
+    const size_t kept = (size_t)3 * (S + El);
+    cudaSetDevice(h->device);
+    for (size_t i = kept; i < h->layers.size(); i++) {
+        LayerDev &L = h->layers[i];
+        L.tiled.release();
+        L.w.release();
+        L.s.release();
+        L.b32.release();
+        L.b64.release();
+    }
+    h->layers.resize(kept);
+    h->routed_of_slot.resize(S + El);
+    for (int e = 0; e < E; e++)
+        if (h->slot_of[e] >= S + El) h->slot_of[e] = -1;
+    for (int e = 0; e < E; e++)
+        if (rep[e] && h->slot_of[e] < 0) {
+            h->slot_of[e] = (int)h->routed_of_slot.size();
+            h->routed_of_slot.push_back(e);
+            h->layers.resize(h->layers.size() + 3);
+        }
+    h->replicated = rep;
+    h->n_replicas = n;
+    h->table_dirty = 1;
     return 0;
 }
 

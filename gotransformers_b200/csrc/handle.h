@@ -59,11 +59,19 @@ struct gtmoe_handle {
     cudaStream_t stream = nullptr;
     cudaStream_t own_stream = nullptr;
     std::mutex mu;
+    int no_tc = 0, no_decode = 0;  // kernel-path test switches (read at creation)
 
     // expert parallelism
     int n_ranks = 1, rank = 0;
     int e_begin = 0, e_local = 0;
     void *ep = nullptr;  // EpState (ep.cu)
+    // Expert table: slot of each routed expert this handle holds (-1 if it
+    // does not), and the routed expert of each slot from n_shared on.  The
+    // owned experts take slots n_shared .. n_shared + e_local - 1; hot-expert
+    // replicas that another rank owns (gtmoe_ep_set_replicas) follow.
+    std::vector<int> slot_of, routed_of_slot;
+    std::vector<char> replicated;  // per routed expert (expert parallel)
+    int n_replicas = 0;
 
     // router
     int router_set = 0;
@@ -72,7 +80,7 @@ struct gtmoe_handle {
     std::vector<double> h_bal;
     double wmax = 0;
 
-    std::vector<LayerDev> layers;  // (S + e_local) * 3
+    std::vector<LayerDev> layers;  // (number of slots) * 3
     DevBuf table;
     int table_dirty = 1;
     gtmoe::TcWeights tc;  // tensor-core layouts (tc.h)

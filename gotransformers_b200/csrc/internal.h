@@ -11,6 +11,8 @@ namespace gtmoe {
 // Counts kernel launches made by the library (gtmoe_read_timing).
 void note_launches(int n);
 
+
+
 // Limits of this build (checked by gtmoe_create).
 constexpr int kMaxRoutedExperts = 1024;
 constexpr int kMaxTopK = 32;
@@ -30,7 +32,7 @@ struct RouterArgs {
     int use_tc;                 // logits on the tensor cores (router_tc.cu)
     const void *w3;             // 3 x E_pad x d bf16 split of w64 (tensor-core path)
     int e_pad;
-    int *err;                   // bounded-wait error flag
+    int *err;                   // error flag: a bounded wait's code, or kErrNegativeTokenId
     int sms;
     double *logits;             // T x E scratch
     int32_t *chosen;            // T x k
@@ -40,6 +42,8 @@ struct RouterArgs {
     int *flagged;               // T: tokens whose choice the fix-up kernel settles
 };
 int launch_router(const RouterArgs &a, cudaStream_t st);
+// Error code the hash router records for a negative device token ID.
+constexpr int kErrNegativeTokenId = 100;
 bool router_tc_usable(const void *x, int x_dtype, int64_t T, int d);
 int launch_router_logits_tc(const void *x, int64_t T, int d, int E, int E_pad, const void *w3, double *logits,
                             int *err, int sms, cudaStream_t st);

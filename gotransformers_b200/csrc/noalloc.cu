@@ -17,6 +17,15 @@
 // the array and it keeps the last call's contents; the parts that must start
 // at zero are cleared by each call.  Calls that overlap on the GPU (different
 // streams or handles on one device) race on the array.
+//
+// Failures inside a call's kernels -- a bounded wait of the tensor-core router
+// that ran out, or (hash routing) a negative token ID, which the reference
+// panics on (mixtureofexperts.go:141-143) -- cannot be seen when the call
+// returns, since the call does not wait for its kernels.  The kernels record
+// them in an error word of the array that only a report clears; each call
+// first waits for the work already queued on its stream and, if that word is
+// set, clears it and returns the error (GTMOE_ETIMEOUT or GTMOE_EINVAL)
+// without routing, so the previous call's chosen/gates are known to be invalid.
 #include <mutex>
 
 #include "handle.h"
@@ -30,7 +39,7 @@ constexpr int64_t kMaxChoices = 524288;  // T * experts_per_token
 constexpr size_t kOffLogits = 0;
 constexpr size_t kOffGates32 = kOffLogits + kMaxLogits * sizeof(double);
 constexpr size_t kOffFlagged = kOffGates32 + kMaxChoices * sizeof(float);
-constexpr size_t kOffCounters = kOffFlagged + kMaxTokens * sizeof(int);  // [0] fix-up count, [1] wait error
+constexpr size_t kOffCounters = kOffFlagged + kMaxTokens * sizeof(int);  // [0] fix-up count, [1] error word
 constexpr size_t kScratchBytes = kOffCounters + 256;
 
 constexpr int kMaxDevices = 64;
@@ -94,7 +103,23 @@ extern "C" GTMOE_API int gtmoe_route_noalloc(gtmoe_t h, const void *x, int x_dty
     int sms = 148;
     GT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->device));
     int *counters = (int *)(scratch + kOffCounters);
-    GT_CUDA(cudaMemsetAsync(counters, 0, 2 * sizeof(int), h->stream));
+    // an error an earlier call's kernels recorded (the word is sticky until reported)
+    int prev_err = 0;
+    GT_CUDA(cudaMemcpyAsync(&prev_err, counters + 1, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    GT_CUDA(cudaStreamSynchronize(h->stream));
+    if (prev_err != 0) {
+        GT_CUDA(cudaMemsetAsync(counters + 1, 0, sizeof(int), h->stream));
+        GT_CUDA(cudaStreamSynchronize(h->stream));
+        if (prev_err == kErrNegativeTokenId)
+            return fail(GTMOE_EINVAL,
+                        "gtmoe_route_noalloc: an earlier call was given a negative token ID (its chosen and gates "
+                        "are invalid); this call did not run");
+        return fail(GTMOE_ETIMEOUT,
+                    "gtmoe_route_noalloc: an earlier call's router gave up waiting (barrier %d; its chosen and "
+                    "gates are invalid); this call did not run",
+                    prev_err);
+    }
+    GT_CUDA(cudaMemsetAsync(counters, 0, sizeof(int), h->stream));
 
     RouterArgs ra;
     ra.hash = c.hash_routing;
@@ -109,7 +134,7 @@ extern "C" GTMOE_API int gtmoe_route_noalloc(gtmoe_t h, const void *x, int x_dty
     ra.w64 = h->wr64.as<double>();
     ra.bias = h->br.as<double>();
     ra.balance = h->bal.as<double>();
-    ra.use_tc = !c.hash_routing && h->wr3.p && router_tc_usable(x, x_dtype, T, d);
+    ra.use_tc = !c.hash_routing && h->wr3.p && !h->no_tc && router_tc_usable(x, x_dtype, T, d);
     ra.thresh_scale = (ra.use_tc ? kRouterTcErr : kRouterSimtErr) * h->wmax;
     ra.w3 = h->wr3.p;
     ra.e_pad = h->e_pad;

@@ -389,10 +389,15 @@ __global__ void __launch_bounds__(256)
 }
 
 // hashedExperts (mixtureofexperts.go:88-96); gates 1/k (:148-151)
+// A negative token ID is misuse that the reference panics on
+// (mixtureofexperts.go:141-143); callers that pass device IDs the host has not
+// checked see it as kErrNegativeTokenId in *err (the experts computed from the
+// wrapped ID stay in range, so later kernels read valid indices).
 __global__ void hash_route_kernel(const int64_t *__restrict__ ids, int64_t T, int E, int k, int32_t *__restrict__ chosen,
-                                  double *__restrict__ gates64, float *__restrict__ gates32) {
+                                  double *__restrict__ gates64, float *__restrict__ gates32, int *err) {
     int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= T) return;
+    if (ids[t] < 0 && err) atomicCAS(err, 0, kErrNegativeTokenId);
     uint64_t first = ((uint64_t)ids[t] * 2654435761ull + 12345ull) % (uint64_t)E;
     double g = 1.0 / (double)k;
     for (int i = 0; i < k; i++) {
@@ -437,7 +442,7 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
     if (a.T == 0) return 0;
     if (a.hash) {
         hash_route_kernel<<<(unsigned)((a.T + 255) / 256), 256, 0, st>>>(a.token_ids, a.T, a.E, a.k, a.chosen,
-                                                                         a.gates64, a.gates32);
+                                                                         a.gates64, a.gates32, a.err);
         GT_CUDA(cudaGetLastError());
         note_launches(1);
         return 0;

@@ -206,7 +206,6 @@ __global__ void __launch_bounds__(kRThreads, 1)
 bool router_tc_usable(const void *x, int x_dtype, int64_t T, int d) {
     if (x_dtype != GTMOE_DTYPE_BF16 || T < 256 || d % kRBK != 0) return false;
     if (((uintptr_t)x & 15) != 0) return false;
-    if (getenv("GTMOE_DISABLE_TC")) return false;
     return true;
 }
 

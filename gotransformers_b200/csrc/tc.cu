@@ -762,7 +762,7 @@ bool tc_supported(const gtmoe_handle *h, int64_t T) {
     const gtmoe_config &c = h->cfg;
     if (c.weight_precision != GTMOE_INT8 && c.weight_precision != GTMOE_FP4) return false;
     if (T <= 0) return false;
-    if (getenv("GTMOE_DISABLE_TC")) return false;
+    if (h->no_tc) return false;
     return shapes_ok(c);
 }
 

@@ -189,6 +189,31 @@ int parse(WeightFile &wf) {
                                     "wrong amount of data",
                                     wf.path.c_str(), p.name.c_str(), (unsigned long long)p.rows,
                                     (unsigned long long)p.width);
+                    // RowsFromSnapshot checks only that combined count, so a
+                    // snapshot with, say, fewer scales and more codes passes it
+                    // and the reference panics later, when DotRow indexes past
+                    // the shorter list.  Such a record is damaged either way;
+                    // it is refused here, before any layer setter could read
+                    // past the end of a list.
+                    {
+                        uint64_t codes = 0, want_codes = p.rows * p.width, want_scales = 0;
+                        switch (prec) {
+                            case GTMOE_FLOAT64: codes = p.f64.count; break;
+                            case GTMOE_FLOAT32: codes = p.f32.count; break;
+                            case GTMOE_INT8: codes = p.i8.count, want_scales = p.rows * blocks; break;
+                            default:
+                                codes = p.fp4.count, want_codes = p.rows * ((p.width + 1) / 2),
+                                want_scales = p.rows * blocks;
+                        }
+                        if (codes != want_codes || p.scales.count != want_scales)
+                            return fail(GTMOE_EINVAL,
+                                        "%s: compressed parameter \"%s\": rows snapshot holds %llu codes and %llu "
+                                        "scales; %llu rows of width %llu need %llu and %llu",
+                                        wf.path.c_str(), p.name.c_str(), (unsigned long long)codes,
+                                        (unsigned long long)p.scales.count, (unsigned long long)p.rows,
+                                        (unsigned long long)p.width, (unsigned long long)want_codes,
+                                        (unsigned long long)want_scales);
+                    }
                     break;
                 }
                 default:

@@ -128,6 +128,19 @@ class MixtureOfExperts:
     def handle(self):
         return self._h
 
+    def set_replicas(self, experts):
+        """Expert parallel: routed experts held (and computed for this rank's
+        own tokens) on every rank; call on every rank before the first
+        forward, then set those experts' layers on every rank too."""
+        arr = np.ascontiguousarray(np.asarray(list(experts), dtype=np.int32))
+        check(_lib.lib().gtmoe_ep_set_replicas(self._h, int(arr.size), _addr(arr) if arr.size else None))
+        self.replicas = [int(e) for e in arr]
+
+    def holds(self, expert: int) -> bool:
+        """Whether this handle holds routed expert `expert` (owned or replicated)."""
+        el = self.cfg.n_routed // self.ep_ranks
+        return self.ep_rank * el <= expert < (self.ep_rank + 1) * el or expert in getattr(self, "replicas", ())
+
     def set_stream(self, stream_ptr: int | None):
         check(_lib.lib().gtmoe_set_stream(self._h, stream_ptr))
 

@@ -151,11 +151,54 @@ def zipf_router_bias(E: int, k: int, s: float, seed: int, samples: int = 4096, i
     return bias
 
 
+def expected_rates(cfg: MoEConfig, samples: int = 20000, seed: int = 99) -> np.ndarray:
+    """Expected selection rate of each routed expert (chosen per token) under
+    the config's router biases, with the N(0,1) logit model the biases were
+    fitted with; sums to k."""
+    E, k = cfg.n_routed, cfg.k
+    if cfg.hash_routing:
+        return np.full(E, k / E)
+    rb = zipf_router_bias(E, k, cfg.zipf_s, cfg.weight_seed) if cfg.zipf_s else np.zeros(E)
+    z = np.random.default_rng(seed).standard_normal((samples, E)) + rb
+    aff = np.sqrt(np.where(z > 20, z, np.log1p(np.exp(np.minimum(z, 20)))))
+    kth = -np.partition(-aff, k - 1, axis=1)[:, k - 1 : k]
+    return (aff >= kth).mean(axis=0)
+
+
+def choose_replicas(cfg: MoEConfig, ranks: int, max_replicas: int = 16, target: float = 1.03) -> list:
+    """Hot experts to hold on every expert-parallel rank: while the most
+    loaded rank's expected rows exceed `target` x the mean, replicate that
+    rank's hottest owned expert (its rows then run on their tokens' ranks).
+    Returns the experts, ascending."""
+    if ranks < 2:
+        return []
+    rate = expected_rates(cfg)
+    E, T = cfg.n_routed, cfg.T
+    el, tl = E // ranks, T // ranks
+    rep = set()
+
+    def rows(q):
+        owned = [e for e in range(q * el, (q + 1) * el) if e not in rep]
+        return cfg.n_shared * tl + T * rate[owned].sum() + tl * rate[sorted(rep)].sum()
+
+    mean = T * (cfg.n_shared + cfg.k) / ranks
+    while len(rep) < max_replicas:
+        loads = [rows(q) for q in range(ranks)]
+        q = int(np.argmax(loads))
+        if loads[q] <= target * mean:
+            break
+        cand = [e for e in range(q * el, (q + 1) * el) if e not in rep]
+        if not cand:
+            break
+        rep.add(max(cand, key=lambda e: rate[e]))
+    return sorted(rep)
+
+
 def load_config_on_gpu(cfg: MoEConfig, moe, keep_host: bool = False, device: int = 0):
     """Generates cfg's weights on the GPU (gtmoe_fill_normal + the GPU
     quantiser, gtmoe_quantize_rows) and sets them on `moe` (a
     moe.MixtureOfExperts, possibly one expert-parallel rank: only the routed
-    experts it owns are generated).  With keep_host, also returns the host
+    experts it holds -- owned or replicated -- are generated).  With keep_host, also returns the host
     copies {("router",): (w, bias)} | {(e, which): (codes, scales)} for a CPU
     checker."""
     import torch
@@ -173,8 +216,7 @@ def load_config_on_gpu(cfg: MoEConfig, moe, keep_host: bool = False, device: int
         moe.set_router(wr_h, rb)
         if keep_host:
             host[("router",)] = (wr_h, rb)
-    e_local = E // moe.ep_ranks
-    owned = list(range(S)) + [S + moe.ep_rank * e_local + i for i in range(e_local)]
+    owned = list(range(S)) + [S + e for e in range(E) if moe.holds(e)]
     buf = torch.empty(max(h * d, d * h), dtype=torch.float64, device=dev)
     blocks = lambda w: (w + 15) // 16
     for e in owned:

@@ -105,6 +105,20 @@ GTMOE_API int gtmoe_ep_unique_id(void *nccl_id_128);
 GTMOE_API int gtmoe_create_ep(const gtmoe_config *cfg, int device, int n_ranks, int rank, const void *nccl_id_128,
                     gtmoe_t *out);
 
+/* Hot-expert replicas of an expert-parallel handle (opt-in; no counterpart in
+ * the reference, which has no multi-GPU MoE).  The n routed experts listed in
+ * `experts` (host int32, distinct) are held by EVERY rank: each rank computes
+ * their rows for its own tokens, the way it computes the shared experts, so
+ * those rows never cross NVLink and never queue on the owning rank.  Every
+ * other routed expert stays owned by index.  Under a skewed router (a few
+ * experts that nearly every token picks) this evens out the ranks' work.
+ * Results are those of the plain layout (a row's arithmetic does not depend on
+ * where it runs).  Call it identically on every rank, before the first
+ * Forward; then set the listed experts' layers on every rank too
+ * (gtmoe_set_expert_layer accepts owned and replicated experts).  A later call
+ * replaces the list; n = 0 drops it.  GTMOE_EINVAL on a single-GPU handle. */
+GTMOE_API int gtmoe_ep_set_replicas(gtmoe_t h, int n, const int32_t *experts);
+
 /* The mixture-of-experts half of transformer.Block.Forward (block.go:72-77,
  * no hyper-connections, dropout off): out = x + Forward(RMSNorm(x)), in one
  * call.  gtmoe_set_norm sets the block's FeedForwardNorm (RMSNorm weights,
@@ -267,7 +281,14 @@ GTMOE_API int gtmoe_read_timing(gtmoe_t h, double *ms, int n_phases, int64_t *ca
  * are device pointers; the results equal gtmoe_forward's chosen and gates.
  * Asynchronous on the handle's stream.  The first call on a device looks the
  * array up and should come before any stream capture.  Calls share the array:
- * calls that overlap on the GPU race. */
+ * calls that overlap on the GPU race.
+ * Errors of the kernels themselves are reported by the NEXT call: a call
+ * first waits for the work already queued on the handle's stream, and if an
+ * earlier call recorded a failure -- a bounded device wait of the router that
+ * ran out, or, with hash routing, a negative token ID (the reference panics,
+ * mixtureofexperts.go:141-143; token_ids are device memory here and are not
+ * checked on the host) -- it returns GTMOE_ETIMEOUT or GTMOE_EINVAL without
+ * routing: that earlier call's chosen and gates are invalid. */
 GTMOE_API int gtmoe_route_noalloc(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids,
                                   int32_t *chosen, double *gates);
 

@@ -530,3 +530,90 @@ void gto_update_balance(double *balance, const int64_t *load, int E, double rate
         if ((double)load[e] > average) balance[e] -= rate;
     }
 }
+
+/* ------------------------------------------- seeded benchmark inputs */
+
+/* Not a reference function: the benchmark's synthetic inputs, so that the
+ * CPU reference arm of bench.py can make its weights without the GPU library.
+ * Value j of stream (seed, stream) is a pure function of those numbers --
+ * SplitMix64 + Box-Muller, the definition written out in
+ * gotransformers_b200/synthetic.py (which the library's GPU generator follows
+ * too; libm and CUDA's log/cos may differ in the last bit of a value):
+ *   key = splitmix64(seed ^ (stream * 0xD1B54A32D192ED03))
+ *   a, b = splitmix64(key + 2j), splitmix64(key + 2j + 1)
+ *   u1 = ((a >> 11) + 1) * 2^-53, u2 = (b >> 11) * 2^-53
+ *   z = sqrt(-2 ln u1) * cos(2 pi u2)                                     */
+static uint64_t splitmix64(uint64_t x) {
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static double synth_normal(uint64_t key, uint64_t j) {
+    const uint64_t a = splitmix64(key + 2 * j), b = splitmix64(key + 2 * j + 1);
+    const double u1 = ((double)(a >> 11) + 1.0) * 0x1p-53;
+    const double u2 = (double)(b >> 11) * 0x1p-53;
+    return sqrt(-2.0 * log(u1)) * cos(2.0 * M_PI * u2);
+}
+
+typedef struct {
+    int precision, width;
+    uint64_t key;
+    double stddev;
+    int first, last;
+    unsigned char *codes;
+    float *scales;
+    size_t row_bytes;
+    int blocks;
+    int rc;
+} synth_job;
+
+static void *synth_worker(void *arg) {
+    synth_job *j = (synth_job *)arg;
+    double *row = (double *)malloc(sizeof(double) * (size_t)j->width);
+    if (!row) {
+        j->rc = -1;
+        return NULL;
+    }
+    for (int r = j->first; r < j->last; r++) {
+        for (int i = 0; i < j->width; i++)
+            row[i] = j->stddev * synth_normal(j->key, (uint64_t)r * (uint64_t)j->width + (uint64_t)i);
+        /* lowprecision.Rows.Append, one row at a time (rows.go:38-79) */
+        int rc = gto_quantize_rows(j->precision, 1, j->width, row, j->codes + (size_t)r * j->row_bytes,
+                                   j->scales ? j->scales + (size_t)r * j->blocks : NULL);
+        if (rc) j->rc = rc;
+    }
+    free(row);
+    return NULL;
+}
+
+/* rows x width values stddev * z (value index r*width + i of the stream),
+ * quantised row by row into the RowsSnapshot arrays of `precision`. */
+int gto_synth_rows(int precision, int rows, int width, uint64_t seed, uint64_t stream, double stddev, void *codes,
+                   float *scales, int threads) {
+    if (rows < 0 || width < 1) return -1;
+    const uint64_t key = splitmix64(seed ^ (stream * 0xD1B54A32D192ED03ull));
+    size_t row_bytes = precision == GTO_FLOAT64   ? 8 * (size_t)width
+                       : precision == GTO_FLOAT32 ? 4 * (size_t)width
+                       : precision == GTO_INT8    ? (size_t)width
+                                                  : (size_t)gto_fp4_row_bytes(width);
+    int nt = threads < 1 ? 1 : threads > 256 ? 256 : threads;
+    if (nt > rows) nt = rows < 1 ? 1 : rows;
+    synth_job jobs[256];
+    pthread_t tids[256];
+    int per = (rows + nt - 1) / nt, rc = 0;
+    for (int t = 0; t < nt; t++) {
+        int first = t * per, last = first + per < rows ? first + per : rows;
+        jobs[t] = (synth_job){precision, width, key, stddev, first, last, (unsigned char *)codes,
+                              (precision == GTO_INT8 || precision == GTO_FP4) ? scales : NULL, row_bytes,
+                              gto_scale_blocks(width), 0};
+        if (nt > 1) pthread_create(&tids[t], NULL, synth_worker, &jobs[t]);
+        else synth_worker(&jobs[t]);
+    }
+    for (int t = 0; t < nt; t++) {
+        if (nt > 1) pthread_join(tids[t], NULL);
+        if (jobs[t].rc) rc = jobs[t].rc;
+    }
+    return rc;
+}

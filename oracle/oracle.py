@@ -100,6 +100,8 @@ def lib():
             L.gto_activate.argtypes = [i, d, d]
             L.gto_activate.restype = d
             L.gto_hashed_experts.argtypes = [ctypes.c_int64, i, i, vp]
+            L.gto_synth_rows.argtypes = [i, i, i, ctypes.c_uint64, ctypes.c_uint64, d, vp, vp, i]
+            L.gto_synth_rows.restype = i
             _lib = L
     return _lib
 
@@ -172,6 +174,30 @@ def quantize_rows(precision: int, values: np.ndarray) -> Layer:
     rc = lib().gto_quantize_rows(precision, rows, width, _ptr(values), _ptr(codes), _ptr(scales))
     if rc != 0:
         raise ValueError("gto_quantize_rows failed")
+    return Layer(precision, rows, width, codes, scales)
+
+
+def synth_rows(precision: int, rows: int, width: int, seed: int, stream: int, stddev: float,
+               threads: int = 1) -> Layer:
+    """Seeded benchmark weights (not a reference function): rows x width
+    values stddev * N(0,1) of stream (seed, stream) -- the generator written
+    out in gotransformers_b200/synthetic.py -- quantised row by row with the
+    reference quantiser (lowprecision/rows.go:38-79).  Lets the CPU reference
+    arm of bench.py make the benchmark's weights without the GPU library."""
+    blocks = scale_blocks(width)
+    if precision == FLOAT64:
+        codes = np.empty(rows * width, np.float64)
+    elif precision == FLOAT32:
+        codes = np.empty(rows * width, np.float32)
+    elif precision == INT8:
+        codes = np.empty(rows * width, np.int8)
+    else:
+        codes = np.empty(rows * fp4_row_bytes(width), np.uint8)
+    scales = np.empty(rows * blocks, np.float32) if precision in (INT8, FP4) else None
+    rc = lib().gto_synth_rows(precision, rows, width, seed & 0xFFFFFFFFFFFFFFFF, stream, stddev, _ptr(codes),
+                              _ptr(scales), threads)
+    if rc != 0:
+        raise ValueError(f"gto_synth_rows failed ({rc})")
     return Layer(precision, rows, width, codes, scales)
 
 

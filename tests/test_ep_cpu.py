@@ -6,7 +6,9 @@ Plan (ep.cu): each rank routes its own tokens, orders its (token, slot) rows
 by global expert (stable, token-ascending), all-gathers every rank's
 per-expert counts, sends each owner its rows, regroups received rows
 expert-major / source-ascending, runs the owned experts, returns the rows in
-the order they came, and combines in the reference order."""
+the order they came, and combines in the reference order.  With hot-expert
+replicas (gtmoe_ep_set_replicas) a replicated expert's rows stay on their
+token's rank and run there."""
 import os
 import socket
 
@@ -39,7 +41,7 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, result_dir):
+def _rank_main(rank, world, port, result_dir, replicas=()):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -58,6 +60,20 @@ def _rank_main(rank, world, port, result_dir):
     gathered = [torch.zeros(E, dtype=torch.int64) for _ in range(world)]
     dist.all_gather(gathered, torch.from_numpy(load))
     Lg = np.stack([g.numpy() for g in gathered])  # [source, expert]
+    rep = np.zeros(E, bool)
+    rep[list(replicas)] = True
+    # replicated experts' rows run here, on their token's rank: they leave the
+    # exchange (their counts are zeroed in the exchange plan)
+    local = np.zeros((0, d))
+    local_pos = np.zeros(0, np.int64)
+    if rep.any():
+        pos = np.arange(len(order))
+        keep = ~rep[flat[order]]
+        local_pos, local = pos[~keep], send_rows[~keep]
+        local_e = flat[order][~keep]
+        send_rows = send_rows[keep]
+        Lg = Lg.copy()
+        Lg[:, rep] = 0
     send_cnt = [int(Lg[rank, q * El:(q + 1) * El].sum()) for q in range(world)]
     send_off = np.concatenate([[0], np.cumsum(send_cnt)])
     recv_cnt = [int(Lg[s, rank * El:(rank + 1) * El].sum()) for s in range(world)]
@@ -89,7 +105,18 @@ def _rank_main(rank, world, port, result_dir):
     for s in range(world):
         ret_send[s][: recv_cnt[s]] = torch.from_numpy(back[s])
     ret_recv = _exchange(ret_send, world, rank)
-    yret = np.concatenate([ret_recv[q][: send_cnt[q]].numpy() for q in range(world)])
+    yret_sent = np.concatenate([ret_recv[q][: send_cnt[q]].numpy() for q in range(world)])
+    yret = np.zeros((len(order), d))
+    if rep.any():
+        mask = np.ones(len(order), bool)
+        mask[local_pos] = False
+        yret[mask] = yret_sent
+        for e in np.unique(local_e):
+            sel = local_e == e
+            g, u, dn = spec.experts[S + e]
+            yret[local_pos[sel]] = O.gated_forward(g, u, dn, local[sel])
+    else:
+        yret = yret_sent
     # combine in the reference order
     out = np.zeros((Tl, d))
     for s in range(S):
@@ -103,9 +130,10 @@ def _rank_main(rank, world, port, result_dir):
     dist.destroy_process_group()
 
 
-def test_expert_parallel_plan_matches_single_process(tmp_path):
+@pytest.mark.parametrize("replicas", [(), (1, 6)])
+def test_expert_parallel_plan_matches_single_process(tmp_path, replicas):
     port = _free_port()
-    mp.start_processes(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn")
+    mp.start_processes(_rank_main, args=(2, port, str(tmp_path), replicas), nprocs=2, start_method="spawn")
     spec, x, ids = make_case(**CASE)
     ref = O.moe_forward(spec, x)["out"]
     got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(2)])

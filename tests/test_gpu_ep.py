@@ -2,9 +2,12 @@
 n_routed/G of the routed experts and an uneven slice of the tokens (one rank
 may have none); concatenated outputs must equal one single-GPU handle's
 outputs on the same weights (same expert choices, output within 1e-6
-rel-L2), and the balance update must use the load summed over ranks.  Each
+rel-L2), the routing (chosen experts, each rank's expert-ordered rows, the
+per-expert loads) must equal the oracle's router (mixtureofexperts.go:
+150-190), and the balance update must use the load summed over ranks.  Each
 rank first runs a smaller prefix of its slice and then its whole slice twice,
-so the peer buffers grow once and are then reused."""
+so the peer buffers grow once and are then reused.  One case holds hot-expert
+replicas (gtmoe_ep_set_replicas) on every rank."""
 import os
 import socket
 
@@ -24,7 +27,11 @@ CASES = {
     # also: a step where one rank's arguments are wrong fails on every rank
     "hash routing, refused step": dict(T=512, d=256, h=128, n_shared=1, n_routed=8, k=3, precision=O.INT8, seed=34,
                                        hash_routing=True, x_bf16=True),
+    "fp4 hot-expert replicas": dict(T=1200, d=512, h=256, n_shared=1, n_routed=16, k=4, precision=O.FP4, seed=35,
+                                    x_bf16=True),
 }
+# routed experts held by every rank, per case (the others stay owned by index)
+REPLICAS = {"fp4 hot-expert replicas": [0, 5, 6, 15]}
 # uneven token split between the ranks, as fractions of T (rank 1 of 4 and 8 gets none)
 SPLITS = {2: [0.62], 4: [0.3, 0.3, 0.72], 8: [0.1, 0.1, 0.25, 0.4, 0.55, 0.7, 0.9]}
 
@@ -77,13 +84,14 @@ def _rank(rank, world, port, name, outdir):
                            device=rank, ep_ranks=world, ep_rank=rank, nccl_id=obj[0])
     if not spec.hash_routing:
         m.set_router(to_rows(spec.router), spec.router.bias)
-    El = spec.n_routed // world
+    if name in REPLICAS:
+        m.set_replicas(REPLICAS[name])
     for e, layers in enumerate(spec.experts):
         if e < spec.n_shared:
             kind, idx = G.SHARED, e
         else:
             idx = e - spec.n_shared
-            if not (rank * El <= idx < (rank + 1) * El):
+            if not m.holds(idx):
                 continue
             kind = G.ROUTED
         for which, L in enumerate(layers):
@@ -111,6 +119,8 @@ def _rank(rank, world, port, name, outdir):
     torch.cuda.synchronize()
     np.save(os.path.join(outdir, f"out{rank}.npy"), out.cpu().numpy())
     np.save(os.path.join(outdir, f"chosen{rank}.npy"), m.last_chosen_experts)
+    np.save(os.path.join(outdir, f"perm{rank}.npy"), m.last_rows_for_expert)
+    np.save(os.path.join(outdir, f"load{rank}.npy"), m.last_expert_load())
     m.update_balance(0.05)
     np.save(os.path.join(outdir, f"bal{rank}.npy"), m.balance_biases)
     m.close()
@@ -143,6 +153,16 @@ def test_expert_parallel_matches_single_gpu(name, tmp_path):
     got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(world)])
     got_chosen = np.concatenate([np.load(tmp_path / f"chosen{r}.npy") for r in range(world)])
     assert np.array_equal(got_chosen, chosen)
+    # routing against the oracle: every rank's chosen experts, its rows in
+    # expert order (rowsForExpert over its own tokens) and its loads
+    ro = O.moe_route(spec, x, ids, threads=8)
+    assert np.array_equal(got_chosen, ro["chosen"])
+    for r in range(world):
+        sl = _slice(r, world, x.shape[0])
+        flat = ro["chosen"][sl].reshape(-1)
+        want_perm = np.argsort(flat, kind="stable") // spec.k
+        assert np.array_equal(np.load(tmp_path / f"perm{r}.npy"), want_perm), r
+        assert np.array_equal(np.load(tmp_path / f"load{r}.npy"), np.bincount(flat, minlength=spec.n_routed)), r
     assert rel_l2(got, ref) <= 1e-6
     # the first, smaller call: each rank's prefix rows (rows are independent)
     for r in range(world):

@@ -170,12 +170,15 @@ def test_tensor_core_path_matches_simt_path(prec, monkeypatch):
                              x_bf16=True, layer_bias=0.05)
     m = gpu_moe(spec)
     tc = m.forward(x, ids)
-    monkeypatch.setenv("GTMOE_DISABLE_TC", "1")
-    simt = m.forward(x, ids)
+    monkeypatch.setenv("GTMOE_DISABLE_TC", "1")  # read when a handle is created
+    m2 = gpu_moe(spec)
+    simt = m2.forward(x, ids)
+    assert np.array_equal(m2.last_chosen_experts, m.last_chosen_experts)
     assert rel_l2(tc, simt) <= 1e-2
     ref = O.moe_forward(spec, x, ids, threads=8)["out"]
     assert rel_l2(tc, ref) <= TOL[prec]
     m.close()
+    m2.close()
 
 
 def test_empty_batch():
@@ -256,9 +259,39 @@ def config_case(name):
         experts.append(tuple(layers))
     spec = O.MoESpec(d=cfg.d, h=cfg.h, n_shared=cfg.n_shared, n_routed=cfg.n_routed, k=cfg.k, router=router,
                      experts=experts)
+    check_quantiser_sample(cfg, host)
     x = synthetic.make_x_on_gpu(cfg).to(torch.float64).cpu().numpy()
     ids = np.arange(cfg.T, dtype=np.int64)
     return spec, x, ids, m
+
+
+def check_quantiser_sample(cfg, host, n_rows=16):
+    """The config's weights are quantised on the GPU, and the oracle then
+    reads those same bytes, so a GPU-quantiser fault at the config's widths
+    would agree with itself.  Here the float64 values of a seeded sample of
+    rows of every layer kind (shared and routed; gate, up, down) are made
+    again and quantised by the oracle's restatement of Rows.Append
+    (lowprecision/rows.go:38-79): codes and scales must be bit-identical."""
+    import torch
+
+    rng = np.random.default_rng(101)
+    S, E = cfg.n_shared, cfg.n_routed
+    experts = ([0] if S else []) + [int(S + e) for e in rng.choice(E, size=min(2, E), replace=False)]
+    for e in experts:
+        for which, (rows, width) in enumerate([(cfg.h, cfg.d), (cfg.h, cfg.d), (cfg.d, cfg.h)]):
+            vals = torch.empty((rows, width), dtype=torch.float64, device="cuda")
+            G.fill_normal(vals, cfg.weight_seed, synthetic.expert_stream(e, which), stddev=1.0 / np.sqrt(width))
+            pick = np.sort(rng.choice(rows, size=min(n_rows, rows), replace=False))
+            ref = O.quantize_rows(cfg.precision, vals.cpu().numpy()[pick])
+            codes, scales = host[(e, which)]
+            row_bytes = ref.values.nbytes // len(pick)
+            got = np.asarray(codes).view(np.uint8).reshape(rows, -1)[pick]
+            assert got.shape[1] == row_bytes
+            assert np.array_equal(got, ref.values.view(np.uint8).reshape(len(pick), -1)), (e, which)
+            if ref.scales is not None:
+                blocks = (width + 15) // 16
+                assert np.array_equal(np.asarray(scales).reshape(rows, blocks)[pick],
+                                      ref.scales.reshape(len(pick), blocks)), (e, which)
 
 
 def test_config_c1_full():
@@ -310,13 +343,15 @@ def test_decode_path_matches_tensor_core_path(prec):
     m = gpu_moe(spec)
     out_dec = m.forward(x, ids)
     chosen = m.last_chosen_experts.copy()
-    os.environ["GTMOE_DISABLE_DECODE"] = "1"
+    os.environ["GTMOE_DISABLE_DECODE"] = "1"  # read when a handle is created
     try:
-        out_tc = m.forward(x, ids)
+        m2 = gpu_moe(spec)
     finally:
         del os.environ["GTMOE_DISABLE_DECODE"]
-    assert np.array_equal(m.last_chosen_experts, chosen)
+    out_tc = m2.forward(x, ids)
+    assert np.array_equal(m2.last_chosen_experts, chosen)
     err_dec = check_against_oracle(spec, x, ids, out_dec, m)
-    err_tc = check_against_oracle(spec, x, ids, out_tc, m)
+    err_tc = check_against_oracle(spec, x, ids, out_tc, m2)
     assert err_dec <= err_tc + 1e-4, (err_dec, err_tc)
     m.close()
+    m2.close()

@@ -310,3 +310,37 @@ def test_rmsnorm_restatement():
     w = np.linspace(0.5, 1.5, 37)
     ref = x / np.sqrt((x * x).mean(axis=1, keepdims=True) + 1e-6) * w
     np.testing.assert_allclose(O.rmsnorm(x, w, 1e-6), ref, rtol=1e-13)
+
+
+def test_clamped_activations_known_answers():
+    """activationfunction_test.go:52-57: ClampedSiLU(2) clamps 100 to silu(2)
+    and ClampedLinear(2) clamps -100 to -2, exactly; and the clamped
+    derivatives the oracle's backward uses match central differences of the
+    oracle's forward activations (TestClampedActivations, :45-51)."""
+    import math
+    from types import SimpleNamespace
+
+    L = O.lib()
+    silu2 = 2.0 * (1.0 / (1.0 + math.exp(-2.0)))  # silu = x * sigmoid(x), activationfunction.go:102-105
+    assert L.gto_activate(O.ACT_CLAMPED_SILU, 2.0, 100.0) == silu2
+    assert L.gto_activate(O.ACT_CLAMPED_LINEAR, 2.0, -100.0) == -2.0
+    assert L.gto_activate(O.ACT_CLAMPED_LINEAR, 2.0, 100.0) == 2.0
+    spec = SimpleNamespace(clamped=True, clamp_limit=2.0)
+    h = 1e-6
+    for x in (-5.0, -1.3, -0.2, 0.3, 1.7, 4.0):
+        for act, deriv in ((O.ACT_CLAMPED_SILU, O._gate_deriv), (O.ACT_CLAMPED_LINEAR, O._up_deriv)):
+            num = (L.gto_activate(act, 2.0, x + h) - L.gto_activate(act, 2.0, x - h)) / (2 * h)
+            assert abs(num - float(deriv(np.float64(x), spec))) <= 1e-6, (act, x)
+
+
+def test_host_generator_matches_the_python_definition():
+    """oracle.synth_rows (the CPU reference arm's weights) is the generator of
+    synthetic.py followed by the reference quantiser."""
+    rows, width, seed, stream = 7, 45, 10, synthetic.expert_stream(3, 2)
+    want = synthetic.normal(seed, stream, rows * width).reshape(rows, width) / np.sqrt(width)
+    got = O.synth_rows(O.FLOAT64, rows, width, seed, stream, 1.0 / np.sqrt(width), threads=3)
+    np.testing.assert_allclose(got.values.reshape(rows, width), want, rtol=1e-14, atol=0)
+    q = O.synth_rows(O.INT8, rows, width, seed, stream, 1.0 / np.sqrt(width), threads=2)
+    ref = O.quantize_rows(O.INT8, want)
+    assert np.mean(q.values == ref.values) > 0.999
+    np.testing.assert_allclose(q.scales, ref.scales, rtol=1e-6)

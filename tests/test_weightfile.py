@@ -100,6 +100,19 @@ def test_damaged_files_fail_like_the_reference(tmp_path):
     write(str(wrong), [("w", compressed_record(O.INT8, 4, 20, L.values, L.scales[:-1]))])
     _expect_error(wrong, "has the wrong amount of data")
 
+    # the combined byte count RowsFromSnapshot checks is right, the split is
+    # not: one scale fewer and four more code bytes.  The reference reader
+    # accepts it and DotRow panics later; the loader refuses it up front.
+    split = tmp_path / "split.bin"
+    codes = np.concatenate([L.values, np.zeros(4, np.int8)])
+    write(str(split), [("w", compressed_record(O.INT8, 4, 20, codes, L.scales[:-1]))])
+    _expect_error(split, "holds 84 codes and 7 scales; 4 rows of width 20 need 80 and 8")
+    Lf = _layer(O.FP4, 3, 33, 8)
+    split4 = tmp_path / "split4.bin"
+    write(str(split4), [("w", compressed_record(O.FP4, 3, 33, Lf.values[:-8], np.concatenate(
+        [Lf.scales, np.ones(2, np.float32)])))])
+    _expect_error(split4, "holds 43 codes and 11 scales; 3 rows of width 33 need 51 and 9")
+
     wide = tmp_path / "wide.bin"
     write(str(wide), [("w", compressed_record(O.INT8, 4, 0, np.zeros(0, np.int8), np.zeros(0, np.float32)))])
     _expect_error(wide, "which does not fit in the file")

@@ -65,3 +65,36 @@ def test_route_noalloc_rejects_sizes_beyond_its_scratch():
                                                   chosen.data_ptr(), gates.data_ptr()))
     assert e.value.code == -1 and "fixed scratch" in str(e.value)
     m.close()
+
+
+def test_route_noalloc_reports_a_negative_token_id_on_the_next_call():
+    """With hash routing the token IDs are device memory that the host does
+    not read; the kernel records a negative ID (the reference panics on it,
+    mixtureofexperts.go:141-143) and the next call reports it without routing.
+    The call after that routes normally again."""
+    import torch
+
+    spec, x, ids = make_case(T=40, d=32, h=32, n_shared=0, n_routed=8, k=2, precision=O.INT8, hash_routing=True,
+                             seed=5)
+    m = gpu_moe(spec)
+    T, k = x.shape[0], spec.k
+    xd = torch.from_numpy(x).to(torch.float32).cuda()
+    chosen = torch.full((T, k), -1, dtype=torch.int32, device="cuda")
+    gates = torch.zeros((T, k), dtype=torch.float64, device="cuda")
+    L = _lib.lib()
+    bad = np.asarray(ids, np.int64).copy()
+    bad[7] = -3
+    bad_d = torch.from_numpy(bad).cuda()
+    good_d = torch.from_numpy(np.asarray(ids, np.int64)).cuda()
+    call = lambda ids_d: L.gtmoe_route_noalloc(m.handle, xd.data_ptr(), _lib.DTYPE_F32, T, ids_d.data_ptr(),
+                                               chosen.data_ptr(), gates.data_ptr())
+    assert call(bad_d) == 0  # asynchronous: the kernel has not run yet
+    with pytest.raises(_lib.GtmoeError) as e:
+        _lib.check(call(good_d))
+    assert e.value.code == -1 and "negative token ID" in str(e.value)
+    _lib.check(call(good_d))
+    torch.cuda.synchronize()
+    want = np.array([O.hashed_experts(int(i), spec.n_routed, k) for i in ids], np.int32)
+    assert np.array_equal(chosen.cpu().numpy(), want)
+    np.testing.assert_allclose(gates.cpu().numpy(), 1.0 / k)
+    m.close()
