@@ -107,6 +107,10 @@ CONFIGS = {
     "c4_8": MoEConfig("c4_8", 8, 2048, 1408, 1, 64, 6, 2, False, weight_seed=6, act_seed=8),
     "c4_64": MoEConfig("c4_64", 64, 2048, 1408, 1, 64, 6, 2, False, weight_seed=6, act_seed=9),
     "c5": MoEConfig("c5", 65536, 4096, 2048, 1, 256, 8, 3, True, zipf_s=1.0, weight_seed=10, act_seed=11),
+    # c5's layer shapes and mean routed-group size (T*k/E = 2048 rows) at an
+    # eighth of its tokens and experts: about 3 GB on the device, small enough
+    # for a many-pass ncu capture of the expert kernels
+    "c5s": MoEConfig("c5s", 8192, 4096, 2048, 1, 32, 8, 3, True, zipf_s=1.0, weight_seed=12, act_seed=13),
 }
 
 
