@@ -351,20 +351,25 @@ def main():
     kname, col = max((("expert_gate_up", ig), ("expert_down", idn)), key=lambda kv: phases[kv[0]])
     slow = max(per_rank, key=lambda v: v[col])
     kms, rows = slow[col], slow[2]
-    traffic = profiled_traffic(kname, cfg.name, T_local)
-    if decode_shaped(cfg):
-        # weight streaming: bytes of the touched experts' layers (codes + block
-        # scales) plus activation rows in and out, over the kernel's time
+    traffic_ent = profiled_traffic(kname, cfg.name, T_local)
+    traffic = traffic_ent["bytes"] if traffic_ent else None
+    simt = cfg.precision in (0, 1)  # Float64 / Float32 experts run on the SIMT kernels (no tensor path)
+    if decode_shaped(cfg) or simt:
+        # weight streaming (decode) or FFMA kernels: bytes of the touched
+        # experts' layers (codes + block scales) plus the activation rows in
+        # and out (bf16 on the decode path, float32 on the SIMT path), over the
+        # kernel's time
         touched = int((moe.last_expert_load() > 0).sum()) + cfg.n_shared
-        bpv = {2: 1.0 + 4 / 16, 3: 0.5 + 4 / 16}[cfg.precision]
-        n_layers, k_in, n_out = (2, cfg.d, cfg.h) if kname == "expert_gate_up" else (1, cfg.h, cfg.d)
-        kbytes = touched * n_layers * cfg.h * cfg.d * bpv + rows * (k_in + n_out) * 2
+        kbytes = kernel_bytes(cfg, kname, rows, touched, act_bytes=4 if simt else 2)
         achieved = kbytes / (kms * 1e-3) / 1e9 if kms > 0 else 0.0
         roofline = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                     "peak_source": f"{peaks['source']} HBM copy bandwidth",
                     "algorithmic_bytes_per_launch": int(kbytes), "touched_experts": touched,
-                    "avg_ms": round(kms, 4)}
+                    "avg_ms": round(kms, 4), "traffic_source": traffic_ent}
+        if simt:
+            roofline["note"] = ("Float32 experts: FFMA kernels; the layer's weights and rows fit in L2, so this "
+                                "is a warm-L2 rate against the HBM copy peak")
     else:
         kflops = rows * (4.0 if kname == "expert_gate_up" else 2.0) * cfg.d * cfg.h
         achieved = kflops / (kms * 1e-3) / 1e12 if kms > 0 else 0.0
@@ -372,7 +377,9 @@ def main():
                     "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                     "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": traffic,
                     "peak_source": f"{peaks['source']} bf16 sustained (kernel timed inside a long step loop)",
-                    "algorithmic_flops_per_launch": kflops, "avg_ms": round(kms, 4)}
+                    "algorithmic_flops_per_launch": kflops, "avg_ms": round(kms, 4),
+                    "algorithmic_bytes_per_launch": int(kernel_bytes(cfg, kname, rows, cfg.n_shared + cfg.n_routed)),
+                    "traffic_source": traffic_ent}
 
     cpu_baseline = None
     if want_cpu:
@@ -436,6 +443,15 @@ def workload_config(cfg, world: int, mode: str, replicas=()) -> dict:
             "l2": l2_note(cfg)}
 
 
+def kernel_bytes(cfg, kernel: str, rows: int, touched: int, act_bytes: int = 2) -> float:
+    """Algorithmic bytes of one expert-kernel launch: the touched experts'
+    weights of that kernel (codes + one float32 scale per 16 values) plus its
+    activation rows read and written."""
+    bpv = {0: 8.0, 1: 4.0, 2: 1.0 + 4 / 16, 3: 0.5 + 4 / 16}[cfg.precision]
+    n_layers, k_in, n_out = (2, cfg.d, cfg.h) if kernel == "expert_gate_up" else (1, cfg.h, cfg.d)
+    return touched * n_layers * cfg.h * cfg.d * bpv + rows * (k_in + n_out) * act_bytes
+
+
 def decode_shaped(cfg) -> bool:
     """A few tokens per expert: the forward streams expert weights (HBM-bound)."""
     return cfg.T <= 64
@@ -469,7 +485,8 @@ def profiled_traffic(kernel: str, config: str, T_local: int):
         return None
     if int(ent["tokens"]) != int(T_local):
         return None
-    return int(ent["bytes_per_launch"])
+    return {"bytes": int(ent["bytes_per_launch"]), "source": ent["source"],
+            **({"scaled_from": ent["scaled_from"]} if "scaled_from" in ent else {})}
 
 
 def host_spec_and_sample(cfg, n_tokens: int, threads: int, seed: int = 7):

@@ -536,7 +536,6 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
         dc.yp = h->yp.p;
         dc.sms = h->tc.sms;
         dc.err = h->tc.err;
-        dc.max_rows = (int)T;
         GT_CHECK(h->phase_begin(3));
         GT_CHECK(launch_decode(dc, 1, st));
         GT_CHECK(h->phase_end(3));

@@ -22,17 +22,13 @@
 //
 // Work unit: (16-row tile of a group, block of 64 output features = one
 // 64-row half of a weight chunk).  A CTA of eight compute warps and one
-// producer warp runs a contiguous range of units, so consecutive units mostly
-// share a tile (a tile's feature blocks are consecutive units).  The producer
-// copies a tile's token rows once per tile (one bulk copy per row, all
-// inputs; padded rows: conflict-free fragment loads) and keeps a ring of
-// weight steps, one contiguous bulk copy per layer per 128-input step (gate
-// and up for kernel 1; the records of consecutive k-blocks of a 64-row half
-// are adjacent): the TMA engine's rate per CTA grows with the size of each
-// copy, so few large copies replace many small ones.  The token tile holds
-// min(16, T) rows and the ring takes the rest of the shared memory of two
-// CTAs per SM (2-8 stages): the bytes in flight per SM are what bound a
-// weight-streaming kernel.  "full" mbarriers carry the transaction counts,
+// producer warp runs a unit.  The producer copies the tile's token rows once
+// per unit (one bulk copy per row, all inputs; padded rows: conflict-free
+// fragment loads) and keeps a 2-stage ring of weight steps, one contiguous
+// bulk copy per layer per 128-input step (gate and up for kernel 1; the
+// records of consecutive k-blocks of a 64-row half are adjacent): the TMA
+// engine's rate per CTA grows with the size of each copy, so few large copies
+// replace many small ones.  "full" mbarriers carry the transaction counts,
 // "empty" ones are released by each compute warp; no CTA-wide barrier.  The
 // tokens are the MMA's M side (16 per m-tile) and the weights its N side:
 // warp w owns features 8w..8w+7, so each lane decodes one weight row per
@@ -52,8 +48,7 @@ constexpr int kComputeWarps = 8;                          // 8 features each
 constexpr int kDecodeThreads = (kComputeWarps + 1) * 32;  // + one producer warp
 constexpr int kDecodeFeatures = kHalfRows;               // output features per unit
 constexpr int kDecodeStepKB = 2;                          // 64-input k-blocks per weight step
-constexpr int kMaxDecodeStages = 8;
-constexpr int kDecodeCtaSmem = 113 * 1024;  // shared memory per CTA at two CTAs per SM
+constexpr int kDecodeStages = 2;
 
 template <int PREC>
 struct DecodeLayout {
@@ -140,17 +135,16 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     const __nv_bfloat16 *xin = (const __nv_bfloat16 *)(GATED ? a.xp : a.hp);
     __nv_bfloat16 *out = (__nv_bfloat16 *)(GATED ? a.hp : a.yp);
     const int64_t units = __ldg(a.tile_prefix + a.n_groups) * blocks;
-    const uint32_t NS = (uint32_t)a.stages;
-    uint8_t *xs = dsmem;                                      // a.tile_rows x xpitch
-    uint8_t *ring = dsmem + a.tile_rows * xpitch;             // a.stages x ST::kBytes
+    uint8_t *xs = dsmem;                                      // kDecodeTileRows x xpitch
+    uint8_t *ring = dsmem + kDecodeTileRows * xpitch;         // kDecodeStages x ST::kBytes
 
-    __shared__ uint64_t full[kMaxDecodeStages];   // weight step landed (expect_tx by the producer)
-    __shared__ uint64_t empty[kMaxDecodeStages];  // every compute warp is done with the step
-    __shared__ uint64_t xfull, xempty;            // token rows of a tile landed / released
-    __shared__ float rscale[kDecodeTileRows];     // 2^-e of each token row (f16 tile = bf16 row * 2^e)
+    __shared__ uint64_t full[kDecodeStages];   // weight step landed (expect_tx by the producer)
+    __shared__ uint64_t empty[kDecodeStages];  // every compute warp is done with the step
+    __shared__ uint64_t xfull, xempty;         // token rows of the unit landed / released
+    __shared__ float rscale[kDecodeTileRows];  // 2^-e of each token row (f16 tile = bf16 row * 2^e)
     __shared__ int abort_flag;
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < NS; s++) {
+        for (int s = 0; s < kDecodeStages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kComputeWarps);
         }
@@ -161,20 +155,13 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     }
     __syncthreads();
     volatile int *abort_p = (volatile int *)&abort_flag;
-    uint32_t n = 0;      // weight steps of this CTA so far: slot = n % NS, parity = (n / NS) & 1
-    uint32_t nx = 0;     // token tiles of this CTA so far (token-row buffer parity)
-    int64_t cur_tile = -1;
-
-    // This CTA's units: a contiguous range (one unit per CTA while there are
-    // fewer units than CTAs, so that they spread over the SMs).
-    const int64_t G = gridDim.x, b = blockIdx.x;
-    const int64_t u_begin = units < G ? b : b * units / G;
-    const int64_t u_end = units < G ? (b < units ? b + 1 : b) : (b + 1) * units / G;
+    uint32_t n = 0;      // weight steps of this CTA so far: slot = n % S, parity = (n / S) & 1
+    uint32_t nu = 0;     // units of this CTA so far (token-row buffer parity)
 
     // Every warp walks all of this CTA's units, also after an abort (its
     // waits then return at once): the compute warps' named barrier is
     // reached by all eight of them, whatever each one saw of the flag.
-    for (int64_t u = u_begin; u < u_end; u++) {
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x, nu++) {
         const int64_t tile = u / blocks;
         const int fb = (int)(u % blocks);
         const int gi = unit_group(a.tile_prefix, a.n_groups, tile);
@@ -182,11 +169,6 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
         const ExpertLayers &L = a.experts[grp.expert];
         const int64_t r0 = (tile - __ldg(a.tile_prefix + gi)) * kDecodeTileRows;  // first row of this tile
         const int m = grp.m - r0 < kDecodeTileRows ? (int)(grp.m - r0) : kDecodeTileRows;
-        const bool new_tile = tile != cur_tile;  // the same for every warp
-        // the next unit of this CTA has another tile (or there is none): the
-        // token rows are released after this unit
-        const bool last_use = u + 1 >= u_end || (u + 1) / blocks != tile;
-        cur_tile = tile;
 
         if (warp == kComputeWarps) {
             // ---- producer
@@ -195,19 +177,15 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             const uint8_t *w0 = L.tiled[which] + (int64_t)(2 * nt + half) * KB * DL::kHalf;
             const uint8_t *w1 = GATED ? L.tiled[1] + (int64_t)(2 * nt + half) * KB * DL::kHalf : nullptr;
             const uint8_t *xrow0 = (const uint8_t *)(xin + ((GATED ? grp.x_row0 : grp.h_row0) + r0) * (int64_t)K);
-            if (new_tile) {
-                if (nx > 0 && !*abort_p) mbar_wait(&xempty, (nx - 1) & 1, abort_p, a.err, 13);
-                nx++;
-                if (*abort_p) continue;  // no new copies once a wait has given up
-                if (lane == 0) mbar_arrive_expect_tx(&xfull, (uint32_t)m * K * 2);
-                __syncwarp();
-                for (int r = lane; r < m; r += 32)
-                    bulk_copy(xs + r * xpitch, xrow0 + (int64_t)r * K * 2, K * 2, &xfull);
-            }
-            if (*abort_p) continue;
+            if (nu > 0 && !*abort_p) mbar_wait(&xempty, (nu - 1) & 1, abort_p, a.err, 13);
+            if (*abort_p) continue;  // no new copies once a wait has given up
+            if (lane == 0) mbar_arrive_expect_tx(&xfull, (uint32_t)m * K * 2);
+            __syncwarp();
+            for (int r = lane; r < m; r += 32) bulk_copy(xs + r * xpitch, xrow0 + (int64_t)r * K * 2, K * 2, &xfull);
             for (int kb = 0; kb < KB; kb += kDecodeStepKB, n++) {
-                const uint32_t slot = n % NS;
-                if (n >= NS && !*abort_p) mbar_wait(&empty[slot], ((n / NS) - 1) & 1, abort_p, a.err, 10);
+                const uint32_t slot = n % kDecodeStages;
+                if (n >= kDecodeStages && !*abort_p)
+                    mbar_wait(&empty[slot], ((n / kDecodeStages) - 1) & 1, abort_p, a.err, 10);
                 if (*abort_p) break;
                 if (lane == 0) {
                     uint8_t *st = ring + slot * ST::kBytes;
@@ -228,13 +206,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
 #pragma unroll
             for (int c = 0; c < 4; c++) acc[l][c] = 0.f;
         const int row = warp * 8 + g8;  // this lane's weight row (feature) in the half
-        if (new_tile) {
-            if (!*abort_p) mbar_wait(&xfull, nx & 1, abort_p, a.err, 14);
-            nx++;
-            // bf16 token rows -> f16 in place, each row scaled by the power of two
-            // that puts its largest magnitude in [2^14, 2^15): exact, no overflow
+        if (!*abort_p) mbar_wait(&xfull, nu & 1, abort_p, a.err, 14);
+        // bf16 token rows -> f16 in place, each row scaled by the power of two
+        // that puts its largest magnitude in [2^14, 2^15): exact, no overflow
 #pragma unroll
-            for (int rr = 0; rr < 2; rr++) {
+        for (int rr = 0; rr < 2; rr++) {
             const int r = warp + kComputeWarps * rr;
             if (r >= m) continue;
             uint32_t *p = reinterpret_cast<uint32_t *>(xs + r * xpitch);
@@ -252,19 +228,15 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
                 const uint32_t v = p[i];
                 p[i] = pack_f16(__uint_as_float(v << 16) * up, __uint_as_float(v & 0xFFFF0000u) * up);
             }
-                if (lane == 0) rscale[r] = __uint_as_float((uint32_t)(127 - e) << 23);
-            }
-            // the producer's next copies into the tile come after these writes
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
+            if (lane == 0) rscale[r] = __uint_as_float((uint32_t)(127 - e) << 23);
         }
-        // fragment rows g8 and g8 + 8; rows past the tile (all past the group's
-        // last row) read the tile's last row: their products are not stored
-        const uint8_t *xrow = xs + min(g8, a.tile_rows - 1) * xpitch + 8 * q;
-        const uint8_t *xrow_hi = xs + min(g8 + 8, a.tile_rows - 1) * xpitch + 8 * q;
+        // the producer's next copies into the tile come after these writes
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
+        const uint8_t *xrow = xs + g8 * xpitch + 8 * q;
         for (int kb0 = 0; kb0 < KB; kb0 += kDecodeStepKB, n++) {
-            const uint32_t slot = n % NS;
-            if (!*abort_p) mbar_wait(&full[slot], (n / NS) & 1, abort_p, a.err, 9);
+            const uint32_t slot = n % kDecodeStages;
+            if (!*abort_p) mbar_wait(&full[slot], (n / kDecodeStages) & 1, abort_p, a.err, 9);
             if (*abort_p) break;
             const uint8_t *st = ring + slot * ST::kBytes;
 #pragma unroll
@@ -277,8 +249,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
                                                               half_scale_off(row, DL::kCodeBytes));
 #pragma unroll
                 for (int s = 0; s < 4; s++) {
-                    const uint2 lo = *reinterpret_cast<const uint2 *>(xrow + kb * 128 + 32 * s);
-                    const uint2 hi = *reinterpret_cast<const uint2 *>(xrow_hi + kb * 128 + 32 * s);
+                    const uint8_t *xa = xrow + kb * 128 + 32 * s;
+                    const uint2 lo = *reinterpret_cast<const uint2 *>(xa);
+                    const uint2 hi = *reinterpret_cast<const uint2 *>(xa + 8 * xpitch);
                     const uint32_t af[4] = {lo.x, hi.x, lo.y, hi.y};
 #pragma unroll
                     for (int l = 0; l < ST::kLayers; l++) {
@@ -292,11 +265,12 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
-        // epilogue: acc[l] = tokens (r0 + g8, r0 + g8 + 8) x features (f, f + 1),
-        // in units of the rows' scales (read before the rows are released)
-        const float rs0 = rscale[g8], rs1 = rscale[g8 + 8];
         __syncwarp();
-        if (last_use && lane == 0) mbar_arrive(&xempty);
+        if (lane == 0) mbar_arrive(&xempty);
+
+        // epilogue: acc[l] = tokens (r0 + g8, r0 + g8 + 8) x features (f, f + 1),
+        // in units of the rows' scales
+        const float rs0 = rscale[g8], rs1 = rscale[g8 + 8];
 #pragma unroll
         for (int l = 0; l < 2; l++) {
             acc[l][0] *= rs0;
@@ -332,26 +306,14 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     }
 }
 
-// Token tile of min(16, T) rows; the weight ring takes the rest of the
-// shared memory of two CTAs per SM, 2 to kMaxDecodeStages stages.
-template <int PREC, bool GATED>
-void decode_plan(DecodeArgs &a) {
-    a.tile_rows = a.max_rows < kDecodeTileRows ? (a.max_rows < 1 ? 1 : a.max_rows) : kDecodeTileRows;
-    const int tile = a.tile_rows * decode_x_pitch(GATED ? a.d : a.h);
-    int stages = (kDecodeCtaSmem - tile) / DecodeStage<PREC, GATED>::kBytes;
-    a.stages = stages < 2 ? 2 : stages > kMaxDecodeStages ? kMaxDecodeStages : stages;
-}
-
 template <int PREC, bool GATED>
 int decode_smem_bytes(const DecodeArgs &a) {
-    return a.tile_rows * decode_x_pitch(GATED ? a.d : a.h) + a.stages * DecodeStage<PREC, GATED>::kBytes;
+    return kDecodeTileRows * decode_x_pitch(GATED ? a.d : a.h) + kDecodeStages * DecodeStage<PREC, GATED>::kBytes;
 }
 
 template <int PREC, bool GATED>
-int launch_decode_one(const DecodeArgs &args, cudaStream_t st) {
+int launch_decode_one(const DecodeArgs &a, cudaStream_t st) {
     auto kern = decode_kernel<PREC, GATED>;
-    DecodeArgs a = args;
-    decode_plan<PREC, GATED>(a);
     const int smem = decode_smem_bytes<PREC, GATED>(a);
     static int attr = 0;
     if (smem > attr) {
@@ -371,7 +333,7 @@ int launch_decode_one(const DecodeArgs &args, cudaStream_t st) {
 bool decode_usable(int precision, int d, int h, int64_t T) {
     // the token tile of a unit (16 rows x all inputs) and the weight ring fit in shared memory
     const int kmax = d > h ? d : h;
-    const int smem = kDecodeTileRows * decode_x_pitch(kmax) + 2 * DecodeStage<GTMOE_INT8, true>::kBytes;
+    const int smem = kDecodeTileRows * decode_x_pitch(kmax) + kDecodeStages * DecodeStage<GTMOE_INT8, true>::kBytes;
     return (precision == GTMOE_INT8 || precision == GTMOE_FP4) && T <= kDecodeMaxRows &&
            d % (64 * kDecodeStepKB) == 0 && h % (64 * kDecodeStepKB) == 0 && d % 128 == 0 && h % 128 == 0 &&
            smem <= 200 * 1024;

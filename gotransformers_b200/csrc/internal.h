@@ -109,9 +109,6 @@ struct DecodeArgs {
     void *yp;        // bf16 rows x d
     int sms;
     int *err;  // device flag: nonzero when a bounded wait expired
-    int max_rows;  // rows of the largest group (the batch's T): sizes the token tile
-    // set by launch_decode: token-tile rows and weight-ring stages in shared memory
-    int tile_rows = kDecodeTileRows, stages = 2;
 };
 bool decode_usable(int precision, int d, int h, int64_t T);
 int launch_decode(const DecodeArgs &a, int which, cudaStream_t st);  // which: 1 gate/up, 2 down

@@ -92,8 +92,9 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void *__restri
     }
 }
 
-// Few tokens (decode-shaped batches): one warp per (token, expert) instead of
-// 64 x 64 tiles, so that the whole GPU works on a handful of tokens.  The
+// Few tokens (decode-shaped batches) or few experts: one warp per (token,
+// expert) instead of 64 x 64 tiles, so that the whole GPU works on a handful
+// of tokens, or on a router with fewer than 64 experts.  The
 // arithmetic is router_logits_kernel's, operation for operation: float32
 // sums of each 16-input block by sequential fmaf from zero, then the blocks
 // added in float64 in input order -- both kernels give the same bits.
@@ -198,14 +199,52 @@ __device__ __forceinline__ void load_scores(const double *__restrict__ logits, c
     }
 }
 
+// ||x_t|| for the error margin.  bf16 rows (16-byte aligned, d a multiple of
+// 8) are read 16 bytes per lane with four loads in flight; other rows by
+// element, unrolled by four.  Squares of bf16/float32 values are exact in
+// float64; only the sum rounds (far below the margin's slack).
 template <int XDT>
 __device__ __forceinline__ double warp_x_norm(const void *__restrict__ x, int64_t t, int d) {
     const int lane = threadIdx.x & 31;
-    double ss = 0;
-    for (int i = lane; i < d; i += 32) {
-        double v = load_as_double(x, XDT, t * d + i);
-        ss += v * v;
+    double s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+    if (XDT == GTMOE_DTYPE_BF16 && (d & 7) == 0 && (((uintptr_t)x) & 15) == 0) {
+        const uint4 *row = reinterpret_cast<const uint4 *>((const __nv_bfloat16 *)x + t * d);
+        const int nv = d >> 3;
+        auto sq8 = [](const uint4 v) {
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            double a = 0;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const double lo = (double)__uint_as_float(w[q] << 16), hi = (double)__uint_as_float(w[q] & 0xFFFF0000u);
+                a += lo * lo + hi * hi;
+            }
+            return a;
+        };
+        int i = lane;
+        for (; i + 96 < nv; i += 128) {
+            const uint4 v0 = __ldg(row + i), v1 = __ldg(row + i + 32), v2 = __ldg(row + i + 64), v3 = __ldg(row + i + 96);
+            s0 += sq8(v0);
+            s1 += sq8(v1);
+            s2 += sq8(v2);
+            s3 += sq8(v3);
+        }
+        for (; i < nv; i += 32) s0 += sq8(__ldg(row + i));
+    } else {
+        int i = lane;
+        for (; i + 96 < d; i += 128) {
+            const double v0 = load_as_double(x, XDT, t * d + i), v1 = load_as_double(x, XDT, t * d + i + 32);
+            const double v2 = load_as_double(x, XDT, t * d + i + 64), v3 = load_as_double(x, XDT, t * d + i + 96);
+            s0 += v0 * v0;
+            s1 += v1 * v1;
+            s2 += v2 * v2;
+            s3 += v3 * v3;
+        }
+        for (; i < d; i += 32) {
+            const double v = load_as_double(x, XDT, t * d + i);
+            s0 += v * v;
+        }
     }
+    double ss = (s0 + s1) + (s2 + s3);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     return sqrt(ss);
@@ -449,7 +488,9 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
     }
     if (a.use_tc) {
         GT_CHECK(launch_router_logits_tc(a.x, a.T, a.d, a.E, a.e_pad, a.w3, a.logits, a.err, a.sms, st));
-    } else if (a.T <= kRouterSmallT) {
+    } else if ((a.T <= kRouterSmallT || a.E < kRouterTile) && a.T <= 65535) {  // grid.y holds the tokens
+        // few tokens, or fewer experts than one 64-wide tile (the tile kernel
+        // would launch T/64 CTAs and leave most of each tile empty)
         dim3 grid((unsigned)((a.E + kRouterSmallWarps - 1) / kRouterSmallWarps), (unsigned)a.T);
         const size_t smem = sizeof(float) * kRouterSmallWarps * ((a.d + kRouterK - 1) / kRouterK);
         if (smem > 48 * 1024) return fail(GTMOE_EINVAL, "router: d_model %d too large", a.d);

@@ -1,12 +1,13 @@
 """The Go drop-in's call sequence, replayed by a C program
 (wrapper_sequence.c) that includes include/gtmoe.h and links libgtmoe.so.
 
-The mixture is the reference's usual training-around-frozen-experts flow:
+The mixture is the reference's training-around-frozen-layers flow:
 NewClampedMixtureOfExperts (clamped SwiGLU experts, mixtureofexperts.go:40),
 a router that Model.CompressWeights compressed to Int8 (transformer/
-memory.go:25-34), uncompressed Float64 expert layers frozen with FreezeBase,
-then Forward, Backward (router gradients accumulated), LastExpertLoad and
-UpdateBalance.  On a machine without a GPU the program must stop at
+memory.go:25-34) and that is therefore frozen (FreezeBase: a compressed layer
+that is not frozen panics in Backward, perceptron/layer.go:164-167, and gets
+no gradients when it is, :184), uncompressed Float64 expert layers frozen
+with FreezeBase, then Forward, Backward, LastExpertLoad and UpdateBalance.  On a machine without a GPU the program must stop at
 gtmoe_create with GTMOE_ENODEVICE; on a B200 its results must match the
 oracle's Forward and Backward (mixtureofexperts.go:122-216, :227-285) and
 balance update (:293-310)."""
@@ -62,10 +63,10 @@ def _case():
     return spec, x, ids, dout
 
 
-def _write_model(path, spec, x, ids, dout, gate_activation=None):
+def _write_model(path, spec, x, ids, dout, gate_activation=None, freeze_router=True):
     out = bytearray(b"GTMW")
     out += struct.pack("<6i", spec.d, spec.h, spec.n_shared, spec.n_routed, spec.k, int(spec.hash_routing))
-    _layer(out, "moe.router", "Linear", spec.router, freeze=False, compressed=True)
+    _layer(out, "moe.router", "Linear", spec.router, freeze=freeze_router, compressed=True)
     out += np.ascontiguousarray(spec.balance, "<f8").tobytes()
     for e, layers in enumerate(spec.experts):
         base = f"moe.shared{e + 1}" if e < spec.n_shared else f"moe.expert{e - spec.n_shared + 1}"
@@ -133,9 +134,12 @@ def test_wrapper_sequence_matches_oracle(tmp_path):
     assert rel_l2(out, ref["out"]) <= 1e-5  # Float64 experts
     assert np.array_equal(load, ref["load"])
     bref = O.moe_backward(spec, x, dout)
-    assert rel_l2(dx, bref["dx"]) <= 1e-9
-    assert rel_l2(wg, bref["router_weight_grad"]) <= 1e-9
-    assert rel_l2(bg, bref["router_bias_grad"]) <= 1e-9
+    assert rel_l2(dx, bref["dx"]) <= 1e-9  # input gradients still go through the frozen router
+    assert not wg.any() and not bg.any()  # a frozen router accumulates no gradients
     want = spec.balance.copy()
     O.update_balance(want, ref["load"], RATE)
     assert np.array_equal(balance, want)
+    # a compressed router that is not frozen: the reference's Backward panics
+    _write_model(tmp_path / "unfrozen.bin", spec, x, ids, dout, freeze_router=False)
+    r = subprocess.run([exe, str(tmp_path / "unfrozen.bin"), str(tmp_path / "o.bin")], capture_output=True, text=True)
+    assert r.returncode == 1 and "weights are compressed for running the model" in r.stderr, r.stderr
