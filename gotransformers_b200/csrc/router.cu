@@ -92,9 +92,8 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void *__restri
     }
 }
 
-// Few tokens (decode-shaped batches) or few experts: one warp per (token,
-// expert) instead of 64 x 64 tiles, so that the whole GPU works on a handful
-// of tokens, or on a router with fewer than 64 experts.  The
+// Few tokens (decode-shaped batches): one warp per (token, expert) instead of
+// 64 x 64 tiles, so that the whole GPU works on a handful of tokens.  The
 // arithmetic is router_logits_kernel's, operation for operation: float32
 // sums of each 16-input block by sequential fmaf from zero, then the blocks
 // added in float64 in input order -- both kernels give the same bits.
@@ -130,6 +129,47 @@ __global__ void __launch_bounds__(kRouterSmallWarps * 32)
         for (int b = 0; b < nb; b++) acc += (double)mine[b];
         logits[t * E + e] = acc;
     }
+}
+
+// Many tokens and at most 64 experts: one warp per token, one lane per expert
+// (two for 33-64 experts), the router weights input-major (w32t[i * E + e]) so
+// that each load of a lane's weight coalesces across the warp, and every lane
+// reads the same x value.  Per expert the arithmetic is router_logits_kernel's
+// operation for operation -- float32 sums of each 16-input block by sequential
+// fmaf from zero (inputs past d as zero products), the blocks added in float64
+// in input order -- so all three logits kernels give the same bits.  (The
+// 64 x 64 tile kernel would launch only T/64 CTAs here and leave most of each
+// tile's expert columns empty.)
+constexpr int kRouterLanesMaxE = 64;
+
+template <int XDT>
+__global__ void __launch_bounds__(256) router_logits_lanes_kernel(const void *__restrict__ x,
+                                                                  const float *__restrict__ w32t, int64_t T, int E,
+                                                                  int d, double *__restrict__ logits) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (t >= T) return;
+    const int e0 = lane, e1 = lane + 32;
+    const bool has0 = e0 < E, has1 = e1 < E;
+    double acc0 = 0.0, acc1 = 0.0;
+    const int nb = (d + kRouterK - 1) / kRouterK;
+    for (int b = 0; b < nb; b++) {
+        float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < kRouterK; c++) {
+            const int kk = b * kRouterK + c;
+            const bool in = kk < d;
+            const float xv = in ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
+            const float w0 = in && has0 ? __ldg(w32t + (int64_t)kk * E + e0) : 0.f;
+            const float w1 = in && has1 ? __ldg(w32t + (int64_t)kk * E + e1) : 0.f;
+            p0 = fmaf(xv, w0, p0);
+            p1 = fmaf(xv, w1, p1);
+        }
+        acc0 += (double)p0;
+        acc1 += (double)p1;
+    }
+    if (has0) logits[t * E + e0] = acc0;
+    if (has1) logits[t * E + e1] = acc1;
 }
 
 // activationfunction/moreactivationfunctions.go:8-16, mixtureofexperts.go:80-82
@@ -488,9 +528,7 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
     }
     if (a.use_tc) {
         GT_CHECK(launch_router_logits_tc(a.x, a.T, a.d, a.E, a.e_pad, a.w3, a.logits, a.err, a.sms, st));
-    } else if ((a.T <= kRouterSmallT || a.E < kRouterTile) && a.T <= 65535) {  // grid.y holds the tokens
-        // few tokens, or fewer experts than one 64-wide tile (the tile kernel
-        // would launch T/64 CTAs and leave most of each tile empty)
+    } else if (a.T <= kRouterSmallT) {
         dim3 grid((unsigned)((a.E + kRouterSmallWarps - 1) / kRouterSmallWarps), (unsigned)a.T);
         const size_t smem = sizeof(float) * kRouterSmallWarps * ((a.d + kRouterK - 1) / kRouterK);
         if (smem > 48 * 1024) return fail(GTMOE_EINVAL, "router: d_model %d too large", a.d);
@@ -503,6 +541,16 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
         else
             router_logits_small_kernel<GTMOE_DTYPE_BF16><<<grid, kRouterSmallWarps * 32, smem, st>>>(
                 a.x, a.w32, a.T, a.E, a.d, a.logits);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+    } else if (a.E <= kRouterLanesMaxE && a.w32t) {
+        const unsigned blocks = (unsigned)((a.T * 32 + 255) / 256);
+        if (a.x_dtype == GTMOE_DTYPE_F64)
+            router_logits_lanes_kernel<GTMOE_DTYPE_F64><<<blocks, 256, 0, st>>>(a.x, a.w32t, a.T, a.E, a.d, a.logits);
+        else if (a.x_dtype == GTMOE_DTYPE_F32)
+            router_logits_lanes_kernel<GTMOE_DTYPE_F32><<<blocks, 256, 0, st>>>(a.x, a.w32t, a.T, a.E, a.d, a.logits);
+        else
+            router_logits_lanes_kernel<GTMOE_DTYPE_BF16><<<blocks, 256, 0, st>>>(a.x, a.w32t, a.T, a.E, a.d, a.logits);
         GT_CUDA(cudaGetLastError());
         note_launches(1);
     } else {
