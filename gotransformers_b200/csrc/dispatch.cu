@@ -98,8 +98,73 @@ __global__ void dispatch_scatter_kernel(const int32_t *__restrict__ chosen, cons
     }
 }
 
+// A batch of at most one chunk (decode-shaped): count, scan and scatter of
+// the three kernels above in one CTA, with the same arithmetic and the same
+// outputs, so that a small forward pays one launch for its dispatch.
+__global__ void __launch_bounds__(1024) dispatch_small_kernel(const int32_t *__restrict__ chosen, int64_t T, int E,
+                                                              int k, int S, int bm, int64_t *__restrict__ load,
+                                                              int64_t *__restrict__ offsets, Group *__restrict__ groups,
+                                                              int64_t *__restrict__ tile_prefix,
+                                                              int32_t *__restrict__ perm, int64_t *__restrict__ slot_row) {
+    extern __shared__ int64_t base[];  // E: next position of each expert's rows
+    int32_t *cnt = reinterpret_cast<int32_t *>(base + E);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int64_t p = threadIdx.x; p < T * k; p += blockDim.x) atomicAdd(&cnt[chosen[p]], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int64_t xbase = S > 0 ? T : 0;
+        int64_t off = 0, tiles = 0;
+        for (int s = 0; s < S; s++) {
+            groups[s] = Group{0, (int64_t)s * T, T, s, 0};
+            tile_prefix[s] = tiles;
+            tiles += (T + bm - 1) / bm;
+        }
+        for (int e = 0; e < E; e++) {
+            const int64_t n = cnt[e];
+            load[e] = n;
+            offsets[e] = off;
+            base[e] = off;
+            groups[S + e] = Group{xbase + off, (int64_t)S * T + off, n, S + e, 0};
+            tile_prefix[S + e] = tiles;
+            tiles += (n + bm - 1) / bm;
+            off += n;
+        }
+        offsets[E] = off;
+        tile_prefix[S + E] = tiles;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {  // the scatter of dispatch_scatter_kernel, one warp over the chunk
+        const int lane = threadIdx.x;
+        const uint32_t lt = (1u << lane) - 1u;
+        for (int64_t p0 = 0; p0 < T * k; p0 += 32) {
+            const int64_t p = p0 + lane;
+            const bool valid = p < T * k;
+            const int e = valid ? chosen[p] : -1;
+            const uint32_t peers = __match_any_sync(0xffffffffu, e);
+            const int rank = __popc(peers & lt);
+            int64_t pos = 0;
+            if (valid) pos = base[e] + rank;
+            __syncwarp();
+            if (valid) {
+                perm[pos] = (int32_t)(p / k);
+                slot_row[p] = pos;
+                if (rank == 0) base[e] += __popc(peers);
+            }
+            __syncwarp();
+        }
+    }
+}
+
 int launch_dispatch(const DispatchArgs &a, cudaStream_t st) {
     int n_chunks = (int)((a.T + kDispatchChunk - 1) / kDispatchChunk);
+    if (a.T > 0 && a.T <= kDispatchChunk) {
+        dispatch_small_kernel<<<1, 1024, a.E * (sizeof(int64_t) + sizeof(int32_t)), st>>>(
+            a.chosen, a.T, a.E, a.k, a.S, a.bm, a.load, a.offsets, a.groups, a.tile_prefix, a.perm, a.slot_row);
+        GT_CUDA(cudaGetLastError());
+        note_launches(1);
+        return 0;
+    }
     if (a.T > 0) {
         dispatch_count_kernel<<<n_chunks, 256, a.E * sizeof(int32_t), st>>>(a.chosen, a.T, a.E, a.k, a.chunk_counts);
         GT_CUDA(cudaGetLastError());

@@ -323,34 +323,6 @@ __device__ __forceinline__ void write_choice(int64_t t, int k, int *pick, double
     }
 }
 
-// One warp per token: scores from the fast logits, top-(k+1), and either the
-// final choice or, when the k-th and (k+1)-th scores are within the error
-// margin, the token's index on the fix-up list.
-template <int XDT, int MAXJ>
-__global__ void __launch_bounds__(256)
-    router_select_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
-                         const double *__restrict__ balance, int64_t T, int E, int k, const void *__restrict__ x, int d,
-                         double thresh_scale, int32_t *__restrict__ chosen, double *__restrict__ gates64,
-                         float *__restrict__ gates32, int *__restrict__ flagged, int *__restrict__ n_flagged) {
-    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (t >= T) return;
-    double score[MAXJ], aff[MAXJ];
-    load_scores<XDT, MAXJ>(logits, bias, balance, t, E, score, aff);
-    int pick[kMaxTopK + 1];
-    double pscore[kMaxTopK + 1], paff[kMaxTopK + 1];
-    const int count = k < E ? k + 1 : k;
-    warp_top<MAXJ>(score, aff, 0u, E, count, pick, pscore, paff);
-    if (k < E) {
-        const double thresh = thresh_scale * warp_x_norm<XDT>(x, t, d);
-        if (!(pscore[k - 1] - pscore[k] > thresh)) {
-            if (lane == 0) flagged[atomicAdd(n_flagged, 1)] = (int)t;
-            return;
-        }
-    }
-    write_choice(t, k, pick, paff, chosen, gates64, gates32);
-}
-
 // x[x0 .. x0+d) . w[0 .. d) as one sequential float64 sum, each product and
 // each partial sum rounded separately, in input order (vectormath.DotProduct,
 // vector.go:67-74), by the whole warp: lane l fetches inputs 32b+l of every
@@ -400,71 +372,115 @@ __device__ double exact_dot_warp(const void *x, int64_t x0, const double *__rest
 // sum, vectormath.DotProduct, vector.go:67-74), and fill the remaining places
 // by exact score, ties to the lower index.
 template <int XDT, int MAXJ>
+__device__ void fixup_token(int64_t t, const double *__restrict__ logits, const double *__restrict__ bias,
+                            const double *__restrict__ balance, int E, int k, const void *__restrict__ x, int d,
+                            const double *__restrict__ w64, double thresh_scale, int32_t *__restrict__ chosen,
+                            double *__restrict__ gates64, float *__restrict__ gates32, double *wbuf) {
+    const int lane = threadIdx.x & 31;
+    double score[MAXJ], aff[MAXJ];
+    load_scores<XDT, MAXJ>(logits, bias, balance, t, E, score, aff);
+    int pick[kMaxTopK + 1];
+    double pscore[kMaxTopK + 1], paff[kMaxTopK + 1];
+    warp_top<MAXJ>(score, aff, 0u, E, k + 1, pick, pscore, paff);
+    const double thresh = thresh_scale * warp_x_norm<XDT>(x, t, d);
+    const double L = pscore[k - 1], U = pscore[k];
+    uint32_t sure = 0, unsure = 0;
+#pragma unroll
+    for (int j = 0; j < MAXJ; j++) {
+        const int e = lane + 32 * j;
+        if (e >= E) continue;
+        if (score[j] > U + thresh) sure |= 1u << j;
+        else if (!(score[j] < L - thresh)) unsure |= 1u << j;
+    }
+#pragma unroll
+    for (int j = 0; j < MAXJ; j++) {
+        uint32_t todo = __ballot_sync(0xffffffffu, (unsure >> j) & 1u);
+        while (todo) {
+            const int src = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const int e = src + 32 * j;
+            double s = exact_dot_warp<XDT>(x, t * d, w64 + (int64_t)e * d, d, wbuf, lane);
+            if (lane == src) {
+                s = __dadd_rn(s, bias[e]);
+                aff[j] = affinity_d(s);
+                score[j] = aff[j] + balance[e];
+            }
+        }
+    }
+    int n_sure = 0;
+#pragma unroll
+    for (int j = 0; j < MAXJ; j++) n_sure += __popc(__ballot_sync(0xffffffffu, (sure >> j) & 1u));
+    // the sure experts first (any order), then the best unsure ones
+    int npick = 0;
+#pragma unroll
+    for (int j = 0; j < MAXJ; j++) {
+        uint32_t bal = __ballot_sync(0xffffffffu, (sure >> j) & 1u);
+        while (bal) {
+            const int src = __ffs(bal) - 1;
+            bal &= bal - 1;
+            const double a = __shfl_sync(0xffffffffu, aff[j], src);
+            if (npick < kMaxTopK) {
+                pick[npick] = src + 32 * j;
+                paff[npick] = a;
+            }
+            npick++;
+        }
+    }
+    warp_top<MAXJ>(score, aff, ~unsure, E, k - n_sure, pick + n_sure, pscore, paff + n_sure);
+    write_choice(t, k, pick, paff, chosen, gates64, gates32);
+}
+
+template <int XDT, int MAXJ>
 __global__ void __launch_bounds__(256)
     router_fixup_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
                         const double *__restrict__ balance, int E, int k, const void *__restrict__ x, int d,
                         const double *__restrict__ w64, double thresh_scale, int32_t *__restrict__ chosen,
                         double *__restrict__ gates64, float *__restrict__ gates32, const int *__restrict__ flagged,
                         const int *__restrict__ n_flagged) {
-    const int lane = threadIdx.x & 31;
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int n = *n_flagged;
     __shared__ double wsum[8][32];  // per warp: one batch of products (exact_dot_warp)
     double *wbuf = wsum[threadIdx.x >> 5];
-    for (int wi = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); wi < n; wi += warps) {
-        const int64_t t = flagged[wi];
-        double score[MAXJ], aff[MAXJ];
-        load_scores<XDT, MAXJ>(logits, bias, balance, t, E, score, aff);
-        int pick[kMaxTopK + 1];
-        double pscore[kMaxTopK + 1], paff[kMaxTopK + 1];
-        warp_top<MAXJ>(score, aff, 0u, E, k + 1, pick, pscore, paff);
+    for (int wi = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); wi < n; wi += warps)
+        fixup_token<XDT, MAXJ>(flagged[wi], logits, bias, balance, E, k, x, d, w64, thresh_scale, chosen, gates64,
+                               gates32, wbuf);
+}
+
+// One warp per token: scores from the fast logits, top-(k+1), and either the
+// final choice or, when the k-th and (k+1)-th scores are within the error
+// margin, the token's index on the fix-up list -- or, for a small batch
+// (inline_fixup), the fix-up itself in this warp.
+template <int XDT, int MAXJ, bool INLINE_FIXUP>
+__global__ void __launch_bounds__(256)
+    router_select_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
+                         const double *__restrict__ balance, int64_t T, int E, int k, const void *__restrict__ x, int d,
+                         double thresh_scale, int32_t *__restrict__ chosen, double *__restrict__ gates64,
+                         float *__restrict__ gates32, int *__restrict__ flagged, int *__restrict__ n_flagged,
+                         const double *__restrict__ w64) {
+    __shared__ double wsum[INLINE_FIXUP ? 8 : 1][32];  // inline fix-up: per warp one batch of products
+    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (t >= T) return;
+    double score[MAXJ], aff[MAXJ];
+    load_scores<XDT, MAXJ>(logits, bias, balance, t, E, score, aff);
+    int pick[kMaxTopK + 1];
+    double pscore[kMaxTopK + 1], paff[kMaxTopK + 1];
+    const int count = k < E ? k + 1 : k;
+    warp_top<MAXJ>(score, aff, 0u, E, count, pick, pscore, paff);
+    if (k < E) {
         const double thresh = thresh_scale * warp_x_norm<XDT>(x, t, d);
-        const double L = pscore[k - 1], U = pscore[k];
-        uint32_t sure = 0, unsure = 0;
-#pragma unroll
-        for (int j = 0; j < MAXJ; j++) {
-            const int e = lane + 32 * j;
-            if (e >= E) continue;
-            if (score[j] > U + thresh) sure |= 1u << j;
-            else if (!(score[j] < L - thresh)) unsure |= 1u << j;
-        }
-#pragma unroll
-        for (int j = 0; j < MAXJ; j++) {
-            uint32_t todo = __ballot_sync(0xffffffffu, (unsure >> j) & 1u);
-            while (todo) {
-                const int src = __ffs(todo) - 1;
-                todo &= todo - 1;
-                const int e = src + 32 * j;
-                double s = exact_dot_warp<XDT>(x, t * d, w64 + (int64_t)e * d, d, wbuf, lane);
-                if (lane == src) {
-                    s = __dadd_rn(s, bias[e]);
-                    aff[j] = affinity_d(s);
-                    score[j] = aff[j] + balance[e];
-                }
+        if (!(pscore[k - 1] - pscore[k] > thresh)) {
+            if (INLINE_FIXUP) {
+                // small batches: this warp settles the token itself (one launch fewer)
+                fixup_token<XDT, MAXJ>(t, logits, bias, balance, E, k, x, d, w64, thresh_scale, chosen, gates64,
+                                       gates32, wsum[INLINE_FIXUP ? (threadIdx.x >> 5) : 0]);
+            } else if (lane == 0) {
+                flagged[atomicAdd(n_flagged, 1)] = (int)t;
             }
+            return;
         }
-        int n_sure = 0;
-#pragma unroll
-        for (int j = 0; j < MAXJ; j++) n_sure += __popc(__ballot_sync(0xffffffffu, (sure >> j) & 1u));
-        // the sure experts first (any order), then the best unsure ones
-        int npick = 0;
-#pragma unroll
-        for (int j = 0; j < MAXJ; j++) {
-            uint32_t bal = __ballot_sync(0xffffffffu, (sure >> j) & 1u);
-            while (bal) {
-                const int src = __ffs(bal) - 1;
-                bal &= bal - 1;
-                const double a = __shfl_sync(0xffffffffu, aff[j], src);
-                if (npick < kMaxTopK) {
-                    pick[npick] = src + 32 * j;
-                    paff[npick] = a;
-                }
-                npick++;
-            }
-        }
-        warp_top<MAXJ>(score, aff, ~unsure, E, k - n_sure, pick + n_sure, pscore, paff + n_sure);
-        write_choice(t, k, pick, paff, chosen, gates64, gates32);
     }
+    write_choice(t, k, pick, paff, chosen, gates64, gates32);
 }
 
 // hashedExperts (mixtureofexperts.go:88-96); gates 1/k (:148-151)
@@ -486,15 +502,24 @@ __global__ void hash_route_kernel(const int64_t *__restrict__ ids, int64_t T, in
     }
 }
 
+constexpr int64_t kInlineFixupT = 256;
+
 template <int XDT, int MAXJ>
 static int launch_select(const RouterArgs &a, cudaStream_t st) {
     unsigned sel_blocks = (unsigned)((a.T * 32 + 255) / 256);
     GT_CUDA(cudaMemsetAsync(a.n_fixups, 0, sizeof(int), st));
-    router_select_kernel<XDT, MAXJ><<<sel_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d,
-                                                                a.thresh_scale, a.chosen, a.gates64, a.gates32,
-                                                                a.flagged, a.n_fixups);
+    // a small batch has few tokens to settle: the select kernel's warps do it
+    const bool inline_fixup = a.T <= kInlineFixupT;
+    if (inline_fixup)
+        router_select_kernel<XDT, MAXJ, true><<<sel_blocks, 256, 0, st>>>(
+            a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d, a.thresh_scale, a.chosen, a.gates64, a.gates32,
+            a.flagged, a.n_fixups, a.w64);
+    else
+        router_select_kernel<XDT, MAXJ, false><<<sel_blocks, 256, 0, st>>>(
+            a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d, a.thresh_scale, a.chosen, a.gates64, a.gates32,
+            a.flagged, a.n_fixups, a.w64);
     GT_CUDA(cudaGetLastError());
-    if (a.k < a.E) {
+    if (a.k < a.E && !inline_fixup) {
         int64_t want = (a.T * 32 + 255) / 256;
         unsigned fix_blocks = (unsigned)(want < (int64_t)a.sms * 8 ? want : (int64_t)a.sms * 8);
         router_fixup_kernel<XDT, MAXJ><<<fix_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.E, a.k, a.x, a.d,
