@@ -55,6 +55,9 @@ def parse_args():
                    help="expert parallel: hot experts held on every rank ('auto': chosen from the config's expected "
                         "expert popularity, '0': none -- routed experts purely owned by index, or a number: the "
                         "hottest experts chosen the same way, at most that many)")
+    p.add_argument("--op", default="forward", choices=["forward", "block"],
+                   help="forward: MixtureOfExperts.Forward (gtmoe_forward); block: the block's feed-forward step "
+                        "x + Forward(RMSNorm(x)) (gtmoe_forward_block, one GPU)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     return p.parse_args()
@@ -225,6 +228,18 @@ def main():
     host = synthetic.load_config_on_gpu(cfg, moe, keep_host=want_cpu, device=local_rank)
     x = synthetic.make_x_on_gpu(cfg, T=T_local, offset_rows=rank * T_local, device=local_rank)
     out = torch.empty((T_local, cfg.d), dtype=torch.bfloat16, device=dev)
+    if args.op == "block":
+        if world > 1:
+            raise SystemExit("--op block runs on one GPU")
+        # the block's FeedForwardNorm: seeded RMSNorm weights around 1
+        moe.set_norm(1.0 + 0.1 * synthetic.normal(cfg.weight_seed, synthetic.STREAM_NORM, cfg.d), 1e-6)
+        out = torch.empty_like(x)  # the block's output has the input's dtype (x is the residual)
+
+    def step(xx, oo):
+        if args.op == "block":
+            moe.forward_block(xx, out=oo, want_routing=False)
+        else:
+            moe.forward(xx, out=oo, want_routing=False)
     # a dedicated stream: torch's default (legacy) stream has handle 0, which
     # the C ABI reads as "the handle's own stream"
     stream = torch.cuda.Stream(dev)
@@ -239,7 +254,7 @@ def main():
     # is running through the whole timed region, and stops right after it
     sampler = ClockSampler()
     for _ in range(args.warmup):
-        moe.forward(x, out=out, want_routing=False)
+        step(x, out)
     torch.cuda.synchronize(dev)
     barrier()
 
@@ -261,12 +276,12 @@ def main():
         for i in range(args.steps):
             flush_buf.fill_(i)
             evs[i][0].record(stream)
-            moe.forward(x, out=out, want_routing=False)
+            step(x, out)
             evs[i][1].record(stream)
     else:
         evs[0][0].record(stream)
         for _ in range(args.steps):
-            moe.forward(x, out=out, want_routing=False)
+            step(x, out)
         evs[0][1].record(stream)
     evs[-1][1].synchronize()
     torch.cuda.nvtx.range_pop()
@@ -284,16 +299,16 @@ def main():
     for i in range(min(args.steps, 5)):
         if flush:
             flush_buf.fill_(i)
-        moe.forward(x, out=out, want_routing=False)
+        step(x, out)
     _lib.check(L.gtmoe_read_timing(moe.handle, phase_ms, _lib.N_PHASES, ctypes.byref(calls), ctypes.byref(plaunch)))
     _lib.check(L.gtmoe_set_timing(moe.handle, 0))
     phases = {n: phase_ms[i] / max(calls.value, 1) for i, n in enumerate(_lib.PHASES)}
 
     # end to end through the C ABI with pinned host buffers
     x_host = x.cpu().pin_memory()
-    out_host = torch.empty((T_local, cfg.d), dtype=torch.bfloat16).pin_memory()
+    out_host = torch.empty((T_local, cfg.d), dtype=out.dtype).pin_memory()
     for _ in range(2):
-        moe.forward(x_host, out=out_host, want_routing=False)
+        step(x_host, out_host)
     barrier()
     e2e_steps = max(3, args.steps // 2)
     eevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -302,12 +317,12 @@ def main():
         for i in range(e2e_steps):
             flush_buf.fill_(i)
             eevs[i][0].record(stream)
-            moe.forward(x_host, out=out_host, want_routing=False)
+            step(x_host, out_host)
             eevs[i][1].record(stream)
     else:
         eevs[0][0].record(stream)
         for _ in range(e2e_steps):
-            moe.forward(x_host, out=out_host, want_routing=False)
+            step(x_host, out_host)
         eevs[0][1].record(stream)
     eevs[-1][1].synchronize()
     barrier()
@@ -389,7 +404,9 @@ def main():
         v, n, dt = time_oracle(spec, x_cpu, args.cpu_seconds, threads)
         cpu_baseline = {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
                         "sample": f"{n} seeded tokens of {cfg.name} ({dt:.1f} s), C float64 restatement of "
-                                  f"the reference CPU path; row independence makes a token sample valid"}
+                                  f"the reference CPU path; row independence makes a token sample valid"
+                                  + ("; the MoE forward only (without the block's RMSNorm and residual)"
+                                     if args.op == "block" else "")}
 
     if rank == 0:
         value = T_total / (ms * 1e-3)
@@ -399,9 +416,12 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 activations, N(0,1/fan_in) weights quantised by the reference "
                     "quantiser, Zipf router bias)",
-            "config": workload_config(cfg, world, mode, getattr(moe, "replicas", [])),
+            "config": {**workload_config(cfg, world, mode, getattr(moe, "replicas", [])),
+                       **({"op": "block step: x + Forward(RMSNorm(x)), gtmoe_forward_block"} if args.op == "block"
+                          else {})},
             "e2e": {"value": round(T_total / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(T_local * cfg.d * 2), "d2h_bytes_per_step": int(T_local * cfg.d * 2)},
+                    "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()),
+                    "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size())},
             "roofline": roofline,
             "cpu_baseline": cpu_baseline,
             "phases_ms": {k: round(v, 4) for k, v in phases.items()},

@@ -802,6 +802,16 @@ int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, int precis
     L.width = width;
     GT_CHECK(tc_relayout_layer(h, L, which));
     GT_CUDA(cudaStreamSynchronize(h->stream));
+    // With the record copy built, the snapshot-layout copy is read only by the
+    // SIMT kernels (which such a shape never runs unless the tensor cores are
+    // switched off) and by the backward: drop it, halving the resident
+    // weights; gtmoe_set_training rebuilds it from the records.
+    L.raw_dropped = 0;
+    if (L.tiled.p && !h->no_tc && !h->training) {
+        L.w.release();
+        L.s.release();
+        L.raw_dropped = 1;
+    }
     L.set = 1;
     h->table_dirty = 1;
     return 0;

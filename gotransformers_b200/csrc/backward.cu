@@ -360,6 +360,12 @@ int gtmoe_set_training(gtmoe_t h, int on) {
     if (!h) return fail(GTMOE_EINVAL, "handle is NULL");
     std::lock_guard<std::mutex> lock(h->mu);
     if (on && h->n_ranks > 1) return fail(GTMOE_EINVAL, "training state is kept on one GPU (not expert parallel)");
+    if (on) {
+        // the backward reads the layers in the RowsSnapshot layout
+        GT_CUDA(cudaSetDevice(h->device));
+        for (auto &L : h->layers) GT_CHECK(tc_restore_raw(h, L));
+        GT_CUDA(cudaStreamSynchronize(h->stream));
+    }
     h->training = on ? 1 : 0;
     if (!on) h->tr_valid = 0;
     return 0;

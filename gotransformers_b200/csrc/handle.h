@@ -45,6 +45,10 @@ struct LayerDev {
     DevBuf w, s, b32, b64;
     DevBuf tiled;  // tile-chunk layout of w + s for the tensor-core kernels (tc.cu)
     int has_bias = 0;
+    // w and s (the RowsSnapshot layout, read only by the SIMT kernels and the
+    // backward) are released once `tiled` holds the same bytes, and rebuilt
+    // from it when training is switched on (tc_restore_raw)
+    int raw_dropped = 0;
 };
 
 }  // namespace gtmoe

@@ -708,6 +708,30 @@ __global__ void relayout_kernel(const uint8_t *__restrict__ codes, const float *
     *reinterpret_cast<float4 *>(rec + half_scale_off(hr, code_bytes)) = s;
 }
 
+// The inverse of relayout_kernel: a record back to the row's codes (Int8
+// bias removed) and its four block scales in the RowsSnapshot layout.
+__global__ void unrelayout_kernel(const uint8_t *__restrict__ tiled, int rows, int K, int code_bytes,
+                                  uint8_t *__restrict__ codes, float *__restrict__ scales) {
+    const int KB = K / kBK;
+    const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (item >= (int64_t)rows * KB) return;
+    const int row = (int)(item / KB), kb = (int)(item % KB);
+    const int hr = row % kHalfRows;
+    const uint8_t *rec = tiled + ((int64_t)(row / kHalfRows) * KB + kb) * half_bytes(code_bytes);
+    const int64_t dst_row = (int64_t)row * KB * code_bytes + (int64_t)kb * code_bytes;
+    const uint32_t bias = code_bytes == 64 ? 0x80808080u : 0u;
+    for (int i = 0; i < code_bytes; i += 16) {
+        uint4 c = *reinterpret_cast<const uint4 *>(rec + half_code_off(hr, i));
+        c.x ^= bias;
+        c.y ^= bias;
+        c.z ^= bias;
+        c.w ^= bias;
+        *reinterpret_cast<uint4 *>(codes + dst_row + i) = c;
+    }
+    *reinterpret_cast<float4 *>(scales + (int64_t)row * (K / 16) + kb * 4) =
+        *reinterpret_cast<const float4 *>(rec + half_scale_off(hr, code_bytes));
+}
+
 template <int PREC, bool GATED>
 int launch_one(const CUtensorMap &map, const TcKernelArgs &ka, int sms, cudaStream_t st) {
     const int threads = (!GATED && ka.ret_ranks > 0) ? kMaxThreads : kNumThreads;
@@ -779,6 +803,20 @@ int tc_relayout_layer(gtmoe_handle *h, LayerDev &L, int which) {
     relayout_kernel<<<(unsigned)((items + 255) / 256), 256, 0, h->stream>>>(
         (const uint8_t *)L.w.p, L.s.as<float>(), L.rows, L.width, code_bytes, L.tiled.as<uint8_t>());
     GT_CUDA(cudaGetLastError());
+    return 0;
+}
+
+int tc_restore_raw(gtmoe_handle *h, LayerDev &L) {
+    if (!L.raw_dropped) return 0;
+    const int code_bytes = L.precision == GTMOE_INT8 ? 64 : 32;
+    const int64_t items = (int64_t)L.rows * (L.width / kBK);
+    GT_CHECK(L.w.ensure((size_t)L.rows * (L.width / kBK) * code_bytes));
+    GT_CHECK(L.s.ensure(sizeof(float) * (size_t)L.rows * (L.width / 16)));
+    unrelayout_kernel<<<(unsigned)((items + 255) / 256), 256, 0, h->stream>>>(
+        L.tiled.as<uint8_t>(), L.rows, L.width, code_bytes, L.w.as<uint8_t>(), L.s.as<float>());
+    GT_CUDA(cudaGetLastError());
+    L.raw_dropped = 0;
+    h->table_dirty = 1;
     return 0;
 }
 

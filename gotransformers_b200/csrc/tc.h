@@ -41,6 +41,9 @@ bool tc_supported(const gtmoe_handle *h, int64_t T);
 // Builds L.tiled (the chunk layout the tensor-core kernels stream) when the
 // handle's shapes and precision use the tensor-core path; no-op otherwise.
 int tc_relayout_layer(gtmoe_handle *h, LayerDev &L, int which);
+// The RowsSnapshot arrays (L.w, L.s) rebuilt from L.tiled, after the layer
+// dropped them (an exact inverse of the set-time permutation).
+int tc_restore_raw(gtmoe_handle *h, LayerDev &L);
 int tc_tile_rows(TcWeights &w);  // m-tile height of the current shape
 int tc_prepare(gtmoe_handle *h, TcWeights &w);
 int launch_grouped_tc(gtmoe_handle *h, TcWeights &w, const TcArgs &a, cudaStream_t st);

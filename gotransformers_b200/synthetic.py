@@ -67,6 +67,7 @@ def bf16_round(a: np.ndarray) -> np.ndarray:
 STREAM_X = 1
 STREAM_ROUTER = 2
 STREAM_ROUTER_BIAS_LOGITS = 3
+STREAM_NORM = 4  # the block's RMSNorm weights
 
 
 def expert_stream(index: int, which: int) -> int:
