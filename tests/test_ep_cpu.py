@@ -138,3 +138,29 @@ def test_expert_parallel_plan_matches_single_process(tmp_path, replicas):
     ref = O.moe_forward(spec, x)["out"]
     got = np.concatenate([np.load(tmp_path / f"out{r}.npy") for r in range(2)])
     assert np.array_equal(got, ref)
+
+
+def test_replica_choice_evens_out_the_expected_rows():
+    """synthetic.choose_replicas (the benchmark's hot-expert list): under c5's
+    Zipf(1.0) router at 8 ranks the most loaded rank's expected rows drop from
+    about 1.5x the mean to within a few percent of it, with at most 16
+    replicas, and the choice is deterministic."""
+    import numpy as np
+
+    from gotransformers_b200 import synthetic
+
+    cfg = synthetic.CONFIGS["c5"]
+    rate = synthetic.expected_rates(cfg)
+    assert abs(rate.sum() - cfg.k) < 1e-9
+
+    def worst(rep, G):
+        el, tl = cfg.n_routed // G, cfg.T // G
+        rows = [cfg.n_shared * tl + cfg.T * rate[[e for e in range(q * el, (q + 1) * el) if e not in rep]].sum()
+                + tl * rate[sorted(rep)].sum() for q in range(G)]
+        return max(rows) / (cfg.T * (cfg.n_shared + cfg.k) / G)
+
+    rep = synthetic.choose_replicas(cfg, 8)
+    assert rep == synthetic.choose_replicas(cfg, 8) and len(rep) <= 16 and rep == sorted(set(rep))
+    assert worst([], 8) > 1.4
+    assert worst(rep, 8) < 1.05
+    assert synthetic.choose_replicas(cfg, 1) == []
