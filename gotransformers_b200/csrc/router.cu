@@ -100,35 +100,42 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void *__restri
 constexpr int kRouterSmallT = 256;
 constexpr int kRouterSmallWarps = 8;
 
+// The warp stages 512-input chunks of the token row and the expert's weight
+// row in shared memory with coalesced loads (element j at j + j/16, so that
+// lane l reading block l's 16 values hits 32 different banks); lane l then
+// forms block l's sum, and the warp adds the chunk's 32 block sums in order.
+constexpr int kSmallChunk = 512;
+constexpr int kSmallPitch = kSmallChunk + kSmallChunk / kRouterK;  // 544
+
 template <int XDT>
 __global__ void __launch_bounds__(kRouterSmallWarps * 32)
     router_logits_small_kernel(const void *__restrict__ x, const float *__restrict__ w, int64_t T, int E, int d,
                                double *__restrict__ logits) {
-    extern __shared__ float blk[];  // [warp][d/16 rounded up] block sums
+    __shared__ float xs[kRouterSmallWarps][kSmallPitch];
+    __shared__ float ws[kRouterSmallWarps][kSmallPitch];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = (d + kRouterK - 1) / kRouterK;
     const int e = blockIdx.x * kRouterSmallWarps + warp;
     const int64_t t = blockIdx.y;
     if (e >= E) return;
-    float *mine = blk + warp * nb;
     const float *we = w + (int64_t)e * d;
-    for (int b = lane; b < nb; b += 32) {
-        float p = 0.f;
-#pragma unroll
-        for (int c = 0; c < kRouterK; c++) {
-            const int kk = b * kRouterK + c;
-            const float xv = kk < d ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
-            const float wv = kk < d ? __ldg(we + kk) : 0.f;
-            p = fmaf(xv, wv, p);
+    float *xw = xs[warp], *ww = ws[warp];
+    double acc = 0.0;
+    for (int c0 = 0; c0 < d; c0 += kSmallChunk) {
+#pragma unroll 4
+        for (int i = 0; i < kSmallChunk / 32; i++) {
+            const int j = 32 * i + lane, kk = c0 + j;
+            xw[j + j / kRouterK] = kk < d ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
+            ww[j + j / kRouterK] = kk < d ? __ldg(we + kk) : 0.f;
         }
-        mine[b] = p;
+        __syncwarp();
+        float p = 0.f;  // block (c0 / 16 + lane): inputs past d are zero products
+#pragma unroll
+        for (int c = 0; c < kRouterK; c++) p = fmaf(xw[lane * (kRouterK + 1) + c], ww[lane * (kRouterK + 1) + c], p);
+        const int nblk = min(32, (d - c0 + kRouterK - 1) / kRouterK);  // blocks of this chunk inside d
+        for (int b = 0; b < nblk; b++) acc += (double)__shfl_sync(0xffffffffu, p, b);
+        __syncwarp();
     }
-    __syncwarp();
-    if (lane == 0) {
-        double acc = 0.0;
-        for (int b = 0; b < nb; b++) acc += (double)mine[b];
-        logits[t * E + e] = acc;
-    }
+    if (lane == 0) logits[t * E + e] = acc;
 }
 
 // Many tokens and at most 64 experts: one warp per token, one lane per expert
@@ -153,20 +160,38 @@ __global__ void __launch_bounds__(256) router_logits_lanes_kernel(const void *__
     const bool has0 = e0 < E, has1 = e1 < E;
     double acc0 = 0.0, acc1 = 0.0;
     const int nb = (d + kRouterK - 1) / kRouterK;
-    for (int b = 0; b < nb; b++) {
-        float p0 = 0.f, p1 = 0.f;
+    // block b's operands, the next block's loaded while this one is summed
+    float xv[kRouterK], w0[kRouterK], w1[kRouterK];
+    auto fetch = [&](int b, float (&xr)[kRouterK], float (&r0)[kRouterK], float (&r1)[kRouterK]) {
 #pragma unroll
         for (int c = 0; c < kRouterK; c++) {
             const int kk = b * kRouterK + c;
             const bool in = kk < d;
-            const float xv = in ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
-            const float w0 = in && has0 ? __ldg(w32t + (int64_t)kk * E + e0) : 0.f;
-            const float w1 = in && has1 ? __ldg(w32t + (int64_t)kk * E + e1) : 0.f;
-            p0 = fmaf(xv, w0, p0);
-            p1 = fmaf(xv, w1, p1);
+            xr[c] = in ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
+            r0[c] = in && has0 ? __ldg(w32t + (int64_t)kk * E + e0) : 0.f;
+            r1[c] = in && has1 ? __ldg(w32t + (int64_t)kk * E + e1) : 0.f;
+        }
+    };
+    fetch(0, xv, w0, w1);
+    for (int b = 0; b < nb; b++) {
+        float xn[kRouterK], n0[kRouterK], n1[kRouterK];
+        if (b + 1 < nb) fetch(b + 1, xn, n0, n1);
+        float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < kRouterK; c++) {
+            p0 = fmaf(xv[c], w0[c], p0);
+            p1 = fmaf(xv[c], w1[c], p1);
         }
         acc0 += (double)p0;
         acc1 += (double)p1;
+        if (b + 1 < nb) {
+#pragma unroll
+            for (int c = 0; c < kRouterK; c++) {
+                xv[c] = xn[c];
+                w0[c] = n0[c];
+                w1[c] = n1[c];
+            }
+        }
     }
     if (has0) logits[t * E + e0] = acc0;
     if (has1) logits[t * E + e1] = acc1;
@@ -555,16 +580,14 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
         GT_CHECK(launch_router_logits_tc(a.x, a.T, a.d, a.E, a.e_pad, a.w3, a.logits, a.err, a.sms, st));
     } else if (a.T <= kRouterSmallT) {
         dim3 grid((unsigned)((a.E + kRouterSmallWarps - 1) / kRouterSmallWarps), (unsigned)a.T);
-        const size_t smem = sizeof(float) * kRouterSmallWarps * ((a.d + kRouterK - 1) / kRouterK);
-        if (smem > 48 * 1024) return fail(GTMOE_EINVAL, "router: d_model %d too large", a.d);
         if (a.x_dtype == GTMOE_DTYPE_F64)
-            router_logits_small_kernel<GTMOE_DTYPE_F64><<<grid, kRouterSmallWarps * 32, smem, st>>>(a.x, a.w32, a.T,
-                                                                                                     a.E, a.d, a.logits);
+            router_logits_small_kernel<GTMOE_DTYPE_F64><<<grid, kRouterSmallWarps * 32, 0, st>>>(a.x, a.w32, a.T,
+                                                                                                  a.E, a.d, a.logits);
         else if (a.x_dtype == GTMOE_DTYPE_F32)
-            router_logits_small_kernel<GTMOE_DTYPE_F32><<<grid, kRouterSmallWarps * 32, smem, st>>>(a.x, a.w32, a.T,
-                                                                                                     a.E, a.d, a.logits);
+            router_logits_small_kernel<GTMOE_DTYPE_F32><<<grid, kRouterSmallWarps * 32, 0, st>>>(a.x, a.w32, a.T,
+                                                                                                  a.E, a.d, a.logits);
         else
-            router_logits_small_kernel<GTMOE_DTYPE_BF16><<<grid, kRouterSmallWarps * 32, smem, st>>>(
+            router_logits_small_kernel<GTMOE_DTYPE_BF16><<<grid, kRouterSmallWarps * 32, 0, st>>>(
                 a.x, a.w32, a.T, a.E, a.d, a.logits);
         GT_CUDA(cudaGetLastError());
         note_launches(1);
