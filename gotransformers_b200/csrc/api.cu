@@ -394,7 +394,7 @@ static std::vector<uint64_t> graph_key(gtmoe_handle *h, const void *x, int x_dty
                                (uint64_t)(uintptr_t)out, (uint64_t)out_dtype, (uint64_t)(uintptr_t)h->stream, wbits,
                                (uint64_t)h->e_pad, (uint64_t)use_tc, (uint64_t)use_decode,
                                (uint64_t)(uintptr_t)h->tc.err};
-    const gtmoe::DevBuf *bufs[] = {&h->wr64,   &h->wr32,   &h->wr32t,  &h->br,     &h->bal,    &h->wr3,   &h->table,
+    const gtmoe::DevBuf *bufs[] = {&h->wr64,   &h->wr32,   &h->br,     &h->bal,    &h->wr3,   &h->table,
                                    &h->logits, &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load,
                                    &h->offsets, &h->perm,  &h->slot_row, &h->groups, &h->tile_prefix, &h->xp,
                                    &h->hp,     &h->yp,     &h->fixups, &h->flagged};
@@ -479,7 +479,6 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     ra.d = d;
     ra.token_ids = ids_dev;
     ra.w32 = h->wr32.as<float>();
-    ra.w32t = h->wr32t.as<float>();
     ra.w64 = h->wr64.as<double>();
     ra.bias = h->br.as<double>();
     ra.balance = h->bal.as<double>();
@@ -630,7 +629,7 @@ void gtmoe_destroy(gtmoe_t h) {
             L.b32.release();
             L.b64.release();
         }
-        DevBuf *bufs[] = {&h->wr64, &h->wr32, &h->wr32t, &h->wr3, &h->br, &h->bal, &h->table, &h->x_in, &h->ids, &h->logits,
+        DevBuf *bufs[] = {&h->wr64, &h->wr32, &h->wr3, &h->br, &h->bal, &h->table, &h->x_in, &h->ids, &h->logits,
                           &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load, &h->offsets, &h->perm,
                           &h->slot_row, &h->groups, &h->tile_prefix, &h->xp, &h->hp, &h->yp, &h->out_dev,
                           &h->res_dev, &h->fixups, &h->flagged, &h->x_pipe[0], &h->x_pipe[1], &h->out_pipe[0],
@@ -714,10 +713,6 @@ int gtmoe_set_router(gtmoe_t h, int precision, const void *values, const float *
     h->e_pad = e_pad;
     GT_CHECK(upload(h->wr64, w64.data(), sizeof(double) * w64.size(), h->stream));
     GT_CHECK(upload(h->wr32, w32.data(), sizeof(float) * w32.size(), h->stream));
-    std::vector<float> w32t(w32.size());  // input-major copy for the per-lane logits kernel
-    for (int e = 0; e < E; e++)
-        for (int i = 0; i < d; i++) w32t[(size_t)i * E + e] = w32[(size_t)e * d + i];
-    GT_CHECK(upload(h->wr32t, w32t.data(), sizeof(float) * w32t.size(), h->stream));
     GT_CHECK(upload(h->br, b.data(), sizeof(double) * E, h->stream));
     GT_CUDA(cudaStreamSynchronize(h->stream));
     h->wmax = wmax * (1 + 1e-6);

@@ -506,7 +506,6 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     ra.d = d;
     ra.token_ids = ids_dev;
     ra.w32 = h->wr32.as<float>();
-    ra.w32t = h->wr32t.as<float>();
     ra.w64 = h->wr64.as<double>();
     ra.bias = h->br.as<double>();
     ra.balance = h->bal.as<double>();

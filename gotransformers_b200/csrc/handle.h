@@ -79,7 +79,7 @@ struct gtmoe_handle {
 
     // router
     int router_set = 0;
-    DevBuf wr64, wr32, wr32t, br, bal, wr3;  // wr32t: d x E; wr3: bf16 hi/mid/lo split, 3 x e_pad x d
+    DevBuf wr64, wr32, br, bal, wr3;  // wr3: bf16 hi/mid/lo split, 3 x e_pad x d
     int e_pad = 0;
     std::vector<double> h_bal;
     double wmax = 0;

@@ -25,7 +25,6 @@ struct RouterArgs {
     int E, k, d;
     const int64_t *token_ids;   // hash routing (device)
     const float *w32;           // E x d
-    const float *w32t;          // d x E (the same values input-major), or NULL
     const double *w64;          // E x d
     const double *bias;         // E
     const double *balance;      // E

@@ -131,7 +131,6 @@ extern "C" GTMOE_API int gtmoe_route_noalloc(gtmoe_t h, const void *x, int x_dty
     ra.d = d;
     ra.token_ids = token_ids;
     ra.w32 = h->wr32.as<float>();
-    ra.w32t = h->wr32t.as<float>();
     ra.w64 = h->wr64.as<double>();
     ra.bias = h->br.as<double>();
     ra.balance = h->bal.as<double>();

@@ -138,65 +138,6 @@ __global__ void __launch_bounds__(kRouterSmallWarps * 32)
     if (lane == 0) logits[t * E + e] = acc;
 }
 
-// Many tokens and at most 64 experts: one warp per token, one lane per expert
-// (two for 33-64 experts), the router weights input-major (w32t[i * E + e]) so
-// that each load of a lane's weight coalesces across the warp, and every lane
-// reads the same x value.  Per expert the arithmetic is router_logits_kernel's
-// operation for operation -- float32 sums of each 16-input block by sequential
-// fmaf from zero (inputs past d as zero products), the blocks added in float64
-// in input order -- so all three logits kernels give the same bits.  (The
-// 64 x 64 tile kernel would launch only T/64 CTAs here and leave most of each
-// tile's expert columns empty.)
-constexpr int kRouterLanesMaxE = 64;
-
-template <int XDT>
-__global__ void __launch_bounds__(256) router_logits_lanes_kernel(const void *__restrict__ x,
-                                                                  const float *__restrict__ w32t, int64_t T, int E,
-                                                                  int d, double *__restrict__ logits) {
-    const int lane = threadIdx.x & 31;
-    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (t >= T) return;
-    const int e0 = lane, e1 = lane + 32;
-    const bool has0 = e0 < E, has1 = e1 < E;
-    double acc0 = 0.0, acc1 = 0.0;
-    const int nb = (d + kRouterK - 1) / kRouterK;
-    // block b's operands, the next block's loaded while this one is summed
-    float xv[kRouterK], w0[kRouterK], w1[kRouterK];
-    auto fetch = [&](int b, float (&xr)[kRouterK], float (&r0)[kRouterK], float (&r1)[kRouterK]) {
-#pragma unroll
-        for (int c = 0; c < kRouterK; c++) {
-            const int kk = b * kRouterK + c;
-            const bool in = kk < d;
-            xr[c] = in ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
-            r0[c] = in && has0 ? __ldg(w32t + (int64_t)kk * E + e0) : 0.f;
-            r1[c] = in && has1 ? __ldg(w32t + (int64_t)kk * E + e1) : 0.f;
-        }
-    };
-    fetch(0, xv, w0, w1);
-    for (int b = 0; b < nb; b++) {
-        float xn[kRouterK], n0[kRouterK], n1[kRouterK];
-        if (b + 1 < nb) fetch(b + 1, xn, n0, n1);
-        float p0 = 0.f, p1 = 0.f;
-#pragma unroll
-        for (int c = 0; c < kRouterK; c++) {
-            p0 = fmaf(xv[c], w0[c], p0);
-            p1 = fmaf(xv[c], w1[c], p1);
-        }
-        acc0 += (double)p0;
-        acc1 += (double)p1;
-        if (b + 1 < nb) {
-#pragma unroll
-            for (int c = 0; c < kRouterK; c++) {
-                xv[c] = xn[c];
-                w0[c] = n0[c];
-                w1[c] = n1[c];
-            }
-        }
-    }
-    if (has0) logits[t * E + e0] = acc0;
-    if (has1) logits[t * E + e1] = acc1;
-}
-
 // activationfunction/moreactivationfunctions.go:8-16, mixtureofexperts.go:80-82
 __device__ __forceinline__ double affinity_d(double logit) {
     double sp;
@@ -589,16 +530,6 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
         else
             router_logits_small_kernel<GTMOE_DTYPE_BF16><<<grid, kRouterSmallWarps * 32, 0, st>>>(
                 a.x, a.w32, a.T, a.E, a.d, a.logits);
-        GT_CUDA(cudaGetLastError());
-        note_launches(1);
-    } else if (a.E <= kRouterLanesMaxE && a.w32t) {
-        const unsigned blocks = (unsigned)((a.T * 32 + 255) / 256);
-        if (a.x_dtype == GTMOE_DTYPE_F64)
-            router_logits_lanes_kernel<GTMOE_DTYPE_F64><<<blocks, 256, 0, st>>>(a.x, a.w32t, a.T, a.E, a.d, a.logits);
-        else if (a.x_dtype == GTMOE_DTYPE_F32)
-            router_logits_lanes_kernel<GTMOE_DTYPE_F32><<<blocks, 256, 0, st>>>(a.x, a.w32t, a.T, a.E, a.d, a.logits);
-        else
-            router_logits_lanes_kernel<GTMOE_DTYPE_BF16><<<blocks, 256, 0, st>>>(a.x, a.w32t, a.T, a.E, a.d, a.logits);
         GT_CUDA(cudaGetLastError());
         note_launches(1);
     } else {
