@@ -47,16 +47,33 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void *__restri
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
 
+    // each thread's share of a 16-input chunk, the next chunk's loaded into
+    // registers while this one is multiplied (the loop is otherwise bound by
+    // one global-load latency per chunk)
+    constexpr int kPer = kRouterTile * kRouterK / 256;
+    float rx[kPer], rw[kPer];
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int j = 0; j < kPer; j++) {
+            const int i = threadIdx.x + 256 * j;
+            const int r = i / kRouterK, c = i % kRouterK;
+            const int64_t t = t0 + r;
+            const int kk = k0 + c;
+            rx[j] = (t < T && kk < d) ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
+            const int e = e0 + r;
+            rw[j] = (e < E && kk < d) ? w[(int64_t)e * d + kk] : 0.f;
+        }
+    };
+    fetch(0);
     for (int k0 = 0; k0 < d; k0 += kRouterK) {
-        for (int i = threadIdx.x; i < kRouterTile * kRouterK; i += blockDim.x) {
-            int r = i / kRouterK, c = i % kRouterK;
-            int64_t t = t0 + r;
-            int kk = k0 + c;
-            xs[c][r] = (t < T && kk < d) ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
-            int e = e0 + r;
-            ws[c][r] = (e < E && kk < d) ? w[(int64_t)e * d + kk] : 0.f;
+#pragma unroll
+        for (int j = 0; j < kPer; j++) {
+            const int i = threadIdx.x + 256 * j;
+            xs[i % kRouterK][i / kRouterK] = rx[j];
+            ws[i % kRouterK][i / kRouterK] = rw[j];
         }
         __syncthreads();
+        if (k0 + kRouterK < d) fetch(k0 + kRouterK);
         float part[4][4];
 #pragma unroll
         for (int i = 0; i < 4; i++)
