@@ -54,6 +54,7 @@ EXPORTS = [
     "gtmoe_quantize_rows",
     "gtmoe_fill_normal",
     "gtmoe_route_noalloc",
+    "gtmoe_bounded_wait_selftest",
     "gtmoe_set_norm",
     "gtmoe_forward_block",
     "gtmoe_set_training",
@@ -128,6 +129,7 @@ def lib():
             L.gtmoe_read_timing.argtypes = [vp, vp, i32, vp, vp]
             L.gtmoe_quantize_rows.argtypes = [i32, vp, i64, i32, vp, vp]
             L.gtmoe_route_noalloc.argtypes = [vp, vp, i32, i64, vp, vp, vp]
+            L.gtmoe_bounded_wait_selftest.argtypes = [i32]
             L.gtmoe_fill_normal.argtypes = [vp, i32, i64, ctypes.c_uint64, ctypes.c_uint64, i64, d]
             L.gtmoe_set_norm.argtypes = [vp, vp, d]
             L.gtmoe_forward_block.argtypes = [vp, vp, i32, i64, vp, vp, i32, vp, vp, vp, vp]

@@ -292,6 +292,16 @@ GTMOE_API int gtmoe_read_timing(gtmoe_t h, double *ms, int n_phases, int64_t *ca
 GTMOE_API int gtmoe_route_noalloc(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids,
                                   int32_t *chosen, double *gates);
 
+/* The library's failure path on a device, without a fault; no counterpart in
+ * the reference.  Every device-side wait of this library is bounded (2 s of
+ * %globaltimer): on expiry the kernel records an error code, stops and
+ * returns, the call reports GTMOE_ETIMEOUT and the CUDA context stays
+ * usable.  This runs that bounded wait on an mbarrier nothing completes and
+ * returns GTMOE_ETIMEOUT once the wait has given up and been reported -- the
+ * expected result; any other code means the failure path does not work on
+ * this device.  Takes about two seconds; allocates 4 bytes. */
+GTMOE_API int gtmoe_bounded_wait_selftest(int device);
+
 /* lowprecision.RowsFromMatrix (lowprecision/rows.go:276-283, Rows.Append
  * rows.go:38-79) on the GPU: quantises rows x width float64 values into the
  * RowsSnapshot arrays described above.  Bit-identical to the reference

@@ -43,6 +43,7 @@ def test_no_cpu_fallback_without_gpu():
     with pytest.raises(_lib.GtmoeError) as e:
         G.MixtureOfExperts(8, 8, 0, 2, 1)
     assert e.value.code == -2  # GTMOE_ENODEVICE
+    assert _lib.lib().gtmoe_bounded_wait_selftest(0) == -2
 
 
 def test_invalid_config_is_rejected_before_touching_a_device():
