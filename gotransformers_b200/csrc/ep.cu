@@ -7,9 +7,13 @@
 //   1. route this rank's tokens (router.cu) and dispatch them over all E
 //      experts (dispatch.cu): the stable permutation orders (token, slot)
 //      rows by global expert, i.e. by destination rank, token-ascending;
-//   2. all-gather every rank's per-expert counts and token count (NCCL, one
-//      G x (E+1) int64 exchange and one host synchronisation: the host needs
-//      the sizes for the group table and the buffers);
+//   2. exchange every rank's per-expert counts and token count (each rank
+//      stores its E+1 int64 into every rank's mailbox over the IPC mappings
+//      and signals; a bounded wait for all G arrivals; one host
+//      synchronisation: the host needs the sizes for the group table and the
+//      buffers).  A rank that stops calling Forward makes the others' wait run
+//      out (GTMOE_ETIMEOUT) instead of hanging them; NCCL is used only at set
+//      up and when the peer buffers grow;
 //   3. the push kernel copies each (token, slot) row straight into the owning
 //      GPU's GEMM input over NVLink (CUDA IPC mappings of every rank's
 //      buffers): expert-major, source-ascending inside an expert, so an
@@ -91,7 +95,10 @@ constexpr int kMaxEpRanks = 16;
 // arrivals a step brings (G sources x this many CTAs).
 constexpr int kPushCtas = 1184;
 constexpr int kPushThreads = 256;
-constexpr int kSigForward = 0, kSigReturn = 1;
+constexpr int kSigForward = 0, kSigReturn = 1, kSigCounts = 2;
+// Each rank's IPC-shared signal block: 32 arrival counters, then the count
+// mailboxes [2 step parities][G ranks][E + 1] int64.
+constexpr size_t kSigCounterBytes = 256;
 
 struct PeerRows {
     unsigned char *p[kMaxEpRanks];
@@ -213,6 +220,37 @@ __global__ void ep_route_kernel(const RetSeg *__restrict__ segs, int n_segs, int
     }
 }
 
+// The step's count exchange: this rank's E + 1 values (per-expert rows, then
+// its token count) into mailbox row `rank` of parity `slot` on every rank,
+// one arrival on every rank's count counter, then a bounded wait until all G
+// ranks' arrivals of this exchange are in.  The mailboxes alternate between
+// two parities: a rank writes exchange n + 2 only after exchange n + 1, which
+// no rank joins before it has read exchange n.
+__global__ void ep_counts_kernel(const int64_t *__restrict__ mine, int n, int rank, int G, int slot,
+                                 const __grid_constant__ PeerSigs sig, unsigned long long target, int *err) {
+    for (int q = 0; q < G; q++) {
+        int64_t *box = reinterpret_cast<int64_t *>(reinterpret_cast<unsigned char *>(sig.p[q]) + kSigCounterBytes) +
+                       ((int64_t)slot * G + rank) * n;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) box[i] = mine[i];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    for (int q = 0; q < G; q++) atomicAdd_system(sig.p[q] + kSigCounts, 1ull);
+    const unsigned long long *counter = sig.p[rank] + kSigCounts;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counter) : "memory");
+        if (v >= target) break;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicCAS(err, 0, 3);
+            return;
+        }
+        __nanosleep(256);
+    }
+}
+
 // Bounded wait until this rank's arrival counter reaches `target`.
 __global__ void ep_wait_kernel(const unsigned long long *counter, unsigned long long target, int *err, int code) {
     if (threadIdx.x != 0) return;
@@ -236,10 +274,10 @@ __global__ void ep_wait_kernel(const unsigned long long *counter, unsigned long 
 struct EpState {
     ncclComm_t comm = nullptr;
     int G = 1, r = 0;
-    DevBuf gathered;  // G x (E + 1) int64: per-expert counts, then the token count (device)
-    std::vector<int64_t> h_gathered;
+    std::vector<int64_t> h_gathered;  // G x (E + 1): per-expert counts, then the token count
     int have_gathered = 0;
-    unsigned long long epoch = 0;  // completed exchanges (same on every rank)
+    unsigned long long epoch = 0;         // completed row exchanges (same on every rank)
+    unsigned long long count_epoch = 0;   // completed count exchanges (same on every rank)
     // IPC-shared buffers: the GEMM input (received rows, then own token rows)
     // and the returned expert outputs ((token, slot) order); capacities in
     // bytes, tracked identically on every rank
@@ -283,18 +321,21 @@ void ep_destroy(gtmoe_handle *h) {
     if (ep->comm && g_nccl.loaded) g_nccl.CommDestroy(ep->comm);
     for (void *p : {ep->x_local, ep->y_local, ep->sig_local, (void *)ep->err, (void *)ep->done})
         if (p) cudaFree(p);
-    DevBuf *bufs[] = {&ep->gathered, &ep->staging, &ep->xconv, &ep->dst_base, &ep->ret_segs, &ep->route,
-                      &ep->peer_tab};
+    DevBuf *bufs[] = {&ep->staging, &ep->xconv, &ep->dst_base, &ep->ret_segs, &ep->route, &ep->peer_tab};
     for (DevBuf *b : bufs) b->release();
     delete ep;
     h->ep = nullptr;
 }
 
-// Maps every rank's signal counters (once, at creation).
+static size_t sig_bytes(int G, int E) { return kSigCounterBytes + 2 * (size_t)G * (E + 1) * sizeof(int64_t); }
+
+// Maps every rank's signal block -- arrival counters and count mailboxes --
+// (once, at creation).
 static int ep_map_signals(gtmoe_handle *h, EpState *ep) {
     const int G = ep->G;
-    GT_CUDA(cudaMalloc(&ep->sig_local, 256));
-    GT_CUDA(cudaMemset(ep->sig_local, 0, 256));
+    const size_t sb = sig_bytes(G, h->cfg.n_routed);
+    GT_CUDA(cudaMalloc(&ep->sig_local, sb));
+    GT_CUDA(cudaMemset(ep->sig_local, 0, sb));
     GT_CUDA(cudaMalloc(&ep->err, sizeof(int)));
     GT_CUDA(cudaMemset(ep->err, 0, sizeof(int)));
     GT_CUDA(cudaMalloc(&ep->done, 4 * sizeof(unsigned int)));
@@ -398,19 +439,43 @@ int ep_global_load(gtmoe_handle *h, int64_t *load) {
     return 0;
 }
 
+// The step's count exchange: h->load holds this rank's per-expert rows and,
+// at [E], its token count; afterwards ep->h_gathered holds every rank's.
+static int ep_exchange_counts(gtmoe_handle *h, EpState *ep, cudaStream_t st) {
+    const int E = h->cfg.n_routed, G = ep->G, n = E + 1;
+    const int slot = (int)(ep->count_epoch & 1);
+    ep->count_epoch++;
+    PeerSigs sg;
+    for (int q = 0; q < kMaxEpRanks; q++) sg.p[q] = q < G ? (unsigned long long *)ep->peer_sig[q] : nullptr;
+    ep_counts_kernel<<<1, 256, 0, st>>>(h->load.as<int64_t>(), n, ep->r, G, slot, sg,
+                                        ep->count_epoch * (unsigned long long)G, ep->err);
+    GT_CUDA(cudaGetLastError());
+    note_launches(1);
+    ep->h_gathered.resize((size_t)G * n);
+    const int64_t *box = reinterpret_cast<const int64_t *>((const unsigned char *)ep->sig_local + kSigCounterBytes) +
+                         (size_t)slot * G * n;
+    GT_CUDA(cudaMemcpyAsync(ep->h_gathered.data(), box, sizeof(int64_t) * G * n, cudaMemcpyDeviceToHost, st));
+    GT_CUDA(cudaStreamSynchronize(st));
+    int werr = 0;
+    GT_CUDA(cudaMemcpy(&werr, ep->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (werr)
+        return fail(GTMOE_ETIMEOUT,
+                    "expert-parallel count exchange gave up waiting for the other ranks (a rank did not call "
+                    "Forward for this step); the handle is unusable");
+    return 0;
+}
+
 // The step's count exchange with this rank's counts replaced by a refusal
 // marker (token count -1): every rank then fails the step together.
 static int ep_refuse_step(gtmoe_handle *h, EpState *ep, int rc) {
     const std::string msg = gtmoe_last_error();
-    const int E = h->cfg.n_routed, G = ep->G;
+    const int E = h->cfg.n_routed;
     cudaStream_t st = h->stream;
     GT_CHECK(h->load.ensure(sizeof(int64_t) * (E + 1)));
-    GT_CHECK(ep->gathered.ensure(sizeof(int64_t) * (size_t)G * (E + 1)));
     std::vector<int64_t> mine(E + 1, 0);
     mine[E] = -1;
     GT_CUDA(cudaMemcpyAsync(h->load.p, mine.data(), sizeof(int64_t) * (E + 1), cudaMemcpyHostToDevice, st));
-    GT_NCCL(g_nccl.AllGather(h->load.p, ep->gathered.p, (size_t)(E + 1), ncclInt64, ep->comm, st));
-    GT_CUDA(cudaStreamSynchronize(st));
+    GT_CHECK(ep_exchange_counts(h, ep, st));
     return fail(rc, "%s", msg.c_str());
 }
 
@@ -492,7 +557,6 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     GT_CHECK(h->tile_prefix.ensure(sizeof(int64_t) * (S + E + 1)));
     GT_CHECK(h->fixups.ensure(sizeof(int)));
     GT_CHECK(h->flagged.ensure(sizeof(int) * (size_t)(T > 0 ? T : 1)));
-    GT_CHECK(ep->gathered.ensure(sizeof(int64_t) * (size_t)G * (E + 1)));
     GT_CHECK(ep->dst_base.ensure(sizeof(int64_t) * E));
     GT_CHECK(refresh_table(h));
 
@@ -547,11 +611,7 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     GT_CHECK(h->phase_begin(6));
     const int64_t T_mine = T;
     GT_CUDA(cudaMemcpyAsync(h->load.as<int64_t>() + E, &T_mine, sizeof(int64_t), cudaMemcpyHostToDevice, st));
-    GT_NCCL(g_nccl.AllGather(h->load.p, ep->gathered.p, (size_t)(E + 1), ncclInt64, ep->comm, st));
-    ep->h_gathered.resize((size_t)G * (E + 1));
-    GT_CUDA(cudaMemcpyAsync(ep->h_gathered.data(), ep->gathered.p, sizeof(int64_t) * G * (E + 1),
-                            cudaMemcpyDeviceToHost, st));
-    GT_CUDA(cudaStreamSynchronize(st));
+    GT_CHECK(ep_exchange_counts(h, ep, st));
     ep->have_gathered = 1;
     const int64_t *hg = ep->h_gathered.data();
     auto L = [&](int s, int e) { return hg[(size_t)s * (E + 1) + e]; };  // rows of rank s for expert e

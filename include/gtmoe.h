@@ -240,8 +240,9 @@ GTMOE_API int gtmoe_set_expert_layer(gtmoe_t h, int kind, int index, int which, 
  * every rank calls it once per step, in the same order.  A rank that cannot
  * run a step calls it with T = -1 (any argument error does the same): the
  * step then fails on every rank with GTMOE_EINVAL and the handles stay
- * usable.  A device wait for the other ranks' rows that runs out (about 2 s)
- * fails the step with GTMOE_ETIMEOUT and leaves the handle unusable.
+ * usable.  A device wait for the other ranks' counts or rows that runs out
+ * (about 2 s; e.g. a rank that does not call Forward for the step) fails the
+ * step with GTMOE_ETIMEOUT and leaves the handle unusable.
  * With host output pointers the call returns after the results are there;
  * with device pointers it is asynchronous on the handle's stream. */
 GTMOE_API int gtmoe_forward(gtmoe_t h, const void *x, int x_dtype, int64_t T, const int64_t *token_ids, const void *residual,

@@ -10,6 +10,7 @@ so the peer buffers grow once and are then reused.  One case holds hot-expert
 replicas (gtmoe_ep_set_replicas) on every rank."""
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -179,3 +180,72 @@ def test_expert_parallel_matches_single_gpu(name, tmp_path):
         for r in range(world - 1):
             assert f"rank {world - 1} refused" in msgs[r], msgs
     assert load.sum() == x.shape[0] * spec.k
+
+
+def _rank_missing(rank, world, port, outdir):
+    """Both ranks run one step; then rank 0 runs another step alone while
+    rank 1 waits on the host (between steps: none of its kernels in flight)."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from gotransformers_b200 import _lib
+    from gotransformers_b200 import moe as G
+    from gpu_helpers import to_rows
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.cuda.set_device(rank)
+    spec, x, ids = make_case(T=256, d=256, h=128, n_shared=1, n_routed=8, k=2, precision=O.INT8, seed=36)
+    idbuf = bytearray(128)
+    if rank == 0:
+        _lib.check(_lib.lib().gtmoe_ep_unique_id((ctypes.c_char * 128).from_buffer(idbuf)))
+    obj = [bytes(idbuf)]
+    dist.broadcast_object_list(obj, src=0)
+    m = G.MixtureOfExperts(spec.d, spec.h, spec.n_shared, spec.n_routed, spec.k, weight_precision=O.INT8,
+                           device=rank, ep_ranks=world, ep_rank=rank, nccl_id=obj[0])
+    m.set_router(to_rows(spec.router), spec.router.bias)
+    for e, layers in enumerate(spec.experts):
+        kind, idx = (G.SHARED, e) if e < spec.n_shared else (G.ROUTED, e - spec.n_shared)
+        if kind == G.ROUTED and not m.holds(idx):
+            continue
+        for which, L in enumerate(layers):
+            m.set_expert_layer(kind, idx, which, to_rows(L), L.bias)
+    xs = torch.from_numpy(np.ascontiguousarray(x[rank * 128:(rank + 1) * 128])).to(torch.float32).cuda()
+    m.forward(xs, out_dtype=_lib.DTYPE_F32)  # a step both ranks run
+    torch.cuda.synchronize()
+    result = "not run"
+    if rank == 0:
+        t0 = time.perf_counter()
+        try:
+            m.forward(xs, out_dtype=_lib.DTYPE_F32)
+            result = "ran"
+        except _lib.GtmoeError as e:
+            result = f"{e.code} {time.perf_counter() - t0:.2f} {e}"
+    dist.barrier()  # rank 1 leaves only after rank 0's step has given up
+    with open(os.path.join(outdir, f"missing{rank}.txt"), "w") as f:
+        f.write(result)
+    m.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_a_missing_rank_times_out_instead_of_hanging(tmp_path):
+    """A rank that does not call Forward for a step: the other rank's count
+    exchange runs out (bounded, about 2 s) and its step fails with
+    GTMOE_ETIMEOUT instead of waiting for ever.  The missing rank stays
+    alive on the host, so no kernel or peer mapping of it goes away while the
+    other rank may still use it."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_rank_missing, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    got = (tmp_path / "missing0.txt").read_text()
+    code, secs = got.split()[:2]
+    assert code == "-6", got
+    assert "count exchange gave up" in got
+    assert 1.5 <= float(secs) <= 30, got
