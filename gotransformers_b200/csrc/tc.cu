@@ -315,8 +315,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     uint32_t *tmem_slot = (uint32_t *)(tmem_full + 4);
     volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
     volatile int *tiles_out = (volatile int *)(tmem_slot + 2);  // epilogue warps' finished tiles (x4)
+    // per token stage: 1 when the step belongs to a half-width (N = 96) tile;
+    // written by the leader's producer before it arrives on full[], read by
+    // the issuer after its wait on full[] (the arrival releases it)
+    volatile uint8_t *stage_half = (volatile uint8_t *)(tmem_slot + 3);
     int *prefix_s = (int *)((uint8_t *)bars + R::kBarBytes);
-    static_assert((2 * SB + 2 * SR + 4) * 8 + 12 <= R::kBarBytes, "barrier area");
+    static_assert((2 * SB + 2 * SR + 4) * 8 + 12 + SB <= R::kBarBytes, "barrier area");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -399,7 +403,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     if (!pair_wait<false>(&b_empty[sb], ((uint32_t)(j / SB) & 1) ^ 1, abort_flag, peer_abort, a.err,
                                           1))
                         break;
-                    if (leader) mbar_arrive_expect_tx(&full[sb], 2 * kBStageBytes);
+                    if (leader) {
+                        stage_half[sb] = half_n ? 1 : 0;
+                        mbar_arrive_expect_tx(&full[sb], 2 * kBStageBytes);
+                    }
                     uint8_t *bt = b_tiles + sb * kBStageBytes;
 #pragma unroll
                     for (int i = 0; i < kStepKB; i++)
@@ -420,11 +427,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             uint32_t j = 0;  // steps issued (A ring stage j & 1, use j >> 1; token stage j % SB)
             int acc = 0;
             uint32_t acc_phase = 0;
-            UnitDecoder dec{prefix_s, a.groups, a.n_groups, n_tiles};
             for (int64_t u = cluster; u < total && !*abort_flag; u += n_clusters) {
-                Unit w;
-                dec.advance(u, w);
-                const uint32_t idesc = dec.grp.m - w.mt * kTileTok <= kCtaTok ? kIdescHalf : kIdesc;
                 if (!pair_wait<false>(&tmem_empty[acc], acc_phase ^ 1, abort_flag, peer_abort, a.err, 2)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kAccCols);
@@ -437,6 +440,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                         break;
                     }
                     tc_fence_after();
+                    const uint32_t idesc = stage_half[sb] ? kIdescHalf : kIdesc;
                     const uint32_t a_tmem = tmem_base + (uint32_t)(kRingCol + (j & 1) * kAStageCols);
                     const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + sb * kBStageBytes));
                     umma2_ts_half<0>(d_tmem, a_tmem, bdesc, idesc, s != 0);
