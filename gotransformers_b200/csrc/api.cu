@@ -393,7 +393,7 @@ static std::vector<uint64_t> graph_key(gtmoe_handle *h, const void *x, int x_dty
     std::vector<uint64_t> k = {(uint64_t)(uintptr_t)x, (uint64_t)x_dtype, (uint64_t)T, (uint64_t)(uintptr_t)res,
                                (uint64_t)(uintptr_t)out, (uint64_t)out_dtype, (uint64_t)(uintptr_t)h->stream, wbits,
                                (uint64_t)h->e_pad, (uint64_t)use_tc, (uint64_t)use_decode,
-                               (uint64_t)(uintptr_t)h->tc.err};
+                               (uint64_t)(uintptr_t)h->tc.err, (uint64_t)(uintptr_t)h->gather_bf16};
     const gtmoe::DevBuf *bufs[] = {&h->wr64,   &h->wr32,   &h->br,     &h->bal,    &h->wr3,   &h->table,
                                    &h->logits, &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load,
                                    &h->offsets, &h->perm,  &h->slot_row, &h->groups, &h->tile_prefix, &h->xp,
@@ -517,7 +517,9 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     GT_CHECK(h->phase_end(1));
 
     GT_CHECK(h->phase_begin(2));
-    GT_CHECK(launch_gather(x_dev, x_dtype, T, d, da.perm, TK, S > 0 ? T : 0, S > 0, h->xp.p, compute, st));
+    const bool bf16_rows = h->gather_bf16 && compute == GTMOE_DTYPE_BF16;
+    GT_CHECK(launch_gather(bf16_rows ? h->gather_bf16 : x_dev, bf16_rows ? GTMOE_DTYPE_BF16 : x_dtype, T, d, da.perm,
+                           TK, S > 0 ? T : 0, S > 0, h->xp.p, compute, st));
     GT_CHECK(h->phase_end(2));
 
     if (use_decode) {
@@ -633,7 +635,8 @@ void gtmoe_destroy(gtmoe_t h) {
                           &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load, &h->offsets, &h->perm,
                           &h->slot_row, &h->groups, &h->tile_prefix, &h->xp, &h->hp, &h->yp, &h->out_dev,
                           &h->res_dev, &h->fixups, &h->flagged, &h->x_pipe[0], &h->x_pipe[1], &h->out_pipe[0],
-                          &h->out_pipe[1], &h->load_acc, &h->norm_w, &h->block_x, &h->block_xn};
+                          &h->out_pipe[1], &h->load_acc, &h->norm_w, &h->block_x, &h->block_xn,
+                          &h->block_xn16};
         for (DevBuf *b : bufs) b->release();
         release_training_state(h);
         for (cudaEvent_t e : h->pipe_ev)

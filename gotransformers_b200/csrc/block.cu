@@ -20,7 +20,7 @@ namespace {
 // lane writes its share of the normalized row.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const void *__restrict__ x, int x_dtype, int64_t T, int d,
                                                       const double *__restrict__ w, double eps,
-                                                      double *__restrict__ y) {
+                                                      double *__restrict__ y, __nv_bfloat16 *__restrict__ y16) {
     __shared__ double buf[8][32];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t warps = (int64_t)gridDim.x * 8;
@@ -41,8 +41,11 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void *__restrict__ x
         }
         s = __shfl_sync(0xffffffffu, s, 0);
         const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(s, (double)d), eps));
-        for (int i = lane; i < d; i += 32)
-            y[x0 + i] = __dmul_rn(__ddiv_rn(load_as_double(x, x_dtype, x0 + i), rms), w[i]);
+        for (int i = lane; i < d; i += 32) {
+            const double v = __dmul_rn(__ddiv_rn(load_as_double(x, x_dtype, x0 + i), rms), w[i]);
+            y[x0 + i] = v;
+            y16[x0 + i] = __double2bfloat16(v);  // what the gather would make of v
+        }
     }
 }
 
@@ -92,14 +95,20 @@ int gtmoe_forward_block(gtmoe_t h, const void *x, int x_dtype, int64_t T, const 
             xd = h->block_x.p;
         }
         GT_CHECK(h->block_xn.ensure(sizeof(double) * (size_t)T * d));
+        GT_CHECK(h->block_xn16.ensure(sizeof(__nv_bfloat16) * (size_t)T * d));
         const int64_t blocks = (T + 7) / 8;
         rmsnorm_kernel<<<(unsigned)(blocks < 65535 ? blocks : 65535), 256, 0, h->stream>>>(
-            xd, x_dtype, T, d, h->norm_w.as<double>(), h->norm_eps, h->block_xn.as<double>());
+            xd, x_dtype, T, d, h->norm_w.as<double>(), h->norm_eps, h->block_xn.as<double>(),
+            h->block_xn16.as<__nv_bfloat16>());
         GT_CUDA(cudaGetLastError());
         note_launches(1);
-        // the mixture on the normalized rows (device, float64), the input as the residual
-        return forward_locked(h, h->block_xn.p, GTMOE_DTYPE_F64, T, token_ids, xd, out, out_dtype, chosen, gates, perm,
-                              load);
+        // the mixture on the normalized rows (device, float64; the experts'
+        // bf16 rows gathered from their bf16 rounding), the input as the residual
+        h->gather_bf16 = h->block_xn16.p;
+        const int rc = forward_locked(h, h->block_xn.p, GTMOE_DTYPE_F64, T, token_ids, xd, out, out_dtype, chosen,
+                                      gates, perm, load);
+        h->gather_bf16 = nullptr;
+        return rc;
     }
 }
 

@@ -108,7 +108,11 @@ struct gtmoe_handle {
 
     // the block's RMSNorm (block.cu): weights (d, float64), epsilon, and the
     // input / normalized rows of gtmoe_forward_block
-    DevBuf norm_w, block_x, block_xn;
+    DevBuf norm_w, block_x, block_xn, block_xn16;
+    // set by gtmoe_forward_block for its inner Forward: the bf16 rounding of
+    // the normalized rows, which the gather copies instead of converting the
+    // float64 rows (the same bits: both round the same double once)
+    const void *gather_bf16 = nullptr;
     double norm_eps = 0;
     int norm_set = 0;
 
