@@ -92,15 +92,10 @@ constexpr int kEpiBytes = 2 * kEpiChunk * kGatePitch * 4;  // 17408
 static_assert(kEpiChunk * kDownPitch * 4 <= kEpiBytes, "epilogue staging");
 constexpr int kPrefixCache = 2048;          // m-tile prefix entries cached in shared memory
 constexpr int kBandTiles = 16;              // m-tiles per band of the unit order (UnitDecoder)
-// instruction descriptor: D f32, A bf16, B bf16, both K-major, M = 256 (2-SM),
-// N = 192 (a full tile: 96 tokens from each CTA) or 96 (a group's last tile
-// when it holds at most 96 tokens: 48 from each CTA)
-constexpr uint32_t idesc_n(int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
-}
-constexpr uint32_t kIdesc = idesc_n(kTileTok);
-constexpr uint32_t kIdescHalf = idesc_n(kTileTok / 2);
-static_assert(kTileTok % 32 == 0 && kTileTok <= 256, "UMMA N for M = 256, full and half tiles");
+// instruction descriptor: D f32, A bf16, B bf16, both K-major, N = 192, M = 256 (2-SM)
+constexpr uint32_t kIdesc =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileTok >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+static_assert(kTileTok % 16 == 0 && kTileTok <= 256, "UMMA N for M = 256");
 
 // Raw record geometry and the shared-memory plan of one precision: a ring of
 // token tiles (released when the step's MMAs complete) and a separate ring of
@@ -153,8 +148,7 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 // 16-byte address units).  Only the step's first MMA may start a fresh
 // accumulation.
 template <int HALF>
-__device__ __forceinline__ void umma2_ts_half(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                              bool accumulate) {
+__device__ __forceinline__ void umma2_ts_half(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, bool accumulate) {
     constexpr uint64_t kSub = HALF ? (kBSubBytes >> 4) : 0;
     const uint32_t a0 = a_tmem + HALF * 32;
     asm volatile(
@@ -166,7 +160,7 @@ __device__ __forceinline__ void umma2_ts_half(uint32_t d_tmem, uint32_t a_tmem, 
         "tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %6, %9, t;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %8, %9, t;\n\t}\n" ::"r"(d_tmem),
         "r"(a0), "l"(bdesc + kSub), "r"(a0 + 8), "l"(bdesc + kSub + 2), "r"(a0 + 16), "l"(bdesc + kSub + 4),
-        "r"(a0 + 24), "l"(bdesc + kSub + 6), "r"(idesc), "r"((uint32_t)(HALF || accumulate)));
+        "r"(a0 + 24), "l"(bdesc + kSub + 6), "r"(kIdesc), "r"((uint32_t)(HALF || accumulate)));
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory"); }
@@ -315,12 +309,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     uint32_t *tmem_slot = (uint32_t *)(tmem_full + 4);
     volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
     volatile int *tiles_out = (volatile int *)(tmem_slot + 2);  // epilogue warps' finished tiles (x4)
-    // per token stage: 1 when the step belongs to a half-width (N = 96) tile;
-    // written by the leader's producer before it arrives on full[], read by
-    // the issuer after its wait on full[] (the arrival releases it)
-    volatile uint8_t *stage_half = (volatile uint8_t *)(tmem_slot + 3);
     int *prefix_s = (int *)((uint8_t *)bars + R::kBarBytes);
-    static_assert((2 * SB + 2 * SR + 4) * 8 + 12 + SB <= R::kBarBytes, "barrier area");
+    static_assert((2 * SB + 2 * SR + 4) * 8 + 12 <= R::kBarBytes, "barrier area");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -377,12 +367,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     src1 = GATED ? L.tiled[1] : L.tiled[2];
                 }
                 const Group &grp = dec.grp;
-                // a tail tile of at most 96 tokens runs as N = 96: each CTA
-                // supplies 48 of them (its box still loads 96 rows; the MMA
-                // reads the first 48)
-                const bool half_n = grp.m - w.mt * kTileTok <= kCtaTok;
-                const int row0 = (int)((GATED ? grp.x_row0 : grp.h_row0) + w.mt * kTileTok +
-                                       rank * (half_n ? kCtaTok / 2 : kCtaTok));
+                const int row0 = (int)((GATED ? grp.x_row0 : grp.h_row0) + w.mt * kTileTok + rank * kCtaTok);
                 // this CTA's two 64-row weight blocks: kernel 1 the gate and the up
                 // block of its 64 features, kernel 2 two consecutive blocks
                 const int64_t hb0 = GATED ? 2 * w.nt + rank : 4 * w.nt + 2 * rank;
@@ -403,10 +388,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     if (!pair_wait<false>(&b_empty[sb], ((uint32_t)(j / SB) & 1) ^ 1, abort_flag, peer_abort, a.err,
                                           1))
                         break;
-                    if (leader) {
-                        stage_half[sb] = half_n ? 1 : 0;
-                        mbar_arrive_expect_tx(&full[sb], 2 * kBStageBytes);
-                    }
+                    if (leader) mbar_arrive_expect_tx(&full[sb], 2 * kBStageBytes);
                     uint8_t *bt = b_tiles + sb * kBStageBytes;
 #pragma unroll
                     for (int i = 0; i < kStepKB; i++)
@@ -440,15 +422,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t idesc = stage_half[sb] ? kIdescHalf : kIdesc;
                     const uint32_t a_tmem = tmem_base + (uint32_t)(kRingCol + (j & 1) * kAStageCols);
                     const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + sb * kBStageBytes));
-                    umma2_ts_half<0>(d_tmem, a_tmem, bdesc, idesc, s != 0);
+                    umma2_ts_half<0>(d_tmem, a_tmem, bdesc, s != 0);
                     // probe the next step's barrier between the two halves, so that its
                     // latency overlaps the MMA issue (that phase cannot complete twice
                     // before the next step's MMAs are issued)
                     seen = s + 1 < KS && mbar_try_wait(&full[(j + 1) % SB], ((j + 1) / SB) & 1);
-                    umma2_ts_half<1>(d_tmem, a_tmem, bdesc, idesc, true);
+                    umma2_ts_half<1>(d_tmem, a_tmem, bdesc, true);
                     umma2_commit_mc(&b_empty[sb], 0x3);
                 }
                 if (!ok) break;
