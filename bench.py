@@ -299,6 +299,9 @@ def main():
     for i in range(min(args.steps, 5)):
         if flush:
             flush_buf.fill_(i)
+        # ranks start each step together, so a rank's count-exchange phase
+        # holds the exchange itself, not another rank's host lag
+        barrier()
         step(x, out)
     _lib.check(L.gtmoe_read_timing(moe.handle, phase_ms, _lib.N_PHASES, ctypes.byref(calls), ctypes.byref(plaunch)))
     _lib.check(L.gtmoe_set_timing(moe.handle, 0))
