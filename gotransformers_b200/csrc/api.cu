@@ -362,7 +362,8 @@ static int forward_prepare(gtmoe_handle *h, int64_t T) {
     const int64_t rows_x = (S > 0 ? T : 0) + TK;
     const int64_t rows_h = (int64_t)S * T + TK;
     const int n_chunks = (int)((T + kDispatchChunk - 1) / kDispatchChunk);
-    GT_CHECK(h->logits.ensure(sizeof(double) * (size_t)T * E));
+    // the logits, then ||x_t|| of a few-token batch
+    GT_CHECK(h->logits.ensure(sizeof(double) * ((size_t)T * E + (size_t)std::min<int64_t>(T, kRouterSmallMaxT))));
     GT_CHECK(h->chosen.ensure(sizeof(int32_t) * (size_t)TK));
     GT_CHECK(h->gates64.ensure(sizeof(double) * (size_t)TK));
     GT_CHECK(h->gates32.ensure(sizeof(float) * (size_t)TK));
@@ -388,7 +389,8 @@ static std::vector<uint64_t> graph_key(gtmoe_handle *h, const void *x, int x_dty
     uint64_t wbits;
     memcpy(&wbits, &h->wmax, sizeof(wbits));
     const bool use_tc = tc_supported(h, T);
-    const bool use_decode = use_tc && decode_usable(h->cfg.weight_precision, h->cfg.d_model, h->cfg.hidden, T) &&
+    const bool use_decode = use_tc && decode_usable(h->cfg.weight_precision, h->cfg.d_model, h->cfg.hidden, T,
+                                                      h->cfg.n_shared + h->cfg.n_routed) &&
                             !h->no_decode;
     std::vector<uint64_t> k = {(uint64_t)(uintptr_t)x, (uint64_t)x_dtype, (uint64_t)T, (uint64_t)(uintptr_t)res,
                                (uint64_t)(uintptr_t)out, (uint64_t)out_dtype, (uint64_t)(uintptr_t)h->stream, wbits,
@@ -458,7 +460,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     const bool use_tc = tc_supported(h, T);
     // few rows per expert: stream the weights (decode.cu) instead of 256-row tiles
     const bool use_decode =
-        use_tc && decode_usable(c.weight_precision, d, hd, T) && !h->no_decode;
+        use_tc && decode_usable(c.weight_precision, d, hd, T, S + E) && !h->no_decode;
     const int compute = c.weight_precision == GTMOE_FLOAT64 ? GTMOE_DTYPE_F64
                         : use_tc                            ? GTMOE_DTYPE_BF16
                                                             : GTMOE_DTYPE_F32;
@@ -489,6 +491,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     ra.err = h->tc.err;
     ra.sms = h->tc.sms;
     ra.logits = h->logits.as<double>();
+    ra.xnorm = ra.logits + (size_t)T * E;
     ra.chosen = h->chosen.as<int32_t>();
     ra.gates64 = h->gates64.as<double>();
     ra.gates32 = h->gates32.as<float>();
@@ -511,7 +514,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     da.slot_row = h->slot_row.as<int64_t>();
     da.groups = h->groups.as<Group>();
     da.tile_prefix = h->tile_prefix.as<int64_t>();
-    da.bm = use_decode ? kDecodeTileRows : use_tc ? tc_tile_rows(h->tc) : kSimtBM;
+    da.bm = use_decode ? decode_tile_rows(T) : use_tc ? tc_tile_rows(h->tc) : kSimtBM;
     GT_CHECK(h->phase_begin(1));
     GT_CHECK(launch_dispatch(da, st));
     GT_CHECK(h->phase_end(1));
@@ -537,6 +540,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
         dc.hp = h->hp.p;
         dc.yp = h->yp.p;
         dc.sms = h->tc.sms;
+        dc.tile_rows = decode_tile_rows(T);
         dc.err = h->tc.err;
         GT_CHECK(h->phase_begin(3));
         GT_CHECK(launch_decode(dc, 1, st));

@@ -18,12 +18,27 @@ __device__ __forceinline__ float to_f<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
 
+// The token's output rows and gates, read once into shared memory, so that
+// each thread's loads of the k expert outputs do not wait on them one by one.
+template <typename G>
+__device__ __forceinline__ void stage_slots(const CombineArgs &a, int64_t t, int64_t *srow, G *sgate) {
+    if (threadIdx.x < a.k) {
+        srow[threadIdx.x] = a.routed_row0 + a.slot_row[t * a.k + threadIdx.x];
+        if constexpr (sizeof(G) == 8) sgate[threadIdx.x] = a.gates64[t * a.k + threadIdx.x];
+        else sgate[threadIdx.x] = a.gates32[t * a.k + threadIdx.x];
+    }
+    __syncthreads();
+}
+
 template <typename YT, typename ACC>
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
     const int64_t t = blockIdx.x;
     const YT *__restrict__ y = (const YT *)a.y;
     const YT *__restrict__ yr = (const YT *)(a.y_routed ? a.y_routed : a.y);
     const int d = a.d;
+    __shared__ int64_t srow[kMaxTopK];
+    __shared__ ACC sgate[kMaxTopK];
+    stage_slots(a, t, srow, sgate);
     for (int col = threadIdx.x; col < d; col += blockDim.x) {
         ACC acc = ACC(0);
         for (int s = 0; s < a.S; s++) {
@@ -32,17 +47,12 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
             else v = (ACC)to_f<YT>(y[(a.shared_row0 + (int64_t)s * a.T + t) * d + col]);
             acc = acc + v;
         }
+#pragma unroll 4
         for (int j = 0; j < a.k; j++) {
-            const int64_t row = a.routed_row0 + a.slot_row[t * a.k + j];
-            ACC g, v;
-            if constexpr (sizeof(ACC) == 8) {
-                g = a.gates64[t * a.k + j];
-            } else {
-                g = a.gates32[t * a.k + j];
-            }
-            if constexpr (sizeof(YT) == 8) v = yr[row * d + col];
-            else v = (ACC)to_f<YT>(yr[row * d + col]);
-            acc += g * v;
+            ACC v;
+            if constexpr (sizeof(YT) == 8) v = yr[srow[j] * d + col];
+            else v = (ACC)to_f<YT>(yr[srow[j] * d + col]);
+            acc += sgate[j] * v;
         }
         const int64_t o = t * d + col;
         if (a.residual) acc = (ACC)load_as_double(a.residual, a.out_dtype, o) + acc;
@@ -60,6 +70,9 @@ __global__ void __launch_bounds__(256) combine_bf16x8_kernel(CombineArgs a) {
     const uint4 *__restrict__ y = (const uint4 *)a.y;
     const uint4 *__restrict__ yr = (const uint4 *)(a.y_routed ? a.y_routed : a.y);
     const int dv = a.d / 8;
+    __shared__ int64_t srow[kMaxTopK];
+    __shared__ float sgate[kMaxTopK];
+    stage_slots(a, t, srow, sgate);
     for (int v = threadIdx.x; v < dv; v += blockDim.x) {
         float acc[8];
 #pragma unroll
@@ -74,10 +87,10 @@ __global__ void __launch_bounds__(256) combine_bf16x8_kernel(CombineArgs a) {
                 acc[2 * q + 1] = acc[2 * q + 1] + f.y;
             }
         }
+#pragma unroll 4
         for (int j = 0; j < a.k; j++) {
-            const int64_t row = a.routed_row0 + a.slot_row[t * a.k + j];
-            const float g = a.gates32[t * a.k + j];
-            const uint4 p = yr[row * dv + v];
+            const float g = sgate[j];
+            const uint4 p = yr[srow[j] * dv + v];
             const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&p);
 #pragma unroll
             for (int q = 0; q < 4; q++) {

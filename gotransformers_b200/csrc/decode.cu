@@ -20,8 +20,8 @@
 // bf16 decode, with 11 significant bits instead of 8.  Products accumulate in
 // float32; the epilogue takes the row scales back out.
 //
-// Work unit: (16-row tile of a group, block of 64 output features = one
-// 64-row half of a weight chunk).  A CTA of eight compute warps and one
+// Work unit: (tile of TR = 16 rows of a group, or 8 for batches of at most 8
+// tokens, block of 64 output features = one 64-row half of a weight chunk).  A CTA of eight compute warps and one
 // producer warp runs a unit.  The producer copies the tile's token rows once
 // per unit (one bulk copy per row, all inputs; padded rows: conflict-free
 // fragment loads) and keeps a 2-stage ring of weight steps, one contiguous
@@ -107,20 +107,25 @@ __device__ __forceinline__ void decode_row_block(const uint8_t *codes, float sc,
     }
 }
 
-// Unit u -> (group, 16-row tile, feature block): the m-tile prefix counts
-// tiles of kDecodeTileRows rows per group.
-__device__ __forceinline__ int unit_group(const int64_t *prefix, int n_groups, int64_t tile) {
+// Unit u -> (group, tile, feature block): the m-tile prefix counts tiles of
+// TR rows per group.  The CTA keeps the prefix in shared memory (a search
+// through global memory would cost a dependent load per step, at every unit).
+__device__ __forceinline__ int unit_group(const int *prefix, int n_groups, int tile) {
     int lo = 0, hi = n_groups;  // last g with prefix[g] <= tile
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
-        if (__ldg(prefix + mid) <= tile) lo = mid;
+        if (prefix[mid] <= tile) lo = mid;
         else hi = mid;
     }
     return lo;
 }
 
-template <int PREC, bool GATED>
+// Shared memory of a CTA: the token tile, the weight ring, the tile prefix.
+__host__ __device__ __forceinline__ int decode_prefix_bytes(int n_groups) { return ((n_groups + 1) * 4 + 15) & ~15; }
+
+template <int PREC, bool GATED, int TR>
 __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs a) {
+    static_assert(TR == 8 || TR == 16, "one m16 MMA tile; 8-row tiles leave its rows 8-15 zero");
     using DL = DecodeLayout<PREC>;
     using ST = DecodeStage<PREC, GATED>;
     extern __shared__ __align__(128) uint8_t dsmem[];
@@ -134,14 +139,14 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     const int xpitch = decode_x_pitch(K);
     const __nv_bfloat16 *xin = (const __nv_bfloat16 *)(GATED ? a.xp : a.hp);
     __nv_bfloat16 *out = (__nv_bfloat16 *)(GATED ? a.hp : a.yp);
-    const int64_t units = __ldg(a.tile_prefix + a.n_groups) * blocks;
-    uint8_t *xs = dsmem;                                      // kDecodeTileRows x xpitch
-    uint8_t *ring = dsmem + kDecodeTileRows * xpitch;         // kDecodeStages x ST::kBytes
+    uint8_t *xs = dsmem;                                  // TR x xpitch
+    uint8_t *ring = dsmem + TR * xpitch;                  // kDecodeStages x ST::kBytes
+    int *sprefix = (int *)(ring + kDecodeStages * ST::kBytes);  // n_groups + 1 tile counts
 
     __shared__ uint64_t full[kDecodeStages];   // weight step landed (expect_tx by the producer)
     __shared__ uint64_t empty[kDecodeStages];  // every compute warp is done with the step
     __shared__ uint64_t xfull, xempty;         // token rows of the unit landed / released
-    __shared__ float rscale[kDecodeTileRows];  // 2^-e of each token row (f16 tile = bf16 row * 2^e)
+    __shared__ float rscale[TR];  // 2^-e of each token row (f16 tile = bf16 row * 2^e)
     __shared__ int abort_flag;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDecodeStages; s++) {
@@ -153,7 +158,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    for (int g = threadIdx.x; g <= a.n_groups; g += blockDim.x) sprefix[g] = (int)__ldg(a.tile_prefix + g);
     __syncthreads();
+    const int64_t units = (int64_t)sprefix[a.n_groups] * blocks;
     volatile int *abort_p = (volatile int *)&abort_flag;
     uint32_t n = 0;      // weight steps of this CTA so far: slot = n % S, parity = (n / S) & 1
     uint32_t nu = 0;     // units of this CTA so far (token-row buffer parity)
@@ -164,11 +171,11 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x, nu++) {
         const int64_t tile = u / blocks;
         const int fb = (int)(u % blocks);
-        const int gi = unit_group(a.tile_prefix, a.n_groups, tile);
+        const int gi = unit_group(sprefix, a.n_groups, (int)tile);
         const Group grp = a.groups[gi];
         const ExpertLayers &L = a.experts[grp.expert];
-        const int64_t r0 = (tile - __ldg(a.tile_prefix + gi)) * kDecodeTileRows;  // first row of this tile
-        const int m = grp.m - r0 < kDecodeTileRows ? (int)(grp.m - r0) : kDecodeTileRows;
+        const int64_t r0 = (tile - sprefix[gi]) * TR;  // first row of this tile
+        const int m = grp.m - r0 < TR ? (int)(grp.m - r0) : TR;
 
         if (warp == kComputeWarps) {
             // ---- producer
@@ -206,11 +213,17 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
 #pragma unroll
             for (int c = 0; c < 4; c++) acc[l][c] = 0.f;
         const int row = warp * 8 + g8;  // this lane's weight row (feature) in the half
+        // the epilogue's biases, loaded now so that their latency hides behind the unit
+        const int f = fb * kDecodeFeatures + warp * 8 + 2 * q;
+        const float *bias0 = L.b32[which];
+        const float *bias1 = GATED ? L.b32[1] : nullptr;
+        const float b00 = bias0 ? __ldg(bias0 + f) : 0.f, b01 = bias0 ? __ldg(bias0 + f + 1) : 0.f;
+        const float b10 = bias1 ? __ldg(bias1 + f) : 0.f, b11 = bias1 ? __ldg(bias1 + f + 1) : 0.f;
         if (!*abort_p) mbar_wait(&xfull, nu & 1, abort_p, a.err, 14);
         // bf16 token rows -> f16 in place, each row scaled by the power of two
         // that puts its largest magnitude in [2^14, 2^15): exact, no overflow
 #pragma unroll
-        for (int rr = 0; rr < 2; rr++) {
+        for (int rr = 0; rr < TR / kComputeWarps; rr++) {
             const int r = warp + kComputeWarps * rr;
             if (r >= m) continue;
             uint32_t *p = reinterpret_cast<uint32_t *>(xs + r * xpitch);
@@ -251,7 +264,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
                 for (int s = 0; s < 4; s++) {
                     const uint8_t *xa = xrow + kb * 128 + 32 * s;
                     const uint2 lo = *reinterpret_cast<const uint2 *>(xa);
-                    const uint2 hi = *reinterpret_cast<const uint2 *>(xa + 8 * xpitch);
+                    const uint2 hi = TR > 8 ? *reinterpret_cast<const uint2 *>(xa + 8 * xpitch) : make_uint2(0u, 0u);
                     const uint32_t af[4] = {lo.x, hi.x, lo.y, hi.y};
 #pragma unroll
                     for (int l = 0; l < ST::kLayers; l++) {
@@ -270,7 +283,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
 
         // epilogue: acc[l] = tokens (r0 + g8, r0 + g8 + 8) x features (f, f + 1),
         // in units of the rows' scales
-        const float rs0 = rscale[g8], rs1 = rscale[g8 + 8];
+        const float rs0 = rscale[g8], rs1 = TR > 8 ? rscale[(g8 + 8) % TR] : 0.f;
 #pragma unroll
         for (int l = 0; l < 2; l++) {
             acc[l][0] *= rs0;
@@ -278,14 +291,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             acc[l][2] *= rs1;
             acc[l][3] *= rs1;
         }
-        const int f = fb * kDecodeFeatures + warp * 8 + 2 * q;
-        const float *bias0 = L.b32[which];
-        const float *bias1 = GATED ? L.b32[1] : nullptr;
         const float lim = (float)a.clamp_limit;
-        const float b00 = bias0 ? __ldg(bias0 + f) : 0.f, b01 = bias0 ? __ldg(bias0 + f + 1) : 0.f;
-        const float b10 = bias1 ? __ldg(bias1 + f) : 0.f, b11 = bias1 ? __ldg(bias1 + f + 1) : 0.f;
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
+        for (int hf = 0; hf < TR / 8; hf++) {
             const int t = g8 + 8 * hf;
             if (t >= m) continue;
             float v0 = acc[0][2 * hf] + b00, v1 = acc[0][2 * hf + 1] + b01;
@@ -306,22 +314,25 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     }
 }
 
-template <int PREC, bool GATED>
+template <int PREC, bool GATED, int TR>
 int decode_smem_bytes(const DecodeArgs &a) {
-    return kDecodeTileRows * decode_x_pitch(GATED ? a.d : a.h) + kDecodeStages * DecodeStage<PREC, GATED>::kBytes;
+    return TR * decode_x_pitch(GATED ? a.d : a.h) + kDecodeStages * DecodeStage<PREC, GATED>::kBytes +
+           decode_prefix_bytes(a.n_groups);
 }
 
-template <int PREC, bool GATED>
+template <int PREC, bool GATED, int TR>
 int launch_decode_one(const DecodeArgs &a, cudaStream_t st) {
-    auto kern = decode_kernel<PREC, GATED>;
-    const int smem = decode_smem_bytes<PREC, GATED>(a);
+    auto kern = decode_kernel<PREC, GATED, TR>;
+    const int smem = decode_smem_bytes<PREC, GATED, TR>(a);
     static int attr = 0;
     if (smem > attr) {
         GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr = smem;
     }
-    int per_sm = (220 * 1024) / smem;  // resident CTAs per SM the shared memory allows
-    per_sm = per_sm < 1 ? 1 : per_sm > 4 ? 4 : per_sm;
+    // as many CTAs as fit on an SM (shared memory, registers, threads)
+    int per_sm = 0;
+    GT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecodeThreads, smem));
+    per_sm = per_sm < 1 ? 1 : per_sm;
     kern<<<per_sm * a.sms, kDecodeThreads, smem, st>>>(a);
     GT_CUDA(cudaGetLastError());
     note_launches(1);
@@ -330,19 +341,29 @@ int launch_decode_one(const DecodeArgs &a, cudaStream_t st) {
 
 }  // namespace
 
-bool decode_usable(int precision, int d, int h, int64_t T) {
-    // the token tile of a unit (16 rows x all inputs) and the weight ring fit in shared memory
+bool decode_usable(int precision, int d, int h, int64_t T, int n_groups) {
+    // the token tile of a unit (16 rows x all inputs), the weight ring and the
+    // tile prefix fit in shared memory
     const int kmax = d > h ? d : h;
-    const int smem = kDecodeTileRows * decode_x_pitch(kmax) + kDecodeStages * DecodeStage<GTMOE_INT8, true>::kBytes;
+    const int smem = kDecodeTileRows * decode_x_pitch(kmax) + kDecodeStages * DecodeStage<GTMOE_INT8, true>::kBytes +
+                     decode_prefix_bytes(n_groups);
     return (precision == GTMOE_INT8 || precision == GTMOE_FP4) && T <= kDecodeMaxRows &&
            d % (64 * kDecodeStepKB) == 0 && h % (64 * kDecodeStepKB) == 0 && d % 128 == 0 && h % 128 == 0 &&
            smem <= 200 * 1024;
 }
 
-int launch_decode(const DecodeArgs &a, int which, cudaStream_t st) {
+template <int TR>
+static int launch_decode_rows(const DecodeArgs &a, int which, cudaStream_t st) {
     if (a.precision == GTMOE_INT8)
-        return which == 1 ? launch_decode_one<GTMOE_INT8, true>(a, st) : launch_decode_one<GTMOE_INT8, false>(a, st);
-    return which == 1 ? launch_decode_one<GTMOE_FP4, true>(a, st) : launch_decode_one<GTMOE_FP4, false>(a, st);
+        return which == 1 ? launch_decode_one<GTMOE_INT8, true, TR>(a, st)
+                          : launch_decode_one<GTMOE_INT8, false, TR>(a, st);
+    return which == 1 ? launch_decode_one<GTMOE_FP4, true, TR>(a, st) : launch_decode_one<GTMOE_FP4, false, TR>(a, st);
+}
+
+int launch_decode(const DecodeArgs &a, int which, cudaStream_t st) {
+    if (a.tile_rows != 8 && a.tile_rows != kDecodeTileRows)
+        return fail(GTMOE_EINVAL, "decode tiles of %d rows (8 or 16 supported)", a.tile_rows);
+    return a.tile_rows == 8 ? launch_decode_rows<8>(a, which, st) : launch_decode_rows<kDecodeTileRows>(a, which, st);
 }
 
 }  // namespace gtmoe

@@ -544,7 +544,8 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     }
 
     // ---- routing and dispatch over all E experts (this rank's tokens)
-    GT_CHECK(h->logits.ensure(sizeof(double) * (size_t)(T > 0 ? T : 1) * E));
+    GT_CHECK(h->logits.ensure(sizeof(double) *
+                              ((size_t)(T > 0 ? T : 1) * E + (size_t)std::min<int64_t>(T, kRouterSmallMaxT))));
     GT_CHECK(h->chosen.ensure(sizeof(int32_t) * (size_t)(TK > 0 ? TK : 1)));
     GT_CHECK(h->gates64.ensure(sizeof(double) * (size_t)(TK > 0 ? TK : 1)));
     GT_CHECK(h->gates32.ensure(sizeof(float) * (size_t)(TK > 0 ? TK : 1)));
@@ -580,6 +581,7 @@ int ep_forward(gtmoe_handle *h, const void *x, int x_dtype, int64_t T, const int
     ra.err = h->tc.err;
     ra.sms = h->tc.sms;
     ra.logits = h->logits.as<double>();
+    ra.xnorm = ra.logits + (size_t)(T > 0 ? T : 1) * E;
     ra.chosen = h->chosen.as<int32_t>();
     ra.gates64 = h->gates64.as<double>();
     ra.gates32 = h->gates32.as<float>();

@@ -40,7 +40,11 @@ struct RouterArgs {
     float *gates32;             // T x k
     int *n_fixups;              // counter of tokens re-selected in float64
     int *flagged;               // T: tokens whose choice the fix-up kernel settles
+    double *xnorm = nullptr;    // min(T, kRouterSmallMaxT): ||x_t||, left by the few-token logits kernel
 };
+// Batches of at most this many tokens take the one-warp-per-(token, expert)
+// logits kernel (when not on the tensor cores).
+constexpr int64_t kRouterSmallMaxT = 256;
 int launch_router(const RouterArgs &a, cudaStream_t st);
 // Error code the hash router records for a negative device token ID.
 constexpr int kErrNegativeTokenId = 100;
@@ -96,7 +100,11 @@ constexpr int kSimtBM = 64;
 // every group has at most kDecodeMaxRows rows; weights in the tile-chunk
 // layout of the tensor-core path (ExpertLayers::tiled).
 constexpr int kDecodeMaxRows = 64;
-constexpr int kDecodeTileRows = 16;  // rows per decode work unit (dispatch tile height)
+constexpr int kDecodeTileRows = 16;  // most rows per decode work unit (dispatch tile height)
+// rows per decode work unit for a batch of T tokens: no group has more than
+// T rows, so batches of up to 8 tokens use 8-row tiles (half the token tile's
+// shared memory, more CTAs per SM)
+inline int decode_tile_rows(int64_t T) { return T <= 8 ? 8 : kDecodeTileRows; }
 struct DecodeArgs {
     const Group *groups;
     const int64_t *tile_prefix;  // one tile per non-empty group
@@ -108,9 +116,10 @@ struct DecodeArgs {
     void *hp;        // bf16 rows x h
     void *yp;        // bf16 rows x d
     int sms;
+    int tile_rows;  // decode_tile_rows(T): 8 or 16
     int *err;  // device flag: nonzero when a bounded wait expired
 };
-bool decode_usable(int precision, int d, int h, int64_t T);
+bool decode_usable(int precision, int d, int h, int64_t T, int n_groups);  // n_groups = shared + routed
 int launch_decode(const DecodeArgs &a, int which, cudaStream_t st);  // which: 1 gate/up, 2 down
 // which: 1 = gate/up + SwiGLU into hp, 2 = down into yp
 int launch_grouped_simt(const GroupedArgs &a, int which, cudaStream_t st);

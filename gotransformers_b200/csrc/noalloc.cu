@@ -39,7 +39,8 @@ constexpr int64_t kMaxChoices = 524288;  // T * experts_per_token
 constexpr size_t kOffLogits = 0;
 constexpr size_t kOffGates32 = kOffLogits + kMaxLogits * sizeof(double);
 constexpr size_t kOffFlagged = kOffGates32 + kMaxChoices * sizeof(float);
-constexpr size_t kOffCounters = kOffFlagged + kMaxTokens * sizeof(int);  // [0] fix-up count, [1] error word
+constexpr size_t kOffXnorm = kOffFlagged + kMaxTokens * sizeof(int);  // ||x_t|| of a few-token batch
+constexpr size_t kOffCounters = kOffXnorm + kRouterSmallMaxT * sizeof(double);  // [0] fix-up count, [1] error word
 constexpr size_t kScratchBytes = kOffCounters + 256;
 
 constexpr int kMaxDevices = 64;
@@ -141,6 +142,7 @@ extern "C" GTMOE_API int gtmoe_route_noalloc(gtmoe_t h, const void *x, int x_dty
     ra.err = counters + 1;
     ra.sms = sms;
     ra.logits = (double *)(scratch + kOffLogits);
+    ra.xnorm = (double *)(scratch + kOffXnorm);
     ra.chosen = chosen;
     ra.gates64 = gates;
     ra.gates32 = (float *)(scratch + kOffGates32);

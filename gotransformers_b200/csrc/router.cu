@@ -114,37 +114,63 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void *__restri
 // arithmetic is router_logits_kernel's, operation for operation: float32
 // sums of each 16-input block by sequential fmaf from zero, then the blocks
 // added in float64 in input order -- both kernels give the same bits.
-constexpr int kRouterSmallT = 256;
 constexpr int kRouterSmallWarps = 8;
 
 // The warp stages 512-input chunks of the token row and the expert's weight
-// row in shared memory with coalesced loads (element j at j + j/16, so that
-// lane l reading block l's 16 values hits 32 different banks); lane l then
-// forms block l's sum, and the warp adds the chunk's 32 block sums in order.
+// row in shared memory (element j at j + j/16, so that lane l reading block
+// l's 16 values hits 32 different banks); lane l then forms block l's sum,
+// and the warp adds the chunk's 32 block sums in order.  A chunk's 32 loads
+// per lane are issued together into registers, and the next chunk's while
+// the current one is summed, so a row costs about one memory latency rather
+// than one per load.  Warp 0 of the first expert block also sums the
+// token's squares in float64 (||x_t|| for the selection's error margin;
+// squares of float32/bf16 values are exact, float64 rows as loaded), which
+// spares the selection kernel a second pass over the row.
 constexpr int kSmallChunk = 512;
 constexpr int kSmallPitch = kSmallChunk + kSmallChunk / kRouterK;  // 544
+constexpr int kSmallPer = kSmallChunk / 32;                       // loads per lane and chunk
 
 template <int XDT>
 __global__ void __launch_bounds__(kRouterSmallWarps * 32)
     router_logits_small_kernel(const void *__restrict__ x, const float *__restrict__ w, int64_t T, int E, int d,
-                               double *__restrict__ logits) {
+                               double *__restrict__ logits, double *__restrict__ xnorm) {
     __shared__ float xs[kRouterSmallWarps][kSmallPitch];
     __shared__ float ws[kRouterSmallWarps][kSmallPitch];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * kRouterSmallWarps + warp;
     const int64_t t = blockIdx.y;
     if (e >= E) return;
+    const bool norm_warp = xnorm && blockIdx.x == 0 && warp == 0;
     const float *we = w + (int64_t)e * d;
     float *xw = xs[warp], *ww = ws[warp];
+    float rx[kSmallPer], rw[kSmallPer];
+    double sq = 0.0;
+    auto fetch = [&](int c0) {
+#pragma unroll
+        for (int i = 0; i < kSmallPer; i++) {
+            const int kk = c0 + 32 * i + lane;
+            if (XDT == GTMOE_DTYPE_F64) {
+                const double v = kk < d ? ((const double *)x)[t * d + kk] : 0.0;
+                rx[i] = (float)v;
+                if (norm_warp) sq += v * v;
+            } else {
+                rx[i] = kk < d ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
+                if (norm_warp) sq += (double)rx[i] * (double)rx[i];
+            }
+            rw[i] = kk < d ? __ldg(we + kk) : 0.f;
+        }
+    };
     double acc = 0.0;
+    fetch(0);
     for (int c0 = 0; c0 < d; c0 += kSmallChunk) {
-#pragma unroll 4
-        for (int i = 0; i < kSmallChunk / 32; i++) {
-            const int j = 32 * i + lane, kk = c0 + j;
-            xw[j + j / kRouterK] = kk < d ? load_x_f32<XDT>(x, t * d + kk) : 0.f;
-            ww[j + j / kRouterK] = kk < d ? __ldg(we + kk) : 0.f;
+#pragma unroll
+        for (int i = 0; i < kSmallPer; i++) {
+            const int j = 32 * i + lane;
+            xw[j + j / kRouterK] = rx[i];
+            ww[j + j / kRouterK] = rw[i];
         }
         __syncwarp();
+        if (c0 + kSmallChunk < d) fetch(c0 + kSmallChunk);
         float p = 0.f;  // block (c0 / 16 + lane): inputs past d are zero products
 #pragma unroll
         for (int c = 0; c < kRouterK; c++) p = fmaf(xw[lane * (kRouterK + 1) + c], ww[lane * (kRouterK + 1) + c], p);
@@ -153,6 +179,11 @@ __global__ void __launch_bounds__(kRouterSmallWarps * 32)
         __syncwarp();
     }
     if (lane == 0) logits[t * E + e] = acc;
+    if (norm_warp) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        if (lane == 0) xnorm[t] = sqrt(sq);
+    }
 }
 
 // activationfunction/moreactivationfunctions.go:8-16, mixtureofexperts.go:80-82
@@ -357,15 +388,16 @@ __device__ double exact_dot_warp(const void *x, int64_t x0, const double *__rest
 template <int XDT, int MAXJ>
 __device__ void fixup_token(int64_t t, const double *__restrict__ logits, const double *__restrict__ bias,
                             const double *__restrict__ balance, int E, int k, const void *__restrict__ x, int d,
-                            const double *__restrict__ w64, double thresh_scale, int32_t *__restrict__ chosen,
-                            double *__restrict__ gates64, float *__restrict__ gates32, double *wbuf) {
+                            const double *__restrict__ w64, double thresh_scale, const double *__restrict__ xnorm,
+                            int32_t *__restrict__ chosen, double *__restrict__ gates64, float *__restrict__ gates32,
+                            double *wbuf) {
     const int lane = threadIdx.x & 31;
     double score[MAXJ], aff[MAXJ];
     load_scores<XDT, MAXJ>(logits, bias, balance, t, E, score, aff);
     int pick[kMaxTopK + 1];
     double pscore[kMaxTopK + 1], paff[kMaxTopK + 1];
     warp_top<MAXJ>(score, aff, 0u, E, k + 1, pick, pscore, paff);
-    const double thresh = thresh_scale * warp_x_norm<XDT>(x, t, d);
+    const double thresh = thresh_scale * (xnorm ? xnorm[t] : warp_x_norm<XDT>(x, t, d));
     const double L = pscore[k - 1], U = pscore[k];
     uint32_t sure = 0, unsure = 0;
 #pragma unroll
@@ -417,16 +449,16 @@ template <int XDT, int MAXJ>
 __global__ void __launch_bounds__(256)
     router_fixup_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
                         const double *__restrict__ balance, int E, int k, const void *__restrict__ x, int d,
-                        const double *__restrict__ w64, double thresh_scale, int32_t *__restrict__ chosen,
-                        double *__restrict__ gates64, float *__restrict__ gates32, const int *__restrict__ flagged,
-                        const int *__restrict__ n_flagged) {
+                        const double *__restrict__ w64, double thresh_scale, const double *__restrict__ xnorm,
+                        int32_t *__restrict__ chosen, double *__restrict__ gates64, float *__restrict__ gates32,
+                        const int *__restrict__ flagged, const int *__restrict__ n_flagged) {
     const int warps = (gridDim.x * blockDim.x) >> 5;
     const int n = *n_flagged;
     __shared__ double wsum[8][32];  // per warp: one batch of products (exact_dot_warp)
     double *wbuf = wsum[threadIdx.x >> 5];
     for (int wi = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); wi < n; wi += warps)
-        fixup_token<XDT, MAXJ>(flagged[wi], logits, bias, balance, E, k, x, d, w64, thresh_scale, chosen, gates64,
-                               gates32, wbuf);
+        fixup_token<XDT, MAXJ>(flagged[wi], logits, bias, balance, E, k, x, d, w64, thresh_scale, xnorm, chosen,
+                               gates64, gates32, wbuf);
 }
 
 // One warp per token: scores from the fast logits, top-(k+1), and either the
@@ -437,9 +469,9 @@ template <int XDT, int MAXJ, bool INLINE_FIXUP>
 __global__ void __launch_bounds__(256)
     router_select_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
                          const double *__restrict__ balance, int64_t T, int E, int k, const void *__restrict__ x, int d,
-                         double thresh_scale, int32_t *__restrict__ chosen, double *__restrict__ gates64,
-                         float *__restrict__ gates32, int *__restrict__ flagged, int *__restrict__ n_flagged,
-                         const double *__restrict__ w64) {
+                         double thresh_scale, const double *__restrict__ xnorm, int32_t *__restrict__ chosen,
+                         double *__restrict__ gates64, float *__restrict__ gates32, int *__restrict__ flagged,
+                         int *__restrict__ n_flagged, const double *__restrict__ w64) {
     __shared__ double wsum[INLINE_FIXUP ? 8 : 1][32];  // inline fix-up: per warp one batch of products
     const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -451,12 +483,12 @@ __global__ void __launch_bounds__(256)
     const int count = k < E ? k + 1 : k;
     warp_top<MAXJ>(score, aff, 0u, E, count, pick, pscore, paff);
     if (k < E) {
-        const double thresh = thresh_scale * warp_x_norm<XDT>(x, t, d);
+        const double thresh = thresh_scale * (xnorm ? xnorm[t] : warp_x_norm<XDT>(x, t, d));
         if (!(pscore[k - 1] - pscore[k] > thresh)) {
             if (INLINE_FIXUP) {
                 // small batches: this warp settles the token itself (one launch fewer)
-                fixup_token<XDT, MAXJ>(t, logits, bias, balance, E, k, x, d, w64, thresh_scale, chosen, gates64,
-                                       gates32, wsum[INLINE_FIXUP ? (threadIdx.x >> 5) : 0]);
+                fixup_token<XDT, MAXJ>(t, logits, bias, balance, E, k, x, d, w64, thresh_scale, xnorm, chosen,
+                                       gates64, gates32, wsum[INLINE_FIXUP ? (threadIdx.x >> 5) : 0]);
             } else if (lane == 0) {
                 flagged[atomicAdd(n_flagged, 1)] = (int)t;
             }
@@ -488,26 +520,26 @@ __global__ void hash_route_kernel(const int64_t *__restrict__ ids, int64_t T, in
 constexpr int64_t kInlineFixupT = 256;
 
 template <int XDT, int MAXJ>
-static int launch_select(const RouterArgs &a, cudaStream_t st) {
+static int launch_select(const RouterArgs &a, const double *xnorm, cudaStream_t st) {
     unsigned sel_blocks = (unsigned)((a.T * 32 + 255) / 256);
     GT_CUDA(cudaMemsetAsync(a.n_fixups, 0, sizeof(int), st));
     // a small batch has few tokens to settle: the select kernel's warps do it
     const bool inline_fixup = a.T <= kInlineFixupT;
     if (inline_fixup)
         router_select_kernel<XDT, MAXJ, true><<<sel_blocks, 256, 0, st>>>(
-            a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d, a.thresh_scale, a.chosen, a.gates64, a.gates32,
-            a.flagged, a.n_fixups, a.w64);
+            a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d, a.thresh_scale, xnorm, a.chosen, a.gates64,
+            a.gates32, a.flagged, a.n_fixups, a.w64);
     else
         router_select_kernel<XDT, MAXJ, false><<<sel_blocks, 256, 0, st>>>(
-            a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d, a.thresh_scale, a.chosen, a.gates64, a.gates32,
-            a.flagged, a.n_fixups, a.w64);
+            a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d, a.thresh_scale, xnorm, a.chosen, a.gates64,
+            a.gates32, a.flagged, a.n_fixups, a.w64);
     GT_CUDA(cudaGetLastError());
     if (a.k < a.E && !inline_fixup) {
         int64_t want = (a.T * 32 + 255) / 256;
         unsigned fix_blocks = (unsigned)(want < (int64_t)a.sms * 8 ? want : (int64_t)a.sms * 8);
         router_fixup_kernel<XDT, MAXJ><<<fix_blocks, 256, 0, st>>>(a.logits, a.bias, a.balance, a.E, a.k, a.x, a.d,
-                                                                   a.w64, a.thresh_scale, a.chosen, a.gates64,
-                                                                   a.gates32, a.flagged, a.n_fixups);
+                                                                   a.w64, a.thresh_scale, xnorm, a.chosen,
+                                                                   a.gates64, a.gates32, a.flagged, a.n_fixups);
         GT_CUDA(cudaGetLastError());
         note_launches(1);
     }
@@ -516,13 +548,13 @@ static int launch_select(const RouterArgs &a, cudaStream_t st) {
 }
 
 template <int XDT>
-static int launch_select_e(const RouterArgs &a, cudaStream_t st) {
-    if (a.E <= 32) return launch_select<XDT, 1>(a, st);
-    if (a.E <= 64) return launch_select<XDT, 2>(a, st);
-    if (a.E <= 128) return launch_select<XDT, 4>(a, st);
-    if (a.E <= 256) return launch_select<XDT, 8>(a, st);
-    if (a.E <= 512) return launch_select<XDT, 16>(a, st);
-    return launch_select<XDT, 32>(a, st);
+static int launch_select_e(const RouterArgs &a, const double *xnorm, cudaStream_t st) {
+    if (a.E <= 32) return launch_select<XDT, 1>(a, xnorm, st);
+    if (a.E <= 64) return launch_select<XDT, 2>(a, xnorm, st);
+    if (a.E <= 128) return launch_select<XDT, 4>(a, xnorm, st);
+    if (a.E <= 256) return launch_select<XDT, 8>(a, xnorm, st);
+    if (a.E <= 512) return launch_select<XDT, 16>(a, xnorm, st);
+    return launch_select<XDT, 32>(a, xnorm, st);
 }
 
 int launch_router(const RouterArgs &a, cudaStream_t st) {
@@ -534,21 +566,23 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
         note_launches(1);
         return 0;
     }
+    const double *xnorm = nullptr;  // ||x_t|| per token, when the logits kernel left it
     if (a.use_tc) {
         GT_CHECK(launch_router_logits_tc(a.x, a.T, a.d, a.E, a.e_pad, a.w3, a.logits, a.err, a.sms, st));
-    } else if (a.T <= kRouterSmallT) {
+    } else if (a.T <= kRouterSmallMaxT) {
         dim3 grid((unsigned)((a.E + kRouterSmallWarps - 1) / kRouterSmallWarps), (unsigned)a.T);
         if (a.x_dtype == GTMOE_DTYPE_F64)
-            router_logits_small_kernel<GTMOE_DTYPE_F64><<<grid, kRouterSmallWarps * 32, 0, st>>>(a.x, a.w32, a.T,
-                                                                                                  a.E, a.d, a.logits);
+            router_logits_small_kernel<GTMOE_DTYPE_F64><<<grid, kRouterSmallWarps * 32, 0, st>>>(
+                a.x, a.w32, a.T, a.E, a.d, a.logits, a.xnorm);
         else if (a.x_dtype == GTMOE_DTYPE_F32)
-            router_logits_small_kernel<GTMOE_DTYPE_F32><<<grid, kRouterSmallWarps * 32, 0, st>>>(a.x, a.w32, a.T,
-                                                                                                  a.E, a.d, a.logits);
+            router_logits_small_kernel<GTMOE_DTYPE_F32><<<grid, kRouterSmallWarps * 32, 0, st>>>(
+                a.x, a.w32, a.T, a.E, a.d, a.logits, a.xnorm);
         else
             router_logits_small_kernel<GTMOE_DTYPE_BF16><<<grid, kRouterSmallWarps * 32, 0, st>>>(
-                a.x, a.w32, a.T, a.E, a.d, a.logits);
+                a.x, a.w32, a.T, a.E, a.d, a.logits, a.xnorm);
         GT_CUDA(cudaGetLastError());
         note_launches(1);
+        xnorm = a.xnorm;
     } else {
         dim3 grid((unsigned)((a.T + kRouterTile - 1) / kRouterTile),
                   (unsigned)((a.E + kRouterTile - 1) / kRouterTile));
@@ -561,9 +595,9 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
         GT_CUDA(cudaGetLastError());
         note_launches(1);
     }
-    if (a.x_dtype == GTMOE_DTYPE_F64) return launch_select_e<GTMOE_DTYPE_F64>(a, st);
-    if (a.x_dtype == GTMOE_DTYPE_F32) return launch_select_e<GTMOE_DTYPE_F32>(a, st);
-    return launch_select_e<GTMOE_DTYPE_BF16>(a, st);
+    if (a.x_dtype == GTMOE_DTYPE_F64) return launch_select_e<GTMOE_DTYPE_F64>(a, xnorm, st);
+    if (a.x_dtype == GTMOE_DTYPE_F32) return launch_select_e<GTMOE_DTYPE_F32>(a, xnorm, st);
+    return launch_select_e<GTMOE_DTYPE_BF16>(a, xnorm, st);
 }
 
 }  // namespace gtmoe
