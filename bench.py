@@ -48,9 +48,9 @@ def parse_args():
     p.add_argument("--config", default="c5")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--mode", default="auto", choices=["auto", "ep", "replicas"],
-                   help="multi-GPU mode: expert parallel (routed experts sharded by index; token rows exchanged "
-                        "by peer stores over NVLink, per-expert counts by an NCCL all-gather) or token-sharded "
-                        "replicas of the whole layer")
+                   help="multi-GPU mode: expert parallel (routed experts sharded by index; token rows and the "
+                        "per-expert counts exchanged by peer stores over NVLink) or token-sharded replicas of the "
+                        "whole layer")
     p.add_argument("--replicas", default="auto",
                    help="expert parallel: hot experts held on every rank ('auto': chosen from the config's expected "
                         "expert popularity, '0': none -- routed experts purely owned by index, or a number: the "

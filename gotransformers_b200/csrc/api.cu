@@ -497,9 +497,6 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     ra.gates32 = h->gates32.as<float>();
     ra.n_fixups = h->fixups.as<int>();
     ra.flagged = h->flagged.as<int>();
-    GT_CHECK(h->phase_begin(0));
-    GT_CHECK(launch_router(ra, st));
-    GT_CHECK(h->phase_end(0));
 
     DispatchArgs da;
     da.T = T;
@@ -515,14 +512,21 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     da.groups = h->groups.as<Group>();
     da.tile_prefix = h->tile_prefix.as<int64_t>();
     da.bm = use_decode ? decode_tile_rows(T) : use_tc ? tc_tile_rows(h->tc) : kSimtBM;
-    GT_CHECK(h->phase_begin(1));
-    GT_CHECK(launch_dispatch(da, st));
-    GT_CHECK(h->phase_end(1));
+    ra.dispatch = &da;  // a small batch's router runs the dispatch too (its phase then holds both)
+
+    GT_CHECK(h->phase_begin(0));
+    GT_CHECK(launch_router(ra, st));
+    GT_CHECK(h->phase_end(0));
+    if (!router_fuses_dispatch(ra)) {
+        GT_CHECK(h->phase_begin(1));
+        GT_CHECK(launch_dispatch(da, st));
+        GT_CHECK(h->phase_end(1));
+    }
 
     GT_CHECK(h->phase_begin(2));
     const bool bf16_rows = h->gather_bf16 && compute == GTMOE_DTYPE_BF16;
-    GT_CHECK(launch_gather(bf16_rows ? h->gather_bf16 : x_dev, bf16_rows ? GTMOE_DTYPE_BF16 : x_dtype, T, d, da.perm,
-                           TK, S > 0 ? T : 0, S > 0, h->xp.p, compute, st));
+    GT_CHECK(launch_gather(bf16_rows ? h->gather_bf16 : x_dev, bf16_rows ? GTMOE_DTYPE_BF16 : x_dtype, T, d,
+                           da.slot_row, k, S > 0 ? T : 0, S > 0, h->xp.p, compute, st));
     GT_CHECK(h->phase_end(2));
 
     if (use_decode) {

@@ -14,11 +14,16 @@
 // Arithmetic: the token rows (bf16) are converted once per unit to f16,
 // each row scaled by a power of two that puts its largest magnitude in
 // [2^14, 2^15) (exact for every value above 2^-28 of the row's largest,
-// since bf16 significands fit f16's), and the weights
-// are decoded to f16(code * scale) -- for Int8 two byte permutes, a packed
-// subtraction and a packed multiplication per four codes, half the work of a
-// bf16 decode, with 11 significant bits instead of 8.  Products accumulate in
-// float32; the epilogue takes the row scales back out.
+// since bf16 significands fit f16's), and the weight codes are decoded to
+// their unscaled values, exact in f16 (Int8: two byte permutes and a packed
+// subtraction per four codes).  One MMA k-step is one 16-input block, which
+// shares one float32 scale per weight row, so each MMA runs from a zero
+// accumulator and its float32 result is scaled and added to the row's sum
+// (fmaf): the products are exact, the scale is applied at full float32
+// precision, and the MMAs of a step do not wait on one another.  Int8 16-row
+// tiles instead decode f16(code * scale) and accumulate in the MMA
+// (decode_scale_after).  The epilogue takes the token rows' power-of-two
+// scales back out.
 //
 // Work unit: (tile of TR = 16 rows of a group, or 8 for batches of at most 8
 // tokens, block of 64 output features = one 64-row half of a weight chunk).  A CTA of eight compute warps and one
@@ -80,31 +85,69 @@ __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t b
 }
 
 // Not volatile: a pure function of its operands, so the compiler may overlap
-// the next block's loads and decoding with it.
+// the next block's loads and decoding with it.  d = A B (no accumulator
+// input): one 16-input block's products, scaled by the caller.
+__device__ __forceinline__ void mma_f16_16816_zero(float *d, const uint32_t *a, uint32_t b0, uint32_t b1) {
+    const float z = 0.f;
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
+}
+
+// B fragment of one weight row (16 inputs of block s): two f16x2, k-slots
+// (2q, 2q+1) and (2q+8, 2q+9) = physical inputs 4q..4q+3.  The codes' values
+// without their block scale (Int8 -127..127, FP4 +-{0, 0.5, .., 6}), exact in
+// f16: the block of 16 inputs is exactly one MMA k-step, so the scale is
+// applied to the MMA's float32 result instead (decode_scale below).
+template <int PREC>
+__device__ __forceinline__ void decode_row_block(const uint8_t *codes, int row, int s, int q, const Fp4Tables &t1,
+                                                 uint32_t *o) {
+    if (PREC == GTMOE_INT8) {
+        // stored codes are code + 128: f16 1024 + byte, minus 1152
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(codes + half_code_off(row, 16 * s + 4 * q));
+        const uint32_t h01 = prmt(w, 0x64646464u, 0x5140), h23 = prmt(w, 0x64646464u, 0x7362);
+        const __half2 bias = __floats2half2_rn(1152.f, 1152.f);
+        const __half2 v01 = __hsub2(*reinterpret_cast<const __half2 *>(&h01), bias);
+        const __half2 v23 = __hsub2(*reinterpret_cast<const __half2 *>(&h23), bias);
+        o[0] = *reinterpret_cast<const uint32_t *>(&v01);
+        o[1] = *reinterpret_cast<const uint32_t *>(&v23);
+    } else {
+        const uint32_t w = *reinterpret_cast<const uint16_t *>(codes + half_code_off(row, 8 * s + 2 * q));
+        uint32_t v[4];
+        fp4_decode8(w, t1, v);
+        o[0] = v[0];
+        o[1] = v[1];
+    }
+}
+
+// Int8 with the block scale folded into the weights: f16(code * scale) (one
+// more packed multiplication per four codes), for the kernels that
+// accumulate in the MMA (decode_scale_after below).
+__device__ __forceinline__ void decode_row_block_scaled(const uint8_t *codes, float sc, int row, int s, int q,
+                                                        uint32_t *o) {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(codes + half_code_off(row, 16 * s + 4 * q));
+    int8_decode4_f16(w, pack_f16(sc, sc), o);
+}
+
+// Where the block scale is applied.  After the MMA (zero-accumulator MMA per
+// 16-input block, scaled float32 result added by fmaf): FP4, whose scaled
+// decode would rebuild its lookup table for every block, and 8-row tiles.
+// Before it (f16(code * scale) weights accumulated by the MMA itself): Int8
+// 16-row tiles, where the extra fmaf and registers cost more than the
+// multiplication saves (c4 T=64: gate/up 112 vs 117 us).
+template <int PREC, int TR>
+constexpr bool decode_scale_after() { return PREC == GTMOE_FP4 || TR == 8; }
+
 __device__ __forceinline__ void mma_f16_16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
-    asm(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// B fragment of one weight row (16 inputs of block s): two f16x2, k-slots
-// (2q, 2q+1) and (2q+8, 2q+9) = physical inputs 4q..4q+3.
-template <int PREC>
-__device__ __forceinline__ void decode_row_block(const uint8_t *codes, float sc, int row, int s, int q, uint32_t *o) {
-    using DL = DecodeLayout<PREC>;
-    if (PREC == GTMOE_INT8) {
-        const uint32_t w = *reinterpret_cast<const uint32_t *>(codes + half_code_off(row, 16 * s + 4 * q));
-        int8_decode4_f16(w, pack_f16(sc, sc), o);
-    } else {
-        const uint32_t w = *reinterpret_cast<const uint16_t *>(codes + half_code_off(row, 8 * s + 2 * q));
-        const Fp4Tables t = fp4_tables_f16(sc);
-        uint32_t v[4];
-        fp4_decode8(w, t, v);
-        o[0] = v[0];
-        o[1] = v[1];
-    }
+__device__ __forceinline__ float pick4(const float4 &v, int s) {
+    return s == 0 ? v.x : s == 1 ? v.y : s == 2 ? v.z : v.w;
 }
 
 // Unit u -> (group, tile, feature block): the m-tile prefix counts tiles of
@@ -247,6 +290,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
         const uint8_t *xrow = xs + g8 * xpitch + 8 * q;
+        constexpr bool kAfter = decode_scale_after<PREC, TR>();
+        const int fcol = warp * 8 + 2 * q;  // this lane's two accumulator features in the half
+        const Fp4Tables t1 = fp4_tables_f16(1.f);
         for (int kb0 = 0; kb0 < KB; kb0 += kDecodeStepKB, n++) {
             const uint32_t slot = n % kDecodeStages;
             if (!*abort_p) mbar_wait(&full[slot], (n / kDecodeStages) & 1, abort_p, a.err, 9);
@@ -255,11 +301,20 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
 #pragma unroll
             for (int sub = 0; sub < kDecodeStepKB; sub++) {
                 const int kb = kb0 + sub;
-                float4 sc[2];
+                // block scales: after the MMA those of the accumulator features
+                // fcol and fcol + 1, before it those of this lane's decode row
+                float4 sa[2], sb[2];
 #pragma unroll
-                for (int l = 0; l < ST::kLayers; l++)
-                    sc[l] = *reinterpret_cast<const float4 *>(st + l * ST::kLayerBytes + sub * DL::kHalf +
-                                                              half_scale_off(row, DL::kCodeBytes));
+                for (int l = 0; l < ST::kLayers; l++) {
+                    const uint8_t *rec = st + l * ST::kLayerBytes + sub * DL::kHalf;
+                    if constexpr (kAfter) {
+                        const uint8_t *sp = rec + half_scale_off(fcol, DL::kCodeBytes);
+                        sa[l] = *reinterpret_cast<const float4 *>(sp);
+                        sb[l] = *reinterpret_cast<const float4 *>(sp + 16);
+                    } else {
+                        sa[l] = *reinterpret_cast<const float4 *>(rec + half_scale_off(row, DL::kCodeBytes));
+                    }
+                }
 #pragma unroll
                 for (int s = 0; s < 4; s++) {
                     const uint8_t *xa = xrow + kb * 128 + 32 * s;
@@ -268,10 +323,21 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
                     const uint32_t af[4] = {lo.x, hi.x, lo.y, hi.y};
 #pragma unroll
                     for (int l = 0; l < ST::kLayers; l++) {
-                        const float scl = s == 0 ? sc[l].x : s == 1 ? sc[l].y : s == 2 ? sc[l].z : sc[l].w;
+                        const uint8_t *rec = st + l * ST::kLayerBytes + sub * DL::kHalf;
                         uint32_t bw[2];
-                        decode_row_block<PREC>(st + l * ST::kLayerBytes + sub * DL::kHalf, scl, row, s, q, bw);
-                        mma_f16_16816(acc[l], af, bw[0], bw[1]);
+                        if constexpr (kAfter) {
+                            decode_row_block<PREC>(rec, row, s, q, t1, bw);
+                            float dd[4];
+                            mma_f16_16816_zero(dd, af, bw[0], bw[1]);
+                            const float ka = pick4(sa[l], s), kbs = pick4(sb[l], s);
+                            acc[l][0] = fmaf(ka, dd[0], acc[l][0]);
+                            acc[l][1] = fmaf(kbs, dd[1], acc[l][1]);
+                            acc[l][2] = fmaf(ka, dd[2], acc[l][2]);
+                            acc[l][3] = fmaf(kbs, dd[3], acc[l][3]);
+                        } else {
+                            decode_row_block_scaled(rec, pick4(sa[l], s), row, s, q, bw);
+                            mma_f16_16816(acc[l], af, bw[0], bw[1]);
+                        }
                     }
                 }
             }

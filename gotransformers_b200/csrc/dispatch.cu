@@ -10,6 +10,7 @@
 // decide a position.
 #include "common.cuh"
 #include "internal.h"
+#include "dispatch_small.cuh"
 
 namespace gtmoe {
 
@@ -99,108 +100,16 @@ __global__ void dispatch_scatter_kernel(const int32_t *__restrict__ chosen, cons
 }
 
 // A batch of at most one chunk (decode-shaped): count, scan and scatter of
-// the three kernels above in one CTA, with the same arithmetic and the same
-// outputs, so that a small forward pays one launch for its dispatch.  The
-// scan over experts runs on all threads (each a run of consecutive experts,
-// then a block-wide exclusive scan of the runs' row and tile counts), so the
-// group table is written in parallel instead of by one thread.
-constexpr int kSmallDispatchThreads = 1024;
-
+// the three kernels above in one CTA (dispatch_small.cuh), so that a small
+// forward pays one launch for its dispatch.
 __global__ void __launch_bounds__(kSmallDispatchThreads)
     dispatch_small_kernel(const int32_t *__restrict__ chosen, int64_t T, int E, int k, int S, int bm,
                           int64_t *__restrict__ load, int64_t *__restrict__ offsets, Group *__restrict__ groups,
                           int64_t *__restrict__ tile_prefix, int32_t *__restrict__ perm,
                           int64_t *__restrict__ slot_row) {
-    extern __shared__ int64_t base[];  // E: next position of each expert's rows
-    int32_t *cnt = reinterpret_cast<int32_t *>(base + E);
-    __shared__ int64_t wrows[kSmallDispatchThreads / 32], wtiles[kSmallDispatchThreads / 32];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
-    __syncthreads();
-    for (int64_t p = tid; p < T * k; p += blockDim.x) atomicAdd(&cnt[chosen[p]], 1);
-    __syncthreads();
-    // this thread's run of experts [e0, e1)
-    const int per = (E + blockDim.x - 1) / blockDim.x;
-    const int e0 = min(E, tid * per), e1 = min(E, e0 + per);
-    int64_t rows = 0, tiles = 0;
-    for (int e = e0; e < e1; e++) {
-        rows += cnt[e];
-        tiles += (cnt[e] + bm - 1) / bm;
-    }
-    // exclusive scan of (rows, tiles) over the threads
-    int64_t ir = rows, it = tiles;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const int64_t r = __shfl_up_sync(0xffffffffu, ir, off), q = __shfl_up_sync(0xffffffffu, it, off);
-        if (lane >= off) {
-            ir += r;
-            it += q;
-        }
-    }
-    if (lane == 31) {
-        wrows[warp] = ir;
-        wtiles[warp] = it;
-    }
-    __syncthreads();
-    if (warp == 0) {
-        const int nw = blockDim.x >> 5;
-        int64_t r = lane < nw ? wrows[lane] : 0, q = lane < nw ? wtiles[lane] : 0;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int64_t r2 = __shfl_up_sync(0xffffffffu, r, off), q2 = __shfl_up_sync(0xffffffffu, q, off);
-            if (lane >= off) {
-                r += r2;
-                q += q2;
-            }
-        }
-        if (lane < nw) {
-            wrows[lane] = r;  // inclusive over warps
-            wtiles[lane] = q;
-        }
-    }
-    __syncthreads();
-    const int64_t shared_tiles = (int64_t)S * ((T + bm - 1) / bm);
-    int64_t off = ir - rows + (warp > 0 ? wrows[warp - 1] : 0);
-    int64_t tl = shared_tiles + it - tiles + (warp > 0 ? wtiles[warp - 1] : 0);
-    const int64_t xbase = S > 0 ? T : 0;
-    for (int e = e0; e < e1; e++) {
-        const int64_t n = cnt[e];
-        load[e] = n;
-        offsets[e] = off;
-        base[e] = off;
-        groups[S + e] = Group{xbase + off, (int64_t)S * T + off, n, S + e, 0};
-        tile_prefix[S + e] = tl;
-        tl += (n + bm - 1) / bm;
-        off += n;
-    }
-    if (tid < S) {
-        groups[tid] = Group{0, (int64_t)tid * T, T, tid, 0};
-        tile_prefix[tid] = (int64_t)tid * ((T + bm - 1) / bm);
-    }
-    if (tid == blockDim.x - 1) {  // the last run ends at the totals
-        offsets[E] = off;
-        tile_prefix[S + E] = tl;
-    }
-    __syncthreads();
-    if (warp == 0) {  // the scatter of dispatch_scatter_kernel, one warp over the chunk
-        const uint32_t lt = (1u << lane) - 1u;
-        for (int64_t p0 = 0; p0 < T * k; p0 += 32) {
-            const int64_t p = p0 + lane;
-            const bool valid = p < T * k;
-            const int e = valid ? chosen[p] : -1;
-            const uint32_t peers = __match_any_sync(0xffffffffu, e);
-            const int rank = __popc(peers & lt);
-            int64_t pos = 0;
-            if (valid) pos = base[e] + rank;
-            __syncwarp();
-            if (valid) {
-                perm[pos] = (int32_t)(p / k);
-                slot_row[p] = pos;
-                if (rank == 0) base[e] += __popc(peers);
-            }
-            __syncwarp();
-        }
-    }
+    extern __shared__ int64_t base[];  // E: next position of each expert's rows, then E int32 counts
+    dispatch_small_body(chosen, T, E, k, S, bm, load, offsets, groups, tile_prefix, perm, slot_row, base,
+                        reinterpret_cast<int32_t *>(base + E));
 }
 
 int launch_dispatch(const DispatchArgs &a, cudaStream_t st) {
@@ -230,11 +139,20 @@ int launch_dispatch(const DispatchArgs &a, cudaStream_t st) {
     return 0;
 }
 
-// One CTA of kGatherThreads per row; each thread's loads of a row are issued
-// kGatherUnroll at a time, so a row of a few-token batch costs about one memory
-// latency.
+// The gather is token-major: each token row of x is read once and written
+// to its shared-expert row (row t) and to its k routed rows (the dispatch's
+// slot_row), so x is read from memory once instead of once per copy (the
+// routed order visits the tokens in expert order, which at c5-like sizes does
+// not stay in L2 between an expert and the next).
+
+// Conversions: one CTA of kGatherThreads per token; each thread's loads of a
+// row are issued kGatherUnroll at a time, so a row of a few-token batch costs
+// about one memory latency.  A batch too small to fill the GPU this way
+// (fewer than kGatherSplitCtas tokens x copies) takes one CTA per (token,
+// copy) instead (gridDim.y = copies): its rows are in L2 anyway.
 constexpr int kGatherThreads = 256;
 constexpr int kGatherUnroll = 8;
+constexpr int64_t kGatherSplitCtas = 296;
 
 template <typename IN>
 __device__ __forceinline__ double in_as_double(IN v) {
@@ -244,21 +162,18 @@ __device__ __forceinline__ double in_as_double(IN v) {
 
 template <typename IN, typename OUT>
 __global__ void __launch_bounds__(kGatherThreads)
-    gather_kernel(const IN *__restrict__ x, int64_t T, int d, const int32_t *__restrict__ perm, int64_t n_routed,
-                  int64_t xbase, int copy_shared, OUT *__restrict__ xp) {
-    const int64_t w = blockIdx.x;
-    const int64_t n_shared_rows = copy_shared ? T : 0;
-    int64_t src, dst;
-    if (w < n_shared_rows) {
-        src = w;
-        dst = w;
-    } else {
-        const int64_t r = w - n_shared_rows;
-        src = perm[r];
-        dst = xbase + r;
+    gather_kernel(const IN *__restrict__ x, int d, const int64_t *__restrict__ slot_row, int k, int64_t xbase,
+                  int copy_shared, OUT *__restrict__ xp) {
+    const int64_t t = blockIdx.x;
+    __shared__ int64_t dst[kMaxTopK + 1];
+    const int n_dst = (copy_shared ? 1 : 0) + k;
+    if (threadIdx.x < n_dst) {
+        const int j = (int)threadIdx.x - (copy_shared ? 1 : 0);
+        dst[threadIdx.x] = (j < 0 ? t : xbase + slot_row[t * k + j]) * d;
     }
-    const IN *row = x + src * d;
-    OUT *out = xp + dst * d;
+    __syncthreads();
+    const int c0 = gridDim.y > 1 ? (int)blockIdx.y : 0, c1 = gridDim.y > 1 ? c0 + 1 : n_dst;  // copies of this CTA
+    const IN *row = x + t * d;
     constexpr int kStride = kGatherThreads * kGatherUnroll;
     int i = threadIdx.x;
     for (; i + kGatherThreads * (kGatherUnroll - 1) < d; i += kStride) {
@@ -266,60 +181,86 @@ __global__ void __launch_bounds__(kGatherThreads)
 #pragma unroll
         for (int u = 0; u < kGatherUnroll; u++) v[u] = row[i + kGatherThreads * u];
 #pragma unroll
-        for (int u = 0; u < kGatherUnroll; u++) out[i + kGatherThreads * u] = from_double<OUT>(in_as_double(v[u]));
+        for (int u = 0; u < kGatherUnroll; u++) {
+            const OUT o = from_double<OUT>(in_as_double(v[u]));
+            for (int c = c0; c < c1; c++) xp[dst[c] + i + kGatherThreads * u] = o;
+        }
     }
-    for (; i < d; i += kGatherThreads) out[i] = from_double<OUT>(in_as_double(row[i]));
+    for (; i < d; i += kGatherThreads) {
+        const OUT o = from_double<OUT>(in_as_double(row[i]));
+        for (int c = c0; c < c1; c++) xp[dst[c] + i] = o;
+    }
 }
 
 template <typename OUT>
-static void launch_gather_rows(const void *x, int x_dtype, int64_t T, int d, const int32_t *perm, int64_t n_routed,
-                               int64_t xbase, int copy_shared, OUT *xp, int64_t rows, cudaStream_t st) {
+static void launch_gather_rows(const void *x, int x_dtype, int64_t T, int d, const int64_t *slot_row, int k,
+                               int64_t xbase, int copy_shared, OUT *xp, cudaStream_t st) {
+    const int n_dst = (copy_shared ? 1 : 0) + k;
+    const dim3 grid((unsigned)T, T * n_dst < kGatherSplitCtas ? (unsigned)n_dst : 1u);
     if (x_dtype == GTMOE_DTYPE_F64)
-        gather_kernel<double, OUT><<<(unsigned)rows, kGatherThreads, 0, st>>>((const double *)x, T, d, perm, n_routed,
-                                                                             xbase, copy_shared, xp);
+        gather_kernel<double, OUT><<<grid, kGatherThreads, 0, st>>>((const double *)x, d, slot_row, k, xbase,
+                                                                   copy_shared, xp);
     else if (x_dtype == GTMOE_DTYPE_F32)
-        gather_kernel<float, OUT><<<(unsigned)rows, kGatherThreads, 0, st>>>((const float *)x, T, d, perm, n_routed,
-                                                                            xbase, copy_shared, xp);
+        gather_kernel<float, OUT><<<grid, kGatherThreads, 0, st>>>((const float *)x, d, slot_row, k, xbase,
+                                                                  copy_shared, xp);
     else
-        gather_kernel<__nv_bfloat16, OUT><<<(unsigned)rows, kGatherThreads, 0, st>>>(
-            (const __nv_bfloat16 *)x, T, d, perm, n_routed, xbase, copy_shared, xp);
+        gather_kernel<__nv_bfloat16, OUT><<<grid, kGatherThreads, 0, st>>>((const __nv_bfloat16 *)x, d, slot_row, k,
+                                                                          xbase, copy_shared, xp);
 }
 
-// Same-type bf16 rows: 16-byte vector copies.
-__global__ void gather_bf16_vec_kernel(const uint4 *__restrict__ x, int64_t T, int vec_per_row,
-                                       const int32_t *__restrict__ perm, int64_t n_routed, int64_t xbase,
-                                       int copy_shared, uint4 *__restrict__ xp) {
-    int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
-    int64_t n_shared_rows = copy_shared ? T : 0;
-    if (w >= n_shared_rows + n_routed) return;
-    int64_t src, dst;
-    if (w < n_shared_rows) {
-        src = w;
-        dst = w;
-    } else {
-        int64_t r = w - n_shared_rows;
-        src = perm[r];
-        dst = xbase + r;
+// Same-type bf16 rows: one warp per token, 16-byte pieces, four loads in
+// flight per lane, each piece stored to every copy of the row.
+constexpr int kGatherVecUnroll = 4;
+
+__global__ void __launch_bounds__(256)
+    gather_bf16_vec_kernel(const uint4 *__restrict__ x, int64_t T, int dv, const int64_t *__restrict__ slot_row,
+                           int k, int64_t xbase, int copy_shared, uint4 *__restrict__ xp) {
+    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (t >= T) return;
+    // lane j < k holds the first 16-byte piece of routed copy j
+    const int64_t my_dst = lane < k ? (xbase + slot_row[t * k + lane]) * dv : 0;
+    const uint4 *row = x + t * dv;
+    uint4 *shared_row = copy_shared ? xp + t * dv : nullptr;
+    constexpr int kStride = 32 * kGatherVecUnroll;
+    for (int i0 = 0; i0 < dv; i0 += kStride) {
+        uint4 v[kGatherVecUnroll];
+#pragma unroll
+        for (int u = 0; u < kGatherVecUnroll; u++) {
+            const int i = i0 + 32 * u + lane;
+            if (i < dv) v[u] = row[i];
+        }
+#pragma unroll
+        for (int u = 0; u < kGatherVecUnroll; u++) {
+            const int i = i0 + 32 * u + lane;
+            if (shared_row && i < dv) shared_row[i] = v[u];
+        }
+        for (int j = 0; j < k; j++) {
+            const int64_t o = __shfl_sync(0xffffffffu, my_dst, j);
+#pragma unroll
+            for (int u = 0; u < kGatherVecUnroll; u++) {
+                const int i = i0 + 32 * u + lane;
+                if (i < dv) xp[o + i] = v[u];
+            }
+        }
     }
-    for (int i = lane; i < vec_per_row; i += 32) xp[dst * vec_per_row + i] = x[src * vec_per_row + i];
 }
 
-int launch_gather(const void *x, int x_dtype, int64_t T, int d, const int32_t *perm, int64_t n_routed_rows,
-                  int64_t xbase, int copy_shared, void *xp, int xp_dtype, cudaStream_t st) {
-    int64_t rows = (copy_shared ? T : 0) + n_routed_rows;
-    if (rows == 0) return 0;
-    unsigned blocks = (unsigned)((rows * 32 + 255) / 256);
+int launch_gather(const void *x, int x_dtype, int64_t T, int d, const int64_t *slot_row, int k, int64_t xbase,
+                  int copy_shared, void *xp, int xp_dtype, cudaStream_t st) {
+    if (T == 0 || (k == 0 && !copy_shared)) return 0;
+    if (k > kMaxTopK) return fail(GTMOE_EINVAL, "gather: %d copies per token (at most %d)", k, kMaxTopK);
     if (x_dtype == GTMOE_DTYPE_BF16 && xp_dtype == GTMOE_DTYPE_BF16 && d % 8 == 0) {
-        gather_bf16_vec_kernel<<<blocks, 256, 0, st>>>((const uint4 *)x, T, d / 8, perm, n_routed_rows, xbase,
-                                                       copy_shared, (uint4 *)xp);
+        const unsigned blocks = (unsigned)((T * 32 + 255) / 256);
+        gather_bf16_vec_kernel<<<blocks, 256, 0, st>>>((const uint4 *)x, T, d / 8, slot_row, k, xbase, copy_shared,
+                                                       (uint4 *)xp);
     } else if (xp_dtype == GTMOE_DTYPE_F64) {
-        launch_gather_rows<double>(x, x_dtype, T, d, perm, n_routed_rows, xbase, copy_shared, (double *)xp, rows, st);
+        launch_gather_rows<double>(x, x_dtype, T, d, slot_row, k, xbase, copy_shared, (double *)xp, st);
     } else if (xp_dtype == GTMOE_DTYPE_F32) {
-        launch_gather_rows<float>(x, x_dtype, T, d, perm, n_routed_rows, xbase, copy_shared, (float *)xp, rows, st);
+        launch_gather_rows<float>(x, x_dtype, T, d, slot_row, k, xbase, copy_shared, (float *)xp, st);
     } else {
-        launch_gather_rows<__nv_bfloat16>(x, x_dtype, T, d, perm, n_routed_rows, xbase, copy_shared,
-                                          (__nv_bfloat16 *)xp, rows, st);
+        launch_gather_rows<__nv_bfloat16>(x, x_dtype, T, d, slot_row, k, xbase, copy_shared, (__nv_bfloat16 *)xp,
+                                          st);
     }
     GT_CUDA(cudaGetLastError());
     note_launches(1);

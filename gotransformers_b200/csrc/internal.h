@@ -17,6 +17,7 @@ void note_launches(int n);
 constexpr int kMaxRoutedExperts = 1024;
 constexpr int kMaxTopK = 32;
 
+struct DispatchArgs;
 struct RouterArgs {
     int hash;
     const void *x;
@@ -41,11 +42,17 @@ struct RouterArgs {
     int *n_fixups;              // counter of tokens re-selected in float64
     int *flagged;               // T: tokens whose choice the fix-up kernel settles
     double *xnorm = nullptr;    // min(T, kRouterSmallMaxT): ||x_t||, left by the few-token logits kernel
+    // the dispatch of this batch, for a router that runs it itself (router_fuses_dispatch)
+    const DispatchArgs *dispatch = nullptr;
 };
 // Batches of at most this many tokens take the one-warp-per-(token, expert)
 // logits kernel (when not on the tensor cores).
 constexpr int64_t kRouterSmallMaxT = 256;
 int launch_router(const RouterArgs &a, cudaStream_t st);
+// True when launch_router also runs the dispatch of a.dispatch (a batch of at
+// most 32 tokens over at most 128 experts: one CTA selects and dispatches);
+// the caller then skips launch_dispatch.
+bool router_fuses_dispatch(const RouterArgs &a);
 // Error code the hash router records for a negative device token ID.
 constexpr int kErrNegativeTokenId = 100;
 bool router_tc_usable(const void *x, int x_dtype, int64_t T, int d);
@@ -74,10 +81,11 @@ struct DispatchArgs {
 int launch_dispatch(const DispatchArgs &a, cudaStream_t st);
 
 // Gathers activation rows into the expert-sorted buffer, converting dtype.
-// Rows [0, T) are x itself when there are shared experts; routed row r is
-// x[perm[r]] at row xbase + r.
-int launch_gather(const void *x, int x_dtype, int64_t T, int d, const int32_t *perm, int64_t n_routed_rows,
-                  int64_t xbase, int copy_shared, void *xp, int xp_dtype, cudaStream_t st);
+// Rows [0, T) are x itself when there are shared experts (copy_shared); the
+// routed copy j of token t is row xbase + slot_row[t * k + j] (k may be 0:
+// a plain conversion of x).
+int launch_gather(const void *x, int x_dtype, int64_t T, int d, const int64_t *slot_row, int k, int64_t xbase,
+                  int copy_shared, void *xp, int xp_dtype, cudaStream_t st);
 
 // Grouped SwiGLU on SIMT cores, any precision and shape.
 struct GroupedArgs {

@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "dispatch_small.cuh"
 
 namespace gtmoe {
 
@@ -466,16 +467,14 @@ __global__ void __launch_bounds__(256)
 // margin, the token's index on the fix-up list -- or, for a small batch
 // (inline_fixup), the fix-up itself in this warp.
 template <int XDT, int MAXJ, bool INLINE_FIXUP>
-__global__ void __launch_bounds__(256)
-    router_select_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
-                         const double *__restrict__ balance, int64_t T, int E, int k, const void *__restrict__ x, int d,
-                         double thresh_scale, const double *__restrict__ xnorm, int32_t *__restrict__ chosen,
-                         double *__restrict__ gates64, float *__restrict__ gates32, int *__restrict__ flagged,
-                         int *__restrict__ n_flagged, const double *__restrict__ w64) {
-    __shared__ double wsum[INLINE_FIXUP ? 8 : 1][32];  // inline fix-up: per warp one batch of products
-    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+__device__ __forceinline__ void select_token(int64_t t, const double *__restrict__ logits,
+                                             const double *__restrict__ bias, const double *__restrict__ balance,
+                                             int E, int k, const void *__restrict__ x, int d, double thresh_scale,
+                                             const double *__restrict__ xnorm, int32_t *__restrict__ chosen,
+                                             double *__restrict__ gates64, float *__restrict__ gates32,
+                                             int *__restrict__ flagged, int *__restrict__ n_flagged,
+                                             const double *__restrict__ w64, double *wbuf) {
     const int lane = threadIdx.x & 31;
-    if (t >= T) return;
     double score[MAXJ], aff[MAXJ];
     load_scores<XDT, MAXJ>(logits, bias, balance, t, E, score, aff);
     int pick[kMaxTopK + 1];
@@ -488,7 +487,7 @@ __global__ void __launch_bounds__(256)
             if (INLINE_FIXUP) {
                 // small batches: this warp settles the token itself (one launch fewer)
                 fixup_token<XDT, MAXJ>(t, logits, bias, balance, E, k, x, d, w64, thresh_scale, xnorm, chosen,
-                                       gates64, gates32, wsum[INLINE_FIXUP ? (threadIdx.x >> 5) : 0]);
+                                       gates64, gates32, wbuf);
             } else if (lane == 0) {
                 flagged[atomicAdd(n_flagged, 1)] = (int)t;
             }
@@ -496,6 +495,49 @@ __global__ void __launch_bounds__(256)
         }
     }
     write_choice(t, k, pick, paff, chosen, gates64, gates32);
+}
+
+template <int XDT, int MAXJ, bool INLINE_FIXUP>
+__global__ void __launch_bounds__(256)
+    router_select_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
+                         const double *__restrict__ balance, int64_t T, int E, int k, const void *__restrict__ x, int d,
+                         double thresh_scale, const double *__restrict__ xnorm, int32_t *__restrict__ chosen,
+                         double *__restrict__ gates64, float *__restrict__ gates32, int *__restrict__ flagged,
+                         int *__restrict__ n_flagged, const double *__restrict__ w64) {
+    __shared__ double wsum[INLINE_FIXUP ? 8 : 1][32];  // inline fix-up: per warp one batch of products
+    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (t >= T) return;
+    select_token<XDT, MAXJ, INLINE_FIXUP>(t, logits, bias, balance, E, k, x, d, thresh_scale, xnorm, chosen, gates64,
+                                          gates32, flagged, n_flagged, w64,
+                                          wsum[INLINE_FIXUP ? (threadIdx.x >> 5) : 0]);
+}
+
+// A batch of at most kFusedDispatchT tokens: one CTA selects every token's
+// experts (a warp per token, fix-ups inline) and then runs the dispatch on
+// the choices it just wrote (dispatch_small_body), one launch for both.
+constexpr int64_t kFusedDispatchT = 32;
+// ... and at most 128 experts: a warp's scores then fit the registers that
+// 1024 threads leave each thread (64)
+constexpr int kFusedDispatchMaxJ = 4;
+constexpr int kFusedDispatchMaxE = 32 * kFusedDispatchMaxJ;
+
+template <int XDT, int MAXJ>
+__global__ void __launch_bounds__(kSmallDispatchThreads)
+    router_select_dispatch_kernel(const double *__restrict__ logits, const double *__restrict__ bias,
+                                  const double *__restrict__ balance, int64_t T, int E, int k,
+                                  const void *__restrict__ x, int d, double thresh_scale,
+                                  const double *__restrict__ xnorm, int32_t *__restrict__ chosen,
+                                  double *__restrict__ gates64, float *__restrict__ gates32,
+                                  const double *__restrict__ w64, const DispatchArgs da) {
+    extern __shared__ int64_t dsm[];  // dispatch: E int64 positions, E int32 counts
+    __shared__ double wsum[kFusedDispatchT][32];
+    const int64_t t = threadIdx.x >> 5;
+    if (t < T)
+        select_token<XDT, MAXJ, true>(t, logits, bias, balance, E, k, x, d, thresh_scale, xnorm, chosen, gates64,
+                                      gates32, nullptr, nullptr, w64, wsum[t]);
+    __syncthreads();  // every token's choice is in `chosen`, visible to the whole CTA
+    dispatch_small_body(chosen, T, E, k, da.S, da.bm, da.load, da.offsets, da.groups, da.tile_prefix, da.perm,
+                        da.slot_row, dsm, reinterpret_cast<int32_t *>(dsm + E));
 }
 
 // hashedExperts (mixtureofexperts.go:88-96); gates 1/k (:148-151)
@@ -521,10 +563,22 @@ constexpr int64_t kInlineFixupT = 256;
 
 template <int XDT, int MAXJ>
 static int launch_select(const RouterArgs &a, const double *xnorm, cudaStream_t st) {
+    if constexpr (MAXJ <= kFusedDispatchMaxJ) {
+        if (router_fuses_dispatch(a)) {
+            const unsigned threads = (unsigned)(a.T * 32 < 256 ? 256 : a.T * 32);
+            router_select_dispatch_kernel<XDT, MAXJ><<<1, threads, a.E * (sizeof(int64_t) + sizeof(int32_t)), st>>>(
+                a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d, a.thresh_scale, xnorm, a.chosen, a.gates64,
+                a.gates32, a.w64, *a.dispatch);
+            GT_CUDA(cudaGetLastError());
+            note_launches(1);
+            return 0;
+        }
+    }
     unsigned sel_blocks = (unsigned)((a.T * 32 + 255) / 256);
-    GT_CUDA(cudaMemsetAsync(a.n_fixups, 0, sizeof(int), st));
     // a small batch has few tokens to settle: the select kernel's warps do it
+    // (and the fix-up list, with its counter, is not used)
     const bool inline_fixup = a.T <= kInlineFixupT;
+    if (!inline_fixup) GT_CUDA(cudaMemsetAsync(a.n_fixups, 0, sizeof(int), st));
     if (inline_fixup)
         router_select_kernel<XDT, MAXJ, true><<<sel_blocks, 256, 0, st>>>(
             a.logits, a.bias, a.balance, a.T, a.E, a.k, a.x, a.d, a.thresh_scale, xnorm, a.chosen, a.gates64,
@@ -555,6 +609,11 @@ static int launch_select_e(const RouterArgs &a, const double *xnorm, cudaStream_
     if (a.E <= 256) return launch_select<XDT, 8>(a, xnorm, st);
     if (a.E <= 512) return launch_select<XDT, 16>(a, xnorm, st);
     return launch_select<XDT, 32>(a, xnorm, st);
+}
+
+bool router_fuses_dispatch(const RouterArgs &a) {
+    return a.dispatch && !a.hash && a.T > 0 && a.T <= kFusedDispatchT && a.E <= kFusedDispatchMaxE && a.k < a.E &&
+           a.dispatch->T == a.T && a.dispatch->chosen == a.chosen;
 }
 
 int launch_router(const RouterArgs &a, cudaStream_t st) {

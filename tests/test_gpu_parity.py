@@ -336,8 +336,9 @@ def test_config_sampled(name):
 def test_decode_path_matches_tensor_core_path(prec):
     """The same decode-shaped batch through the weight-streaming kernels and
     through the 256-row tensor-core kernels: identical routing, both within
-    tolerance of the oracle, and the decode path (f16 weights, 11 significant
-    bits) at least as close to it as the tensor-core path (bf16 weights)."""
+    tolerance of the oracle, and the decode path (f16 weights with 11
+    significant bits, or exact codes with the block scales applied in
+    float32) at least as close to it as the tensor-core path (bf16 weights)."""
     spec, x, ids = make_case(T=48, d=256, h=256, n_shared=1, n_routed=12, k=3, precision=prec, seed=23,
                              x_bf16=True, layer_bias=0.1)
     m = gpu_moe(spec)
