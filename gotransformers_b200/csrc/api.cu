@@ -545,6 +545,7 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
         dc.yp = h->yp.p;
         dc.sms = h->tc.sms;
         dc.tile_rows = decode_tile_rows(T);
+        dc.max_tiles = decode_max_tiles(T, E, k, S, dc.tile_rows);
         dc.err = h->tc.err;
         GT_CHECK(h->phase_begin(3));
         GT_CHECK(launch_decode(dc, 1, st));

@@ -26,14 +26,21 @@
 // scales back out.
 //
 // Work unit: (tile of TR = 16 rows of a group, or 8 for batches of at most 8
-// tokens, block of 64 output features = one 64-row half of a weight chunk).  A CTA of eight compute warps and one
-// producer warp runs a unit.  The producer copies the tile's token rows once
-// per unit (one bulk copy per row, all inputs; padded rows: conflict-free
-// fragment loads) and keeps a 2-stage ring of weight steps, one contiguous
-// bulk copy per layer per 128-input step (gate and up for kernel 1; the
-// records of consecutive k-blocks of a 64-row half are adjacent): the TMA
-// engine's rate per CTA grows with the size of each copy, so few large copies
-// replace many small ones.  "full" mbarriers carry the transaction counts,
+// tokens, block of 64 output features = one 64-row half of a weight chunk).
+// A CTA of eight compute warps and one producer warp runs a contiguous range
+// of units, tile-major, so consecutive units share their token tile: the
+// producer copies a tile's token rows once per run (one bulk copy per row,
+// all inputs; padded rows: conflict-free fragment loads), the compute warps
+// convert them once.  The producer keeps a ring of weight steps, one
+// contiguous bulk copy per layer per 128-input step (gate and up for kernel
+// 1; the records of consecutive k-blocks of a 64-row half are adjacent): the
+// TMA engine's rate per CTA grows with the size of each copy, so few large
+// copies replace many small ones.  At a tile change it issues the new unit's
+// first weight steps before it waits for the previous tile to be released,
+// so the ring refills while the last steps of the previous tile are
+// computed.  The ring has 2 stages when the batch has units for every CTA
+// that fits; a few-token batch runs one or two CTAs per SM with the deepest
+// ring that fits.  "full" mbarriers carry the transaction counts,
 // "empty" ones are released by each compute warp; no CTA-wide barrier.  The
 // tokens are the MMA's M side (16 per m-tile) and the weights its N side:
 // warp w owns features 8w..8w+7, so each lane decodes one weight row per
@@ -53,7 +60,15 @@ constexpr int kComputeWarps = 8;                          // 8 features each
 constexpr int kDecodeThreads = (kComputeWarps + 1) * 32;  // + one producer warp
 constexpr int kDecodeFeatures = kHalfRows;               // output features per unit
 constexpr int kDecodeStepKB = 2;                          // 64-input k-blocks per weight step
-constexpr int kDecodeStages = 2;
+constexpr int kDecodeStages = 2;       // ring depth with as many CTAs per SM as fit
+constexpr int kDecodeMaxStages = 12;   // deepest ring (few-unit batches)
+#ifndef GTMOE_DECODE_DEEP_RINGS
+#define GTMOE_DECODE_DEEP_RINGS 1
+#endif
+constexpr bool kDecodeDeepRings = GTMOE_DECODE_DEEP_RINGS;
+constexpr int kDecodeSmemPerSm = 228 * 1024;   // B200 shared memory per SM
+constexpr int kDecodeSmemPerCta = 227 * 1024;  // largest dynamic allocation of one CTA
+constexpr int kDecodeStaticSmem = 512;         // the kernel's barriers, row scales, flag (rounded up)
 
 template <int PREC>
 struct DecodeLayout {
@@ -167,7 +182,7 @@ __device__ __forceinline__ int unit_group(const int *prefix, int n_groups, int t
 __host__ __device__ __forceinline__ int decode_prefix_bytes(int n_groups) { return ((n_groups + 1) * 4 + 15) & ~15; }
 
 template <int PREC, bool GATED, int TR>
-__global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs a, const int stages) {
     static_assert(TR == 8 || TR == 16, "one m16 MMA tile; 8-row tiles leave its rows 8-15 zero");
     using DL = DecodeLayout<PREC>;
     using ST = DecodeStage<PREC, GATED>;
@@ -177,22 +192,23 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     const int K = GATED ? a.d : a.h;
     const int n_out = GATED ? a.h : a.d;
     const int KB = K / 64;
+    const int steps = KB / kDecodeStepKB;  // weight steps per unit
     const int blocks = n_out / kDecodeFeatures;
     const int which = GATED ? 0 : 2;
     const int xpitch = decode_x_pitch(K);
     const __nv_bfloat16 *xin = (const __nv_bfloat16 *)(GATED ? a.xp : a.hp);
     __nv_bfloat16 *out = (__nv_bfloat16 *)(GATED ? a.hp : a.yp);
     uint8_t *xs = dsmem;                                  // TR x xpitch
-    uint8_t *ring = dsmem + TR * xpitch;                  // kDecodeStages x ST::kBytes
-    int *sprefix = (int *)(ring + kDecodeStages * ST::kBytes);  // n_groups + 1 tile counts
+    uint8_t *ring = dsmem + TR * xpitch;                  // stages x ST::kBytes
+    int *sprefix = (int *)(ring + stages * ST::kBytes);   // n_groups + 1 tile counts
 
-    __shared__ uint64_t full[kDecodeStages];   // weight step landed (expect_tx by the producer)
-    __shared__ uint64_t empty[kDecodeStages];  // every compute warp is done with the step
-    __shared__ uint64_t xfull, xempty;         // token rows of the unit landed / released
+    __shared__ uint64_t full[kDecodeMaxStages];   // weight step landed (expect_tx by the producer)
+    __shared__ uint64_t empty[kDecodeMaxStages];  // every compute warp is done with the step
+    __shared__ uint64_t xfull, xempty;            // token rows of a tile landed / released
     __shared__ float rscale[TR];  // 2^-e of each token row (f16 tile = bf16 row * 2^e)
     __shared__ int abort_flag;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kDecodeStages; s++) {
+        for (int s = 0; s < stages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kComputeWarps);
         }
@@ -203,49 +219,76 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
     }
     for (int g = threadIdx.x; g <= a.n_groups; g += blockDim.x) sprefix[g] = (int)__ldg(a.tile_prefix + g);
     __syncthreads();
-    const int64_t units = (int64_t)sprefix[a.n_groups] * blocks;
+    const int units = sprefix[a.n_groups] * blocks;  // at most a few hundred thousand
+    // a contiguous range of units per CTA, tile-major: consecutive units of a
+    // run share their token tile, which is loaded and converted once per run
+    const int per_cta = units / (int)gridDim.x, extra = units % (int)gridDim.x;
+    const int u_begin = (int)blockIdx.x * per_cta + ((int)blockIdx.x < extra ? (int)blockIdx.x : extra);
+    const int u_end = u_begin + per_cta + ((int)blockIdx.x < extra ? 1 : 0);
     volatile int *abort_p = (volatile int *)&abort_flag;
-    uint32_t n = 0;      // weight steps of this CTA so far: slot = n % S, parity = (n / S) & 1
-    uint32_t nu = 0;     // units of this CTA so far (token-row buffer parity)
+    // ring position of the next weight step (the same sequence for the
+    // producer and the compute warps): slot, the parity of its barriers'
+    // current phase, and whether the ring has wrapped once (the producer
+    // then waits for the slot to be released)
+    int slot = 0;
+    uint32_t phase = 0;
+    bool wrapped = false;
+    uint32_t nx = 0;  // token tiles of this CTA so far (xfull / xempty parity)
 
     // Every warp walks all of this CTA's units, also after an abort (its
     // waits then return at once): the compute warps' named barrier is
     // reached by all eight of them, whatever each one saw of the flag.
-    for (int64_t u = blockIdx.x; u < units; u += gridDim.x, nu++) {
-        const int64_t tile = u / blocks;
-        const int fb = (int)(u % blocks);
-        const int gi = unit_group(sprefix, a.n_groups, (int)tile);
+    for (int u = u_begin; u < u_end; u++) {
+        const int tile = u / blocks;
+        const int fb = u - tile * blocks;
+        const bool new_tile = u == u_begin || fb == 0;
+        const bool last_of_tile = u + 1 == u_end || fb == blocks - 1;
+        const int gi = unit_group(sprefix, a.n_groups, tile);
         const Group grp = a.groups[gi];
         const ExpertLayers &L = a.experts[grp.expert];
-        const int64_t r0 = (tile - sprefix[gi]) * TR;  // first row of this tile
+        const int64_t r0 = (int64_t)(tile - sprefix[gi]) * TR;  // first row of this tile
         const int m = grp.m - r0 < TR ? (int)(grp.m - r0) : TR;
 
         if (warp == kComputeWarps) {
-            // ---- producer
+            // ---- producer: the unit's weight steps into the ring and, for a
+            // new tile, its token rows.  The rows wait until the compute
+            // warps release the previous tile, so the first weight steps
+            // (as many as the ring holds) go out before that wait: the ring
+            // refills while the previous unit's last steps are computed.
             const int nt = fb >> 1, half = fb & 1;
             // the 64-row block (2 nt + half) of each layer, its k-block records consecutive
             const uint8_t *w0 = L.tiled[which] + (int64_t)(2 * nt + half) * KB * DL::kHalf;
             const uint8_t *w1 = GATED ? L.tiled[1] + (int64_t)(2 * nt + half) * KB * DL::kHalf : nullptr;
             const uint8_t *xrow0 = (const uint8_t *)(xin + ((GATED ? grp.x_row0 : grp.h_row0) + r0) * (int64_t)K);
-            if (nu > 0 && !*abort_p) mbar_wait(&xempty, (nu - 1) & 1, abort_p, a.err, 13);
-            if (*abort_p) continue;  // no new copies once a wait has given up
-            if (lane == 0) mbar_arrive_expect_tx(&xfull, (uint32_t)m * K * 2);
-            __syncwarp();
-            for (int r = lane; r < m; r += 32) bulk_copy(xs + r * xpitch, xrow0 + (int64_t)r * K * 2, K * 2, &xfull);
-            for (int kb = 0; kb < KB; kb += kDecodeStepKB, n++) {
-                const uint32_t slot = n % kDecodeStages;
-                if (n >= kDecodeStages && !*abort_p)
-                    mbar_wait(&empty[slot], ((n / kDecodeStages) - 1) & 1, abort_p, a.err, 10);
+            const int x_at = !new_tile ? -1 : nx == 0 ? 0 : (steps < stages ? steps : stages);
+            for (int i = 0; i <= steps && !*abort_p; i++) {
+                if (i == x_at) {
+                    if (nx > 0) mbar_wait(&xempty, (nx - 1) & 1, abort_p, a.err, 13);
+                    if (*abort_p) break;  // no new copies once a wait has given up
+                    if (lane == 0) mbar_arrive_expect_tx(&xfull, (uint32_t)m * K * 2);
+                    __syncwarp();
+                    for (int r = lane; r < m; r += 32)
+                        bulk_copy(xs + r * xpitch, xrow0 + (int64_t)r * K * 2, K * 2, &xfull);
+                }
+                if (i == steps) break;
+                if (wrapped) mbar_wait(&empty[slot], phase ^ 1, abort_p, a.err, 10);
                 if (*abort_p) break;
                 if (lane == 0) {
                     uint8_t *st = ring + slot * ST::kBytes;
+                    const int kb = i * kDecodeStepKB;
                     mbar_arrive_expect_tx(&full[slot], ST::kBytes);
                     bulk_copy(st, w0 + (int64_t)kb * DL::kHalf, ST::kLayerBytes, &full[slot]);
                     if (GATED)
                         bulk_copy(st + ST::kLayerBytes, w1 + (int64_t)kb * DL::kHalf, ST::kLayerBytes, &full[slot]);
                 }
                 __syncwarp();
+                if (++slot == stages) {
+                    slot = 0;
+                    phase ^= 1;
+                    wrapped = true;
+                }
             }
+            if (new_tile) nx++;
             continue;
         }
 
@@ -262,41 +305,44 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
         const float *bias1 = GATED ? L.b32[1] : nullptr;
         const float b00 = bias0 ? __ldg(bias0 + f) : 0.f, b01 = bias0 ? __ldg(bias0 + f + 1) : 0.f;
         const float b10 = bias1 ? __ldg(bias1 + f) : 0.f, b11 = bias1 ? __ldg(bias1 + f + 1) : 0.f;
-        if (!*abort_p) mbar_wait(&xfull, nu & 1, abort_p, a.err, 14);
-        // bf16 token rows -> f16 in place, each row scaled by the power of two
-        // that puts its largest magnitude in [2^14, 2^15): exact, no overflow
+        if (new_tile) {
+            if (!*abort_p) mbar_wait(&xfull, nx & 1, abort_p, a.err, 14);
+            // bf16 token rows -> f16 in place, each row scaled by the power of two
+            // that puts its largest magnitude in [2^14, 2^15): exact, no overflow
 #pragma unroll
-        for (int rr = 0; rr < TR / kComputeWarps; rr++) {
-            const int r = warp + kComputeWarps * rr;
-            if (r >= m) continue;
-            uint32_t *p = reinterpret_cast<uint32_t *>(xs + r * xpitch);
-            float mx = 0.f;
-            for (int i = lane; i < K / 2; i += 32) {
-                const uint32_t v = p[i];
-                mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(v << 16)), fabsf(__uint_as_float(v & 0xFFFF0000u))));
-            }
+            for (int rr = 0; rr < TR / kComputeWarps; rr++) {
+                const int r = warp + kComputeWarps * rr;
+                if (r >= m) continue;
+                uint32_t *p = reinterpret_cast<uint32_t *>(xs + r * xpitch);
+                float mx = 0.f;
+                for (int i = lane; i < K / 2; i += 32) {
+                    const uint32_t v = p[i];
+                    mx = fmaxf(mx,
+                               fmaxf(fabsf(__uint_as_float(v << 16)), fabsf(__uint_as_float(v & 0xFFFF0000u))));
+                }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            int e = mx > 0.f ? 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127) : 0;
-            e = e < -100 ? -100 : e > 100 ? 100 : e;
-            const float up = __uint_as_float((uint32_t)(e + 127) << 23);
-            for (int i = lane; i < K / 2; i += 32) {
-                const uint32_t v = p[i];
-                p[i] = pack_f16(__uint_as_float(v << 16) * up, __uint_as_float(v & 0xFFFF0000u) * up);
+                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                int e = mx > 0.f ? 14 - ((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127) : 0;
+                e = e < -100 ? -100 : e > 100 ? 100 : e;
+                const float up = __uint_as_float((uint32_t)(e + 127) << 23);
+                for (int i = lane; i < K / 2; i += 32) {
+                    const uint32_t v = p[i];
+                    p[i] = pack_f16(__uint_as_float(v << 16) * up, __uint_as_float(v & 0xFFFF0000u) * up);
+                }
+                if (lane == 0) rscale[r] = __uint_as_float((uint32_t)(127 - e) << 23);
             }
-            if (lane == 0) rscale[r] = __uint_as_float((uint32_t)(127 - e) << 23);
+            // the producer's next copies into the tile come after these writes
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
+            nx++;
         }
-        // the producer's next copies into the tile come after these writes
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
         const uint8_t *xrow = xs + g8 * xpitch + 8 * q;
         constexpr bool kAfter = decode_scale_after<PREC, TR>();
         const int fcol = warp * 8 + 2 * q;  // this lane's two accumulator features in the half
         const Fp4Tables t1 = fp4_tables_f16(1.f);
-        for (int kb0 = 0; kb0 < KB; kb0 += kDecodeStepKB, n++) {
-            const uint32_t slot = n % kDecodeStages;
-            if (!*abort_p) mbar_wait(&full[slot], (n / kDecodeStages) & 1, abort_p, a.err, 9);
-            if (*abort_p) break;
+        for (int kb0 = 0; kb0 < KB; kb0 += kDecodeStepKB) {
+            if (!*abort_p) mbar_wait(&full[slot], phase, abort_p, a.err, 9);
+            if (*abort_p) break;  // every later wait returns at once: the ring position no longer matters
             const uint8_t *st = ring + slot * ST::kBytes;
 #pragma unroll
             for (int sub = 0; sub < kDecodeStepKB; sub++) {
@@ -343,13 +389,19 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == stages) {
+                slot = 0;
+                phase ^= 1;
+            }
         }
+        // the rows' scales are read before the tile is released: the next
+        // tile's conversion rewrites them
+        const float rs0 = rscale[g8], rs1 = TR > 8 ? rscale[(g8 + 8) % TR] : 0.f;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&xempty);
+        if (last_of_tile && lane == 0) mbar_arrive(&xempty);
 
         // epilogue: acc[l] = tokens (r0 + g8, r0 + g8 + 8) x features (f, f + 1),
         // in units of the rows' scales
-        const float rs0 = rscale[g8], rs1 = TR > 8 ? rscale[(g8 + 8) % TR] : 0.f;
 #pragma unroll
         for (int l = 0; l < 2; l++) {
             acc[l][0] *= rs0;
@@ -381,30 +433,46 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const DecodeArgs
 }
 
 template <int PREC, bool GATED, int TR>
-int decode_smem_bytes(const DecodeArgs &a) {
-    return TR * decode_x_pitch(GATED ? a.d : a.h) + kDecodeStages * DecodeStage<PREC, GATED>::kBytes +
+int decode_smem_bytes(const DecodeArgs &a, int stages) {
+    return TR * decode_x_pitch(GATED ? a.d : a.h) + stages * DecodeStage<PREC, GATED>::kBytes +
            decode_prefix_bytes(a.n_groups);
 }
 
+// Launch shape.  A batch with work units for at least two CTAs per SM runs
+// as many CTAs per SM as fit with a 2-stage ring (compute warps per SM hide
+// the decode -> MMA latency chains).  A batch with fewer units (few tokens:
+// T = 1 makes 154 gate/up units) would leave most CTAs idle and each busy
+// one with two steps in flight, latency-bound; it runs one or two CTAs per
+// SM instead, each with the deepest ring that fits (more bytes in flight per
+// unit).
 template <int PREC, bool GATED, int TR>
 int launch_decode_one(const DecodeArgs &a, cudaStream_t st) {
     auto kern = decode_kernel<PREC, GATED, TR>;
-    const int smem = decode_smem_bytes<PREC, GATED, TR>(a);
+    const int n_out = GATED ? a.h : a.d;
+    const int64_t units_max = a.max_tiles * (n_out / kDecodeFeatures);
+    int stages = kDecodeStages, per_sm = 0;
+    if (kDecodeDeepRings && units_max <= 2 * (int64_t)a.sms) {
+        per_sm = units_max <= a.sms ? 1 : 2;
+        const int budget = (per_sm == 1 ? kDecodeSmemPerCta : kDecodeSmemPerSm / 2 - 1024) - kDecodeStaticSmem;
+        const int room = (budget - decode_smem_bytes<PREC, GATED, TR>(a, 0)) / DecodeStage<PREC, GATED>::kBytes;
+        stages = room < kDecodeStages ? kDecodeStages : room > kDecodeMaxStages ? kDecodeMaxStages : room;
+    }
+    const int smem = decode_smem_bytes<PREC, GATED, TR>(a, stages);
     static int attr = 0;
     if (smem > attr) {
         GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr = smem;
     }
-    // as many CTAs as fit on an SM (shared memory, registers, threads)
-    int per_sm = 0;
-    GT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecodeThreads, smem));
-    per_sm = per_sm < 1 ? 1 : per_sm;
-    kern<<<per_sm * a.sms, kDecodeThreads, smem, st>>>(a);
+    // as many CTAs as fit on an SM (shared memory, registers, threads), at most per_sm when set
+    int fit = 0;
+    GT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, kern, kDecodeThreads, smem));
+    fit = fit < 1 ? 1 : fit;
+    per_sm = per_sm == 0 || per_sm > fit ? fit : per_sm;
+    kern<<<per_sm * a.sms, kDecodeThreads, smem, st>>>(a, stages);
     GT_CUDA(cudaGetLastError());
     note_launches(1);
     return 0;
 }
-
 }  // namespace
 
 bool decode_usable(int precision, int d, int h, int64_t T, int n_groups) {

@@ -125,8 +125,19 @@ struct DecodeArgs {
     void *yp;        // bf16 rows x d
     int sms;
     int tile_rows;  // decode_tile_rows(T): 8 or 16
+    int64_t max_tiles;  // upper bound on the batch's tiles (decode_max_tiles), sizes the launch
     int *err;  // device flag: nonzero when a bounded wait expired
 };
+// Most tiles of tile_rows rows a batch of T tokens can make: S shared groups
+// of T rows, and at most min(E, T k) routed groups of at most T rows each
+// (a token picks an expert once) holding T k rows in all.
+inline int64_t decode_max_tiles(int64_t T, int E, int k, int S, int tile_rows) {
+    const int64_t per_group = (T + tile_rows - 1) / tile_rows;
+    const int64_t routed_groups = (int64_t)E < T * k ? (int64_t)E : T * k;
+    const int64_t by_rows = (T * k + tile_rows - 1) / tile_rows + routed_groups;
+    const int64_t by_groups = routed_groups * per_group;
+    return (int64_t)S * per_group + (by_rows < by_groups ? by_rows : by_groups);
+}
 bool decode_usable(int precision, int d, int h, int64_t T, int n_groups);  // n_groups = shared + routed
 int launch_decode(const DecodeArgs &a, int which, cudaStream_t st);  // which: 1 gate/up, 2 down
 // which: 1 = gate/up + SwiGLU into hp, 2 = down into yp
