@@ -55,9 +55,11 @@ def parse_args():
                    help="expert parallel: hot experts held on every rank ('auto': chosen from the config's expected "
                         "expert popularity, '0': none -- routed experts purely owned by index, or a number: the "
                         "hottest experts chosen the same way, at most that many)")
-    p.add_argument("--op", default="forward", choices=["forward", "block"],
+    p.add_argument("--op", default="forward", choices=["forward", "block", "backward"],
                    help="forward: MixtureOfExperts.Forward (gtmoe_forward); block: the block's feed-forward step "
-                        "x + Forward(RMSNorm(x)) (gtmoe_forward_block, one GPU)")
+                        "x + Forward(RMSNorm(x)) (gtmoe_forward_block, one GPU); backward: a training step's "
+                        "mixture part, Forward then Backward (gtmoe_backward: input and router gradients, "
+                        "frozen compressed experts; float64, one GPU)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     return p.parse_args()
@@ -171,6 +173,25 @@ def time_oracle(spec, x_all, budget_s: float, threads: int, min_tokens: int = 2)
     return n / dt, n, dt
 
 
+def time_oracle_backward(spec, x_all, g_all, budget_s: float, min_tokens: int = 2):
+    """Forward + Backward of the oracle on a seeded token sample sized for
+    ~budget_s seconds; returns (tokens/s, tokens, seconds)."""
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(321)
+    T = x_all.shape[0]
+    probe = np.sort(rng.choice(T, size=min(min_tokens, T), replace=False))
+    t0 = time.perf_counter()
+    O.moe_backward(spec, x_all[probe], g_all[probe])
+    per_tok = max((time.perf_counter() - t0) / len(probe), 1e-6)
+    n = int(min(T, max(min_tokens, budget_s / per_tok)))
+    sample = np.sort(rng.choice(T, size=n, replace=False))
+    t0 = time.perf_counter()
+    O.moe_backward(spec, x_all[sample], g_all[sample])
+    dt = time.perf_counter() - t0
+    return n / dt, n, dt
+
+
 # ------------------------------------------------------------------ main
 
 def main():
@@ -234,12 +255,27 @@ def main():
         # the block's FeedForwardNorm: seeded RMSNorm weights around 1
         moe.set_norm(1.0 + 0.1 * synthetic.normal(cfg.weight_seed, synthetic.STREAM_NORM, cfg.d), 1e-6)
         out = torch.empty_like(x)  # the block's output has the input's dtype (x is the residual)
+    grads = None
+    if args.op == "backward":
+        if world > 1:
+            raise SystemExit("--op backward runs on one GPU")
+        moe.set_training(True)
+        # seeded N(0,1) output gradients; the input gradients in float32;
+        # the router's gradients accumulate into float64 storage
+        gen = torch.Generator(device=dev).manual_seed(cfg.act_seed + 17)
+        dout = torch.randn((T_local, cfg.d), generator=gen, device=dev, dtype=torch.float32)
+        grads = {"dout": dout, "dx": torch.empty_like(dout),
+                 "gw": torch.zeros((cfg.n_routed, cfg.d), dtype=torch.float64, device=dev),
+                 "gb": torch.zeros((cfg.n_routed,), dtype=torch.float64, device=dev)}
 
-    def step(xx, oo):
+    def step(xx, oo, g=None):
         if args.op == "block":
             moe.forward_block(xx, out=oo, want_routing=False)
         else:
             moe.forward(xx, out=oo, want_routing=False)
+        if args.op == "backward":
+            g = g or grads
+            moe.backward(g["dout"], input_gradients=g["dx"], router_weight_grad=g["gw"], router_bias_grad=g["gb"])
     # a dedicated stream: torch's default (legacy) stream has handle 0, which
     # the C ABI reads as "the handle's own stream"
     stream = torch.cuda.Stream(dev)
@@ -306,12 +342,29 @@ def main():
     _lib.check(L.gtmoe_read_timing(moe.handle, phase_ms, _lib.N_PHASES, ctypes.byref(calls), ctypes.byref(plaunch)))
     _lib.check(L.gtmoe_set_timing(moe.handle, 0))
     phases = {n: phase_ms[i] / max(calls.value, 1) for i, n in enumerate(_lib.PHASES)}
+    bwd_ms = None
+    if grads is not None:
+        # the backward alone: events around gtmoe_backward after each forward
+        bev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(min(args.steps, 5))]
+        for a_ev, b_ev in bev:
+            moe.forward(x, out=out, want_routing=False)
+            a_ev.record(stream)
+            moe.backward(grads["dout"], input_gradients=grads["dx"], router_weight_grad=grads["gw"],
+                         router_bias_grad=grads["gb"])
+            b_ev.record(stream)
+        bev[-1][1].synchronize()
+        bwd_ms = sum(a_ev.elapsed_time(b_ev) for a_ev, b_ev in bev) / len(bev)
 
     # end to end through the C ABI with pinned host buffers
     x_host = x.cpu().pin_memory()
     out_host = torch.empty((T_local, cfg.d), dtype=out.dtype).pin_memory()
+    g_host = None
+    if grads is not None:
+        g_host = {"dout": grads["dout"].cpu().pin_memory(), "dx": grads["dx"].cpu().pin_memory(),
+                  "gw": grads["gw"], "gb": grads["gb"]}
     for _ in range(2):
-        step(x_host, out_host)
+        step(x_host, out_host, g_host)
     barrier()
     e2e_steps = max(3, args.steps // 2)
     eevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -320,12 +373,12 @@ def main():
         for i in range(e2e_steps):
             flush_buf.fill_(i)
             eevs[i][0].record(stream)
-            step(x_host, out_host)
+            step(x_host, out_host, g_host)
             eevs[i][1].record(stream)
     else:
         eevs[0][0].record(stream)
         for _ in range(e2e_steps):
-            step(x_host, out_host)
+            step(x_host, out_host, g_host)
         eevs[0][1].record(stream)
     eevs[-1][1].synchronize()
     barrier()
@@ -399,8 +452,32 @@ def main():
                     "algorithmic_bytes_per_launch": int(kernel_bytes(cfg, kname, rows, cfg.n_shared + cfg.n_routed)),
                     "traffic_source": traffic_ent}
 
+    if bwd_ms is not None:
+        # float64 work of the backward per work row (bwd_rows_kernel): the gate
+        # and up pre-activations recomputed (2 d h multiply-adds), the routed
+        # row's output (d h), dH = dY Wd (d h), dX = dG Wg + dU Wu (2 d h):
+        # 12 d h FLOPs per routed row, 10 d h per shared row; the router term
+        # (2 T d E for the logits, T E d for its gradients) is added
+        bflops = (12.0 * cfg.k + 10.0 * cfg.n_shared) * T_local * cfg.d * cfg.h + 4.0 * T_local * cfg.d * cfg.n_routed
+        roofline = {"kernel": "backward (gtmoe_backward: bwd_rows_kernel + router terms)", "bound": "fp64",
+                    "achieved": round(bflops / (bwd_ms * 1e-3) / 1e12, 4), "unit": "TFLOP/s", "peak": None,
+                    "frac": None, "traffic": None, "avg_ms": round(bwd_ms, 4),
+                    "algorithmic_flops_per_launch": bflops,
+                    "note": "float64 SIMT, built for exactness (the reference's float64 order), not tuned; no "
+                            "measured FP64 peak on this pool, so no fraction is given",
+                    "forward_roofline": roofline}
+
     cpu_baseline = None
-    if want_cpu:
+    if want_cpu and grads is not None:
+        # the oracle's numpy restatement of Forward + Backward on a seeded token sample
+        spec = oracle_spec(cfg, host)
+        x_cpu = x.to(torch.float64).cpu().numpy()
+        g_cpu = grads["dout"].to(torch.float64).cpu().numpy()
+        v, n, dt = time_oracle_backward(spec, x_cpu, g_cpu, args.cpu_seconds)
+        cpu_baseline = {"value": round(v, 3), "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                        "sample": f"{n} seeded tokens of {cfg.name} ({dt:.1f} s), float64 numpy restatement of "
+                                  f"the reference's Forward + Backward (oracle.moe_backward; BLAS threads)"}
+    elif want_cpu:
         spec = oracle_spec(cfg, host)
         x_cpu = x.to(torch.float64).cpu().numpy()
         threads = os.cpu_count() or 1
@@ -421,7 +498,10 @@ def main():
                     "quantiser, Zipf router bias)",
             "config": {**workload_config(cfg, world, mode, getattr(moe, "replicas", [])),
                        **({"op": "block step: x + Forward(RMSNorm(x)), gtmoe_forward_block"} if args.op == "block"
-                          else {})},
+                          else {}),
+                       **({"op": "training step of the mixture: Forward then Backward (gtmoe_backward, float64 "
+                                 "input and router gradients, frozen compressed experts)"}
+                          if args.op == "backward" else {})},
             "e2e": {"value": round(T_total / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()),
                     "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size())},

@@ -440,34 +440,48 @@ int decode_smem_bytes(const DecodeArgs &a, int stages) {
 
 // Launch shape.  A batch with work units for at least two CTAs per SM runs
 // as many CTAs per SM as fit with a 2-stage ring (compute warps per SM hide
-// the decode -> MMA latency chains).  A batch with fewer units (few tokens:
-// T = 1 makes 154 gate/up units) would leave most CTAs idle and each busy
-// one with two steps in flight, latency-bound; it runs one or two CTAs per
-// SM instead, each with the deepest ring that fits (more bytes in flight per
-// unit).
+// the decode -> MMA latency chains), each with the deepest ring that still
+// lets that many fit (c4 T = 8 down kernel: 4 CTAs with 3 stages, 37.5 ->
+// 35.9 us).  A batch with fewer units (few tokens: T = 1 makes 154 gate/up
+// units) would leave most CTAs idle; it runs one or two CTAs per SM, each
+// with the deepest ring that fits.
+template <int PREC, bool GATED, int TR>
+int decode_ring_for(const DecodeArgs &a, int per_sm) {
+    const int budget = (per_sm == 1 ? kDecodeSmemPerCta : kDecodeSmemPerSm / per_sm - 1024) - kDecodeStaticSmem;
+    const int room = (budget - decode_smem_bytes<PREC, GATED, TR>(a, 0)) / DecodeStage<PREC, GATED>::kBytes;
+    return room < kDecodeStages ? kDecodeStages : room > kDecodeMaxStages ? kDecodeMaxStages : room;
+}
+
 template <int PREC, bool GATED, int TR>
 int launch_decode_one(const DecodeArgs &a, cudaStream_t st) {
     auto kern = decode_kernel<PREC, GATED, TR>;
     const int n_out = GATED ? a.h : a.d;
     const int64_t units_max = a.max_tiles * (n_out / kDecodeFeatures);
-    int stages = kDecodeStages, per_sm = 0;
+    static int attr = 0;
+    auto set_attr = [&](int bytes) -> int {
+        if (bytes > attr) {
+            GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+            attr = bytes;
+        }
+        return 0;
+    };
+    int per_sm = 0;
     if (kDecodeDeepRings && units_max <= 2 * (int64_t)a.sms) {
         per_sm = units_max <= a.sms ? 1 : 2;
-        const int budget = (per_sm == 1 ? kDecodeSmemPerCta : kDecodeSmemPerSm / 2 - 1024) - kDecodeStaticSmem;
-        const int room = (budget - decode_smem_bytes<PREC, GATED, TR>(a, 0)) / DecodeStage<PREC, GATED>::kBytes;
-        stages = room < kDecodeStages ? kDecodeStages : room > kDecodeMaxStages ? kDecodeMaxStages : room;
+    } else {
+        const int smem2 = decode_smem_bytes<PREC, GATED, TR>(a, kDecodeStages);
+        GT_CHECK(set_attr(smem2));
+        GT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecodeThreads, smem2));
+        per_sm = per_sm < 1 ? 1 : per_sm;
     }
+    const int stages = decode_ring_for<PREC, GATED, TR>(a, per_sm);
     const int smem = decode_smem_bytes<PREC, GATED, TR>(a, stages);
-    static int attr = 0;
-    if (smem > attr) {
-        GT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr = smem;
-    }
-    // as many CTAs as fit on an SM (shared memory, registers, threads), at most per_sm when set
+    GT_CHECK(set_attr(smem));
+    // at most per_sm CTAs per SM, as many as fit with this ring
     int fit = 0;
     GT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, kern, kDecodeThreads, smem));
     fit = fit < 1 ? 1 : fit;
-    per_sm = per_sm == 0 || per_sm > fit ? fit : per_sm;
+    per_sm = per_sm > fit ? fit : per_sm;
     kern<<<per_sm * a.sms, kDecodeThreads, smem, st>>>(a, stages);
     GT_CUDA(cudaGetLastError());
     note_launches(1);
