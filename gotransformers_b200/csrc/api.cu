@@ -395,7 +395,8 @@ static std::vector<uint64_t> graph_key(gtmoe_handle *h, const void *x, int x_dty
     std::vector<uint64_t> k = {(uint64_t)(uintptr_t)x, (uint64_t)x_dtype, (uint64_t)T, (uint64_t)(uintptr_t)res,
                                (uint64_t)(uintptr_t)out, (uint64_t)out_dtype, (uint64_t)(uintptr_t)h->stream, wbits,
                                (uint64_t)h->e_pad, (uint64_t)use_tc, (uint64_t)use_decode,
-                               (uint64_t)(uintptr_t)h->tc.err, (uint64_t)(uintptr_t)h->gather_bf16};
+                               (uint64_t)(uintptr_t)h->tc.err, (uint64_t)(uintptr_t)h->gather_bf16,
+                               (uint64_t)(uintptr_t)h->router_bf16_mid, (uint64_t)(uintptr_t)h->router_bf16_lo};
     const gtmoe::DevBuf *bufs[] = {&h->wr64,   &h->wr32,   &h->br,     &h->bal,    &h->wr3,   &h->table,
                                    &h->logits, &h->chosen, &h->gates64, &h->gates32, &h->counts, &h->load,
                                    &h->offsets, &h->perm,  &h->slot_row, &h->groups, &h->tile_prefix, &h->xp,
@@ -485,7 +486,20 @@ int forward_device(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t T, c
     ra.bias = h->br.as<double>();
     ra.balance = h->bal.as<double>();
     ra.use_tc = !c.hash_routing && h->wr3.p && !h->no_tc && router_tc_usable(x_dev, x_dtype, T, d);
-    ra.thresh_scale = (ra.use_tc ? kRouterTcErr : kRouterSimtErr) * h->wmax;
+    double router_err = ra.use_tc ? kRouterTcErr : kRouterSimtErr;
+    // float64 rows that come with their three-term bf16 split (the block
+    // step): logits on the tensor cores from the terms, with the split's margin
+    if (!ra.use_tc && !c.hash_routing && h->wr3.p && !h->no_tc && x_dtype == GTMOE_DTYPE_F64 && h->gather_bf16 &&
+        h->router_bf16_mid && h->router_bf16_lo && router_tc_usable(h->gather_bf16, GTMOE_DTYPE_BF16, T, d) &&
+        router_tc_usable(h->router_bf16_mid, GTMOE_DTYPE_BF16, T, d) &&
+        router_tc_usable(h->router_bf16_lo, GTMOE_DTYPE_BF16, T, d)) {
+        ra.use_tc = 1;
+        ra.x_tc = h->gather_bf16;
+        ra.x_tc_mid = h->router_bf16_mid;
+        ra.x_tc_lo = h->router_bf16_lo;
+        router_err = kRouterTc3Err;
+    }
+    ra.thresh_scale = router_err * h->wmax;
     ra.w3 = h->wr3.p;
     ra.e_pad = h->e_pad;
     ra.err = h->tc.err;

@@ -20,7 +20,9 @@ namespace {
 // lane writes its share of the normalized row.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const void *__restrict__ x, int x_dtype, int64_t T, int d,
                                                       const double *__restrict__ w, double eps,
-                                                      double *__restrict__ y, __nv_bfloat16 *__restrict__ y16) {
+                                                      double *__restrict__ y, __nv_bfloat16 *__restrict__ y16,
+                                                      __nv_bfloat16 *__restrict__ y16mid,
+                                                      __nv_bfloat16 *__restrict__ y16lo) {
     __shared__ double buf[8][32];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t warps = (int64_t)gridDim.x * 8;
@@ -44,7 +46,13 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const void *__restrict__ x
         for (int i = lane; i < d; i += 32) {
             const double v = __dmul_rn(__ddiv_rn(load_as_double(x, x_dtype, x0 + i), rms), w[i]);
             y[x0 + i] = v;
-            y16[x0 + i] = __double2bfloat16(v);  // what the gather would make of v
+            const __nv_bfloat16 hi = __double2bfloat16(v);  // what the gather would make of v
+            y16[x0 + i] = hi;
+            // the router's second and third terms (v - hi - mid - lo within 2^-24 |v|)
+            const double r1 = v - (double)__bfloat162float(hi);
+            const __nv_bfloat16 mid = __double2bfloat16(r1);
+            y16mid[x0 + i] = mid;
+            y16lo[x0 + i] = __double2bfloat16(r1 - (double)__bfloat162float(mid));
         }
     }
 }
@@ -96,18 +104,25 @@ int gtmoe_forward_block(gtmoe_t h, const void *x, int x_dtype, int64_t T, const 
         }
         GT_CHECK(h->block_xn.ensure(sizeof(double) * (size_t)T * d));
         GT_CHECK(h->block_xn16.ensure(sizeof(__nv_bfloat16) * (size_t)T * d));
+        GT_CHECK(h->block_xn16mid.ensure(sizeof(__nv_bfloat16) * (size_t)T * d));
+        GT_CHECK(h->block_xn16lo.ensure(sizeof(__nv_bfloat16) * (size_t)T * d));
         const int64_t blocks = (T + 7) / 8;
         rmsnorm_kernel<<<(unsigned)(blocks < 65535 ? blocks : 65535), 256, 0, h->stream>>>(
             xd, x_dtype, T, d, h->norm_w.as<double>(), h->norm_eps, h->block_xn.as<double>(),
-            h->block_xn16.as<__nv_bfloat16>());
+            h->block_xn16.as<__nv_bfloat16>(), h->block_xn16mid.as<__nv_bfloat16>(),
+            h->block_xn16lo.as<__nv_bfloat16>());
         GT_CUDA(cudaGetLastError());
         note_launches(1);
         // the mixture on the normalized rows (device, float64; the experts'
         // bf16 rows gathered from their bf16 rounding), the input as the residual
         h->gather_bf16 = h->block_xn16.p;
+        h->router_bf16_mid = h->block_xn16mid.p;
+        h->router_bf16_lo = h->block_xn16lo.p;
         const int rc = forward_locked(h, h->block_xn.p, GTMOE_DTYPE_F64, T, token_ids, xd, out, out_dtype, chosen,
                                       gates, perm, load);
         h->gather_bf16 = nullptr;
+        h->router_bf16_mid = nullptr;
+        h->router_bf16_lo = nullptr;
         return rc;
     }
 }

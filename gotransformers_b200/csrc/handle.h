@@ -108,11 +108,15 @@ struct gtmoe_handle {
 
     // the block's RMSNorm (block.cu): weights (d, float64), epsilon, and the
     // input / normalized rows of gtmoe_forward_block
-    DevBuf norm_w, block_x, block_xn, block_xn16;
+    DevBuf norm_w, block_x, block_xn, block_xn16, block_xn16mid, block_xn16lo;
     // set by gtmoe_forward_block for its inner Forward: the bf16 rounding of
     // the normalized rows, which the gather copies instead of converting the
     // float64 rows (the same bits: both round the same double once)
     const void *gather_bf16 = nullptr;
+    // ... and the second and third bf16 terms of those rows, with which the
+    // router computes their logits on the tensor cores (router_tc.cu)
+    const void *router_bf16_mid = nullptr;
+    const void *router_bf16_lo = nullptr;
     double norm_eps = 0;
     int norm_set = 0;
 

@@ -31,6 +31,9 @@ struct RouterArgs {
     const double *balance;      // E
     double thresh_scale;        // score margin per unit ||x_t||: 2 * 0.5 * (logit error bound) / ||x_t||
     int use_tc;                 // logits on the tensor cores (router_tc.cu)
+    const void *x_tc = nullptr;      // their bf16 rows when x is not bf16: x_hi of a float64 split ...
+    const void *x_tc_mid = nullptr;  // ... x_mid ...
+    const void *x_tc_lo = nullptr;   // ... and x_lo (router_tc.cu)
     const void *w3;             // 3 x E_pad x d bf16 split of w64 (tensor-core path)
     int e_pad;
     int *err;                   // error flag: a bounded wait's code, or kErrNegativeTokenId
@@ -56,11 +59,14 @@ bool router_fuses_dispatch(const RouterArgs &a);
 // Error code the hash router records for a negative device token ID.
 constexpr int kErrNegativeTokenId = 100;
 bool router_tc_usable(const void *x, int x_dtype, int64_t T, int d);
-int launch_router_logits_tc(const void *x, int64_t T, int d, int E, int E_pad, const void *w3, double *logits,
-                            int *err, int sms, cudaStream_t st);
-// Logit error bounds (relative to ||x_t|| * max_e ||w_e||) of the two paths.
+// x_mid, x_lo: NULL for bf16 rows x, else the second and third bf16 terms of
+// split float64 rows (x = x + x_mid + x_lo to 2^-24)
+int launch_router_logits_tc(const void *x, const void *x_mid, const void *x_lo, int64_t T, int d, int E, int E_pad,
+                            const void *w3, double *logits, int *err, int sms, cudaStream_t st);
+// Logit error bounds (relative to ||x_t|| * max_e ||w_e||) of the paths.
 constexpr double kRouterSimtErr = 32.0 / 16777216.0;  // 32 * 2^-24
 constexpr double kRouterTcErr = 70.0 / 8388608.0;     // 70 * 2^-23
+constexpr double kRouterTc3Err = 136.0 / 8388608.0;   // 136 * 2^-23: float64 rows as three bf16 terms
 
 // Dispatch: builds the token-ascending permutation of (token, slot) pairs by
 // expert (rowsForExpert, mixtureofexperts.go:175-180) and the group table.

@@ -627,7 +627,8 @@ int launch_router(const RouterArgs &a, cudaStream_t st) {
     }
     const double *xnorm = nullptr;  // ||x_t|| per token, when the logits kernel left it
     if (a.use_tc) {
-        GT_CHECK(launch_router_logits_tc(a.x, a.T, a.d, a.E, a.e_pad, a.w3, a.logits, a.err, a.sms, st));
+        GT_CHECK(launch_router_logits_tc(a.x_tc ? a.x_tc : a.x, a.x_tc_mid, a.x_tc_lo, a.T, a.d, a.E, a.e_pad, a.w3,
+                                         a.logits, a.err, a.sms, st));
     } else if (a.T <= kRouterSmallMaxT) {
         dim3 grid((unsigned)((a.E + kRouterSmallWarps - 1) / kRouterSmallWarps), (unsigned)a.T);
         if (a.x_dtype == GTMOE_DTYPE_F64)

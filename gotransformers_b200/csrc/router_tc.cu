@@ -13,6 +13,14 @@
 // which is the margin the selection kernel uses to decide when to recompute a
 // token's logits in float64 (router.cu).
 //
+// Float64 rows (the block step's RMSNorm output) are split once into three
+// bf16 terms, x = x_hi + x_mid + x_lo + r with |r| <= 2^-24 |x|, and the MMAs
+// add x_hi w_t (t = hi, mid, lo), x_mid w_t (t = hi, mid) and x_lo w_hi: the
+// dropped r w, x_mid w_lo, x_lo w_mid and the weight residual (2^-24 each) and
+// twice the accumulation allowance give 136 * 2^-23 * ||x_t|| * max_e ||w_e||
+// (kRouterTc3Err); tokens inside that margin are settled in float64 as
+// before.
+//
 // Persistent kernel, one CTA per SM: warp 0 TMA producer (x tile + the three
 // weight tiles), warp 1 TMEM allocator + MMA issuer, warps 2-9 epilogue
 // (4 TMEM lane quadrants x 2 column halves).  Tile 128 tokens x 128 experts,
@@ -25,17 +33,25 @@ namespace gtmoe {
 
 namespace {
 
-constexpr int kRStages = 3;
 constexpr int kRBM = 128;
 constexpr int kRBN = 128;
 constexpr int kRBK = 64;
-constexpr int kRATile = kRBM * kRBK * 2;      // 16 KB
+constexpr int kRATile = kRBM * kRBK * 2;      // 16 KB per activation term
 constexpr int kRBSub = kRBN * kRBK * 2;       // 16 KB per weight term
 constexpr int kRBTile = 3 * kRBSub;           // 48 KB
 constexpr int kREpiWarps = 8;
 constexpr int kRThreads = (2 + kREpiWarps) * 32;
 constexpr int kRTmemCols = 256;
-constexpr int kRSmem = kRStages * (kRATile + kRBTile) + 1024 + 256;
+// NX activation terms per row: 1 (bf16 rows, exact) or 3 (float64 rows split
+// into three bf16 terms: the block step's normalized rows).  Ring depth as
+// shared memory allows.
+template <int NX>
+struct RouterTcShape {
+    static constexpr int kStages = NX == 1 ? 3 : 2;
+    static constexpr int kATile = NX * kRATile;
+    static constexpr int kSmem = kStages * (kATile + kRBTile) + 1024 + 256;
+};
+static_assert(RouterTcShape<3>::kSmem <= 232448, "shared memory per CTA");
 constexpr uint32_t kRIdesc =
     (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kRBN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
@@ -46,14 +62,18 @@ struct RouterTcArgs {
     int *err;
 };
 
+template <int NX>
 __global__ void __launch_bounds__(kRThreads, 1)
-    router_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+    router_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmmap,
+                     const __grid_constant__ CUtensorMap xlmap, const __grid_constant__ CUtensorMap wmap,
                      const RouterTcArgs a) {
+    using SH = RouterTcShape<NX>;
+    constexpr int kRStages = SH::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *a_tiles = smem;
-    uint8_t *b_tiles = smem + kRStages * kRATile;
-    uint64_t *bars = (uint64_t *)(smem + kRStages * (kRATile + kRBTile));
+    uint8_t *a_tiles = smem;  // per stage: the x_hi tile (then x_mid, x_lo when NX = 3)
+    uint8_t *b_tiles = smem + kRStages * SH::kATile;
+    uint64_t *bars = (uint64_t *)(smem + kRStages * (SH::kATile + kRBTile));
     uint64_t *full = bars;
     uint64_t *empty = bars + kRStages;
     uint64_t *tfull = bars + 2 * kRStages;
@@ -92,6 +112,10 @@ __global__ void __launch_bounds__(kRThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&xmap) : "memory");
+            if (NX == 3) {
+                asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&xmmap) : "memory");
+                asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&xlmap) : "memory");
+            }
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&wmap) : "memory");
             int stage = 0;
             uint32_t phase = 0;
@@ -99,8 +123,14 @@ __global__ void __launch_bounds__(kRThreads, 1)
                 const int mt = (int)(u / n_nt), nt = (int)(u % n_nt);
                 for (int kb = 0; kb < KB; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err, 11)) break;
-                    mbar_arrive_expect_tx(&full[stage], kRATile + kRBTile);
-                    tma_load_2d(a_tiles + stage * kRATile, &xmap, kb * kRBK, mt * kRBM, &full[stage]);
+                    mbar_arrive_expect_tx(&full[stage], SH::kATile + kRBTile);
+                    tma_load_2d(a_tiles + stage * SH::kATile, &xmap, kb * kRBK, mt * kRBM, &full[stage]);
+                    if (NX == 3) {
+                        tma_load_2d(a_tiles + stage * SH::kATile + kRATile, &xmmap, kb * kRBK, mt * kRBM,
+                                    &full[stage]);
+                        tma_load_2d(a_tiles + stage * SH::kATile + 2 * kRATile, &xlmap, kb * kRBK, mt * kRBM,
+                                    &full[stage]);
+                    }
                     uint8_t *bt = b_tiles + stage * kRBTile;
 #pragma unroll
                     for (int t = 0; t < 3; t++)
@@ -132,16 +162,20 @@ __global__ void __launch_bounds__(kRThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t adesc = sw128_desc(smem_u32(a_tiles + stage * kRATile));
+                    const uint64_t adesc = sw128_desc(smem_u32(a_tiles + stage * SH::kATile));
                     const uint64_t bdesc = sw128_desc(smem_u32(b_tiles + stage * kRBTile));
                     const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kRBN);
+                    // x_hi against the three weight terms; for split rows also
+                    // x_mid against w_hi and w_mid, x_lo against w_hi
 #pragma unroll
                     for (int k = 0; k < kRBK / 16; k++)
 #pragma unroll
-                        for (int t = 0; t < 3; t++)
-                            umma_bf16(d_tmem, adesc + (uint64_t)(2 * k),
-                                      bdesc + (uint64_t)((t * kRBSub) >> 4) + (uint64_t)(2 * k), kRIdesc,
-                                      (k | t) != 0);
+                        for (int xi = 0; xi < NX; xi++)
+#pragma unroll
+                            for (int t = 0; t < 3 - xi; t++)
+                                umma_bf16(d_tmem, adesc + (uint64_t)((xi * kRATile) >> 4) + (uint64_t)(2 * k),
+                                          bdesc + (uint64_t)((t * kRBSub) >> 4) + (uint64_t)(2 * k), kRIdesc,
+                                          (k | t | xi) != 0);
                     umma_commit(&empty[stage]);
                     umma_commit(&tfull[acc]);
                     if (++stage == kRStages) {
@@ -209,10 +243,13 @@ bool router_tc_usable(const void *x, int x_dtype, int64_t T, int d) {
     return true;
 }
 
-int launch_router_logits_tc(const void *x, int64_t T, int d, int E, int E_pad, const void *w3, double *logits,
-                            int *err, int sms, cudaStream_t st) {
-    CUtensorMap xmap, wmap;
+int launch_router_logits_tc(const void *x, const void *x_mid, const void *x_lo, int64_t T, int d, int E, int E_pad,
+                            const void *w3, double *logits, int *err, int sms, cudaStream_t st) {
+    CUtensorMap xmap, xmmap, xlmap, wmap;
+    const bool split = x_mid && x_lo;
     GT_CHECK(encode_bf16_2d(&xmap, x, d, T, kRBK, kRBM));
+    GT_CHECK(encode_bf16_2d(&xmmap, split ? x_mid : x, d, T, kRBK, kRBM));
+    GT_CHECK(encode_bf16_2d(&xlmap, split ? x_lo : x, d, T, kRBK, kRBM));
     GT_CHECK(encode_bf16_2d(&wmap, w3, d, (int64_t)3 * E_pad, kRBK, kRBN));
     RouterTcArgs a;
     a.T = T;
@@ -223,12 +260,18 @@ int launch_router_logits_tc(const void *x, int64_t T, int d, int E, int E_pad, c
     a.err = err;
     static bool attr_set = false;
     if (!attr_set) {
-        GT_CUDA(cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRSmem));
+        GT_CUDA(cudaFuncSetAttribute(router_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     RouterTcShape<1>::kSmem));
+        GT_CUDA(cudaFuncSetAttribute(router_tc_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     RouterTcShape<3>::kSmem));
         attr_set = true;
     }
     const int64_t tiles = ((T + kRBM - 1) / kRBM) * (E_pad / kRBN);
     const int grid = (int)(tiles < sms ? tiles : sms);
-    router_tc_kernel<<<grid, kRThreads, kRSmem, st>>>(xmap, wmap, a);
+    if (split)
+        router_tc_kernel<3><<<grid, kRThreads, RouterTcShape<3>::kSmem, st>>>(xmap, xmmap, xlmap, wmap, a);
+    else
+        router_tc_kernel<1><<<grid, kRThreads, RouterTcShape<1>::kSmem, st>>>(xmap, xmmap, xlmap, wmap, a);
     GT_CUDA(cudaGetLastError());
     note_launches(1);
     return 0;
