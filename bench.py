@@ -453,18 +453,19 @@ def main():
                     "traffic_source": traffic_ent}
 
     if bwd_ms is not None:
-        # float64 work of the backward per work row (bwd_rows_kernel): the gate
-        # and up pre-activations recomputed (2 d h multiply-adds), the routed
-        # row's output (d h), dH = dY Wd (d h), dX = dG Wg + dU Wu (2 d h):
-        # 12 d h FLOPs per routed row, 10 d h per shared row; the router term
-        # (2 T d E for the logits, T E d for its gradients) is added
+        # float64 work of the backward per work row (the grouped GEMM stages):
+        # the gate and up pre-activations recomputed (2 d h multiply-adds), the
+        # routed row's output (d h), dH = dY Wd (d h), dX = dG Wg + dU Wu
+        # (2 d h): 12 d h FLOPs per routed row, 10 d h per shared row; the
+        # router term (2 T d E for the logits, T E d for its gradients) is added
         bflops = (12.0 * cfg.k + 10.0 * cfg.n_shared) * T_local * cfg.d * cfg.h + 4.0 * T_local * cfg.d * cfg.n_routed
-        roofline = {"kernel": "backward (gtmoe_backward: bwd_rows_kernel + router terms)", "bound": "fp64",
+        roofline = {"kernel": "backward (gtmoe_backward: bwd_gemm_kernel stages + router terms)", "bound": "fp64",
                     "achieved": round(bflops / (bwd_ms * 1e-3) / 1e12, 4), "unit": "TFLOP/s", "peak": None,
                     "frac": None, "traffic": None, "avg_ms": round(bwd_ms, 4),
                     "algorithmic_flops_per_launch": bflops,
-                    "note": "float64 SIMT, built for exactness (the reference's float64 order), not tuned; no "
-                            "measured FP64 peak on this pool, so no fraction is given",
+                    "note": "float64 SIMT tiles (64 rows of one expert x 64 outputs), within summation rounding "
+                            "of the reference's float64 arithmetic; no measured FP64 peak on this pool, so no "
+                            "fraction is given",
                     "forward_roofline": roofline}
 
     cpu_baseline = None

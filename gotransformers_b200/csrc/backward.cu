@@ -27,61 +27,17 @@
 //   zeros skipped); dx = expert input gradients + router input gradients.
 //
 // The gate/up pre-activations, hidden values and expert outputs the reference
-// keeps from Forward are recomputed here from the saved float64 input rows
-// with the layers' DotRow (rows.go:207-257: per 16-value block a partial sum
-// of x * code, times float64(scale)).  Sums run in the reference's order.
+// keeps from Forward are recomputed here from the saved float64 input rows.
 // Work rows: r < S*T are (shared expert r / T, token r % T); after them
-// (token t, slot i) for t*k + i, one CTA each.
+// (token t, slot i) for t*k + i.  The experts' part runs as four grouped
+// float64 GEMM stages over tiles of one expert's rows (bwd_gemm_kernel), each
+// output one float64 sum over its inputs in ascending order: the reference's
+// values up to summation rounding (per-16-value partial sums times the scale,
+// rows.go:207-257, and zero gradients skipped there, not here).
 #include "handle.h"
 
 namespace gtmoe {
 namespace {
-
-constexpr int kBwdThreads = 256;
-
-// Rows.DotRow of one layer row against float64 inputs (shared memory).
-__device__ double dot_row_f64(const void *w, const float *s, int prec, int width, int row, const double *x) {
-    const int64_t base = (int64_t)row * width;
-    double total = 0;
-    if (prec == GTMOE_FLOAT64) {
-        const double *v = (const double *)w + base;
-        for (int i = 0; i < width; i++) total += x[i] * v[i];
-    } else if (prec == GTMOE_FLOAT32) {
-        const float *v = (const float *)w + base;
-        for (int i = 0; i < width; i++) total += x[i] * (double)v[i];
-    } else {
-        const int nb = scale_blocks(width);
-        for (int b = 0; b < nb; b++) {
-            const int i1 = min(width, (b + 1) * kValuesPerScale);
-            double partial = 0;
-            if (prec == GTMOE_INT8) {
-                const int8_t *q = (const int8_t *)w + base;
-                for (int i = b * kValuesPerScale; i < i1; i++) partial += x[i] * (double)q[i];
-            } else {
-                const uint8_t *p = (const uint8_t *)w + (int64_t)row * fp4_row_bytes(width);
-                for (int i = b * kValuesPerScale; i < i1; i++) {
-                    const uint8_t byte = p[i / 2];
-                    const uint32_t code = (i & 1) ? (byte >> 4) : (byte & 15u);
-                    partial += x[i] * (double)fp4_value(code);
-                }
-            }
-            total += partial * (double)s[(int64_t)row * nb + b];
-        }
-    }
-    return total;
-}
-
-// One term of Rows.AddScaledRowTo(row, g, target)[col].
-__device__ __forceinline__ double scaled_weight(const void *w, const float *s, int prec, int width, int row, int col,
-                                                double g) {
-    if (prec == GTMOE_FLOAT64) return g * ((const double *)w)[(int64_t)row * width + col];
-    if (prec == GTMOE_FLOAT32) return g * (double)((const float *)w)[(int64_t)row * width + col];
-    const double sc = (double)s[(int64_t)row * scale_blocks(width) + col / kValuesPerScale];
-    if (prec == GTMOE_INT8) return (g * sc) * (double)((const int8_t *)w)[(int64_t)row * width + col];
-    const uint8_t byte = ((const uint8_t *)w)[(int64_t)row * fp4_row_bytes(width) + col / 2];
-    const uint32_t code = (col & 1) ? (byte >> 4) : (byte & 15u);
-    return (g * sc) * (double)fp4_value(code);
-}
 
 __device__ __forceinline__ double sigmoid_d(double x) { return 1.0 / (1.0 + exp(-x)); }
 
@@ -121,83 +77,220 @@ struct BwdArgs {
     double *rows_y;         // T*k x d: routed experts' output rows
 };
 
-// One work row per iteration: recompute the expert's gate/up pre-activations,
-// hidden values and (routed rows) output, then its backward to the input
-// gradients.
-__global__ void __launch_bounds__(kBwdThreads) bwd_rows_kernel(const BwdArgs a) {
-    extern __shared__ double bsm[];
-    const int d = a.d, h = a.h;
-    double *sx = bsm;        // d  input row
-    double *sdy = sx + d;    // d  the expert's output gradients (gate-scaled for routed rows)
-    double *spg = sdy + d;   // h  gate pre-activations
-    double *spu = spg + h;   // h  up pre-activations
-    double *shid = spu + h;  // h  hidden values, then the gate pre-activation gradients
-    double *sdh = shid + h;  // h  up pre-activation gradients
-    const int64_t n_shared_rows = (int64_t)a.S * a.T;
-    const int64_t n_rows = n_shared_rows + a.T * a.k;
-    for (int64_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
-        int64_t t, slot = -1;
-        int e;
-        double gate = 1.0;
-        if (r < n_shared_rows) {
-            e = (int)(r / a.T);
-            t = r % a.T;
-        } else {
-            slot = r - n_shared_rows;
-            t = slot / a.k;
-            e = a.S + a.chosen[slot];
-            gate = a.gates[slot];
+// ---- Grouped float64 GEMM stages (the expert part of the backward).
+//
+// The work rows are taken expert by expert (shared experts' rows s*T + t,
+// then each routed expert's (token, slot) rows in the forward's token order),
+// in tiles of kBgRows rows of one expert, so that every dequantised weight
+// tile serves kBgRows rows instead of one:
+//   stage 0: PG, PU = X Wg^T + bg, X Wu^T + bu          (K = d, N = h)
+//   stage 1: Y = H Wd^T + bd, H = act_g(PG) act_u(PU)     (routed rows; K = h, N = d)
+//   stage 2: dH = dY' Wd (dY' = dout, gate-scaled for routed rows), then in
+//            place PG <- dH act_u(PU) act_g'(PG), PU <- dH act_g(PG) act_u'(PU)
+//                                                        (K = d, N = h)
+//   stage 3: dX = dG Wg + dU Wu                          (K = h, N = d)
+// Each output is one float64 sum over K in ascending order; against the
+// reference's sequence (per-block partial sums times the scale, zeros
+// skipped) it differs by rounding only.
+constexpr int kBgRows = 64;   // rows per tile (one expert)
+constexpr int kBgCols = 64;   // output columns per tile
+constexpr int kBgK = 16;      // inputs per shared-memory step
+constexpr int kBgThreads = 256;
+
+// Work rows in expert-major order (wrow) and each group's first entry (goff):
+// group s < S is shared expert s (rows s*T + t), group S + e routed expert e.
+__global__ void bwd_worklist_kernel(const int32_t *__restrict__ chosen, const int32_t *__restrict__ perm,
+                                    const int64_t *__restrict__ offsets, int64_t T, int k, int S, int E,
+                                    int64_t *__restrict__ wrow, int64_t *__restrict__ goff) {
+    const int64_t n_shared = (int64_t)S * T;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i <= S + E) goff[i] = i <= S ? i * T : n_shared + offsets[i - S];
+    if (i < n_shared) wrow[i] = i;
+    if (i < T * k) {
+        // the (token, slot) pair i: its position in its expert's token list
+        const int64_t t = i / k;
+        const int e = chosen[i];
+        int64_t lo = offsets[e], hi = offsets[e + 1];  // perm[lo..hi) ascending tokens
+        while (hi - lo > 1) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (perm[mid] <= t) lo = mid;
+            else hi = mid;
         }
-        const ExpertLayers &L = a.experts[e];
-        for (int i = threadIdx.x; i < d; i += blockDim.x) {
-            sx[i] = a.x[t * d + i];
-            const double g = a.dout[t * d + i];
-            sdy[i] = slot >= 0 ? g * gate : g;  // vectormath.Scale for routed rows
-        }
-        __syncthreads();
-        // forward recompute: gate and up layers (d -> h), hidden = act_g * act_u
-        for (int j = threadIdx.x; j < h; j += blockDim.x) {
-            const double pg = dot_row_f64(L.w[0], L.s[0], a.prec, d, j, sx) + (L.b64[0] ? L.b64[0][j] : 0.0);
-            const double pu = dot_row_f64(L.w[1], L.s[1], a.prec, d, j, sx) + (L.b64[1] ? L.b64[1][j] : 0.0);
-            spg[j] = pg;
-            spu[j] = pu;
-            shid[j] = gate_act<double>(pg, a.clamped, a.limit) * up_act<double>(pu, a.clamped, a.limit);
-        }
-        __syncthreads();
-        // routed rows: the expert's output row (down layer, linear), for the router term
-        if (slot >= 0)
-            for (int o = threadIdx.x; o < d; o += blockDim.x)
-                a.rows_y[slot * d + o] =
-                    dot_row_f64(L.w[2], L.s[2], a.prec, h, o, shid) + (L.b64[2] ? L.b64[2][o] : 0.0);
-        __syncthreads();
-        // Down.Backward: dH[j] = sum over output neurons o (ascending, zeros
-        // skipped) of the scaled row term; the linear derivative is 1.  Then
-        // the gate / up pre-activation gradients.
-        for (int j = threadIdx.x; j < h; j += blockDim.x) {
-            double dh = 0;
-            for (int o = 0; o < d; o++) {
-                const double g = sdy[o] * 1.0;
-                if (g != 0) dh += scaled_weight(L.w[2], L.s[2], a.prec, h, o, j, g);
+        wrow[n_shared + lo] = n_shared + i;
+    }
+}
+
+// Tiles of kBgRows rows per group: tprefix[g] = tiles before group g.
+__global__ void bwd_tiles_kernel(const int64_t *__restrict__ goff, int G, int64_t *__restrict__ tprefix) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    int64_t n = 0;
+    for (int g = 0; g < G; g++) {
+        tprefix[g] = n;
+        n += (goff[g + 1] - goff[g] + kBgRows - 1) / kBgRows;
+    }
+    tprefix[G] = n;
+}
+
+// Weight (row, col) of a layer as float64 (code times its block scale).
+__device__ __forceinline__ double layer_value(const void *w, const float *s, int prec, int width, int row, int col) {
+    if (prec == GTMOE_FLOAT64) return ((const double *)w)[(int64_t)row * width + col];
+    if (prec == GTMOE_FLOAT32) return (double)((const float *)w)[(int64_t)row * width + col];
+    const double sc = (double)s[(int64_t)row * scale_blocks(width) + col / kValuesPerScale];
+    if (prec == GTMOE_INT8) return sc * (double)((const int8_t *)w)[(int64_t)row * width + col];
+    const uint8_t byte = ((const uint8_t *)w)[(int64_t)row * fp4_row_bytes(width) + col / 2];
+    return sc * (double)fp4_value((col & 1) ? (byte >> 4) : (byte & 15u));
+}
+
+struct BgArgs {
+    const ExpertLayers *experts;  // shared experts first, then routed
+    int prec, S, k, d, h, clamped;
+    double limit;
+    int64_t T;
+    const int64_t *wrow, *goff, *tprefix;
+    int G;                 // groups: S + E
+    const double *x;       // T x d, the Forward's input rows
+    const double *dout;    // T x d
+    const double *gates;   // T x k
+    double *pg, *pu;       // n_rows x h, by work row
+    double *rows_y;        // T*k x d
+    double *rows_dx;       // n_rows x d
+};
+
+// One tile of kBgRows rows (one group) x kBgCols outputs of stage MODE.
+template <int MODE>
+__global__ void __launch_bounds__(kBgThreads) bwd_gemm_kernel(const BgArgs a) {
+    constexpr bool kDual = MODE == 0 || MODE == 3;  // two weight layers (gate and up)
+    constexpr bool kNT = MODE == 0 || MODE == 1;    // W indexed [output][input]
+    const int K = (MODE == 0 || MODE == 2) ? a.d : a.h;
+    const int N = (MODE == 0 || MODE == 2) ? a.h : a.d;
+    __shared__ double sa[kDual && MODE == 3 ? 2 : 1][kBgRows][kBgK + 1];
+    __shared__ double sb[kDual ? 2 : 1][kBgK][kBgCols + 1];
+    __shared__ int64_t srow[kBgRows];
+    const int64_t tile = blockIdx.x;
+    if (tile >= a.tprefix[a.G]) return;
+    int lo = 0, hi = a.G;  // the group of this tile: last g with tprefix[g] <= tile
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (a.tprefix[mid] <= tile) lo = mid;
+        else hi = mid;
+    }
+    const int g = lo;
+    if (MODE == 1 && g < a.S) return;  // the expert outputs are needed for routed rows only
+    const int64_t n_shared = (int64_t)a.S * a.T;
+    const int64_t r0 = (tile - a.tprefix[g]) * kBgRows;
+    const int64_t n_g = a.goff[g + 1] - a.goff[g];
+    const int n0 = blockIdx.y * kBgCols;
+    if (threadIdx.x < kBgRows) {
+        const int64_t i = r0 + threadIdx.x;
+        srow[threadIdx.x] = i < n_g ? a.wrow[a.goff[g] + i] : -1;
+    }
+    const ExpertLayers &L = a.experts[g];
+    __syncthreads();
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // outputs 4 tx .. 4 tx + 3, rows 4 ty .. 4 ty + 3
+    double acc[kDual ? 2 : 1][4][4];
+#pragma unroll
+    for (int l = 0; l < (kDual ? 2 : 1); l++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[l][i][j] = 0.0;
+    for (int k0 = 0; k0 < K; k0 += kBgK) {
+        for (int e = threadIdx.x; e < kBgRows * kBgK; e += kBgThreads) {
+            const int rr = e / kBgK, kk = e % kBgK;
+            const int64_t r = srow[rr];
+            const int kc = k0 + kk;
+            double v0 = 0.0, v1 = 0.0;
+            if (r >= 0 && kc < K) {
+                const int64_t t = r < n_shared ? r % a.T : (r - n_shared) / a.k;
+                if (MODE == 0) {
+                    v0 = a.x[t * a.d + kc];
+                } else if (MODE == 1) {
+                    v0 = gate_act<double>(a.pg[r * a.h + kc], a.clamped, a.limit) *
+                         up_act<double>(a.pu[r * a.h + kc], a.clamped, a.limit);
+                } else if (MODE == 2) {
+                    const double g0 = a.dout[t * a.d + kc];
+                    v0 = r < n_shared ? g0 : g0 * a.gates[r - n_shared];  // vectormath.Scale for routed rows
+                } else {
+                    v0 = a.pg[r * a.h + kc];
+                    v1 = a.pu[r * a.h + kc];
+                }
             }
-            const double pg = spg[j], pu = spu[j];
-            const double go = gate_act<double>(pg, a.clamped, a.limit);
-            const double uo = up_act<double>(pu, a.clamped, a.limit);
-            shid[j] = (dh * uo) * gate_deriv(pg, a.clamped, a.limit);
-            sdh[j] = (dh * go) * up_deriv(pu, a.clamped, a.limit);
+            sa[0][rr][kk] = v0;
+            if (MODE == 3) sa[MODE == 3 ? 1 : 0][rr][kk] = v1;
         }
-        __syncthreads();
-        // Gate.Backward + Up.Backward input gradients (neurons ascending, zeros skipped)
-        double *dst = a.rows_dx + r * d;
-        for (int c = threadIdx.x; c < d; c += blockDim.x) {
-            double dg = 0, du = 0;
-            for (int j = 0; j < h; j++) {
-                const double gg = shid[j], gu = sdh[j];
-                if (gg != 0) dg += scaled_weight(L.w[0], L.s[0], a.prec, d, j, c, gg);
-                if (gu != 0) du += scaled_weight(L.w[1], L.s[1], a.prec, d, j, c, gu);
+        for (int e = threadIdx.x; e < kBgK * kBgCols; e += kBgThreads) {
+            // coalesced along the layer rows: inputs fastest for [output][input], outputs fastest otherwise
+            const int kk = kNT ? e % kBgK : e / kBgCols, nn = kNT ? e / kBgK : e % kBgCols;
+            const int kc = k0 + kk, nc = n0 + nn;
+            double w0 = 0.0, w1 = 0.0;
+            if (kc < K && nc < N) {
+                if (MODE == 0) {
+                    w0 = layer_value(L.w[0], L.s[0], a.prec, a.d, nc, kc);
+                    w1 = layer_value(L.w[1], L.s[1], a.prec, a.d, nc, kc);
+                } else if (MODE == 1) {
+                    w0 = layer_value(L.w[2], L.s[2], a.prec, a.h, nc, kc);
+                } else if (MODE == 2) {
+                    w0 = layer_value(L.w[2], L.s[2], a.prec, a.h, kc, nc);
+                } else {
+                    w0 = layer_value(L.w[0], L.s[0], a.prec, a.d, kc, nc);
+                    w1 = layer_value(L.w[1], L.s[1], a.prec, a.d, kc, nc);
+                }
             }
-            dst[c] = dg + du;
+            sb[0][kk][nn] = w0;
+            if (kDual) sb[kDual ? 1 : 0][kk][nn] = w1;
         }
         __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < kBgK; kk++) {
+            double av[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) av[i] = sa[0][4 * ty + i][kk];
+#pragma unroll
+            for (int j = 0; j < 4; j++) b[j] = sb[0][kk][4 * tx + j];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[0][i][j] = fma(av[i], b[j], acc[0][i][j]);
+            if (kDual) {
+                if (MODE == 3)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) av[i] = sa[MODE == 3 ? 1 : 0][4 * ty + i][kk];
+#pragma unroll
+                for (int j = 0; j < 4; j++) b[j] = sb[kDual ? 1 : 0][kk][4 * tx + j];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) acc[kDual ? 1 : 0][i][j] = fma(av[i], b[j], acc[kDual ? 1 : 0][i][j]);
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int64_t r = srow[4 * ty + i];
+        if (r < 0) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int n = n0 + 4 * tx + j;
+            if (n >= N) continue;
+            if (MODE == 0) {
+                a.pg[r * a.h + n] = acc[0][i][j] + (L.b64[0] ? L.b64[0][n] : 0.0);
+                a.pu[r * a.h + n] = acc[kDual ? 1 : 0][i][j] + (L.b64[1] ? L.b64[1][n] : 0.0);
+            } else if (MODE == 1) {
+                a.rows_y[(r - n_shared) * a.d + n] = acc[0][i][j] + (L.b64[2] ? L.b64[2][n] : 0.0);
+            } else if (MODE == 2) {
+                // the linear down layer's derivative is 1; then the gate / up
+                // pre-activation gradients, in place of the pre-activations
+                const double dh = acc[0][i][j];
+                const double pg = a.pg[r * a.h + n], pu = a.pu[r * a.h + n];
+                const double go = gate_act<double>(pg, a.clamped, a.limit);
+                const double uo = up_act<double>(pu, a.clamped, a.limit);
+                a.pg[r * a.h + n] = (dh * uo) * gate_deriv(pg, a.clamped, a.limit);
+                a.pu[r * a.h + n] = (dh * go) * up_deriv(pu, a.clamped, a.limit);
+            } else {
+                a.rows_dx[r * a.d + n] = acc[0][i][j] + acc[kDual ? 1 : 0][i][j];
+            }
+        }
     }
 }
 
@@ -345,7 +438,7 @@ int save_training_state(gtmoe_handle *h, const void *x_dev, int x_dtype, int64_t
 void release_training_state(gtmoe_handle *h) {
     DevBuf *bufs[] = {&h->tr_x,    &h->tr_chosen, &h->tr_gates, &h->tr_perm, &h->tr_offsets, &h->bw_in,
                       &h->bw_dout, &h->bw_dx,     &h->bw_rows,  &h->bw_y,    &h->bw_lg,      &h->bw_zag,
-                      &h->bw_rw,   &h->bw_rb};
+                      &h->bw_rw,   &h->bw_rb,     &h->bw_work,  &h->bw_pgpu};
     for (DevBuf *b : bufs) b->release();
     h->tr_valid = 0;
 }
@@ -431,11 +524,56 @@ int gtmoe_backward(gtmoe_t h, const void *dout, int dout_dtype, void *dx, int dx
     a.dout = h->bw_dout.as<double>();
     a.rows_dx = h->bw_rows.as<double>();
     a.rows_y = h->bw_y.as<double>();
-    const size_t smem = sizeof(double) * (2 * (size_t)d + 4 * (size_t)hd);
-    if (smem > 220 * 1024) return fail(GTMOE_EINVAL, "backward: d_model and hidden too large for one work row");
-    GT_CUDA(cudaFuncSetAttribute(bwd_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    bwd_rows_kernel<<<grid_for(n_rows, 1), kBwdThreads, smem, st>>>(a);
+    // the experts' part as four grouped float64 GEMM stages over the work
+    // rows taken expert by expert (see bwd_gemm_kernel)
+    const int G = S + E;
+    GT_CHECK(h->bw_work.ensure(sizeof(int64_t) * ((size_t)n_rows + 2 * (size_t)(G + 1))));
+    GT_CHECK(h->bw_pgpu.ensure(2 * sizeof(double) * (size_t)n_rows * hd));
+    int64_t *wrow = h->bw_work.as<int64_t>(), *goff = wrow + n_rows, *tprefix = goff + G + 1;
+    {
+        int64_t n = (int64_t)S * T > T * k ? (int64_t)S * T : T * k;
+        n = n > G + 1 ? n : G + 1;
+        bwd_worklist_kernel<<<grid_for(n, 256), 256, 0, st>>>(a.chosen, h->tr_perm.as<int32_t>(),
+                                                               h->tr_offsets.as<int64_t>(), T, k, S, E, wrow, goff);
+        GT_CUDA(cudaGetLastError());
+        bwd_tiles_kernel<<<1, 32, 0, st>>>(goff, G, tprefix);
+        GT_CUDA(cudaGetLastError());
+    }
+    BgArgs b;
+    b.experts = a.experts;
+    b.prec = a.prec;
+    b.S = S;
+    b.k = k;
+    b.d = d;
+    b.h = hd;
+    b.clamped = a.clamped;
+    b.limit = a.limit;
+    b.T = T;
+    b.wrow = wrow;
+    b.goff = goff;
+    b.tprefix = tprefix;
+    b.G = G;
+    b.x = a.x;
+    b.dout = a.dout;
+    b.gates = a.gates;
+    b.pg = h->bw_pgpu.as<double>();
+    b.pu = b.pg + (size_t)n_rows * hd;
+    b.rows_y = a.rows_y;
+    b.rows_dx = a.rows_dx;
+    const unsigned tiles_ub = (unsigned)(n_rows / kBgRows + G);
+    const dim3 grid_h(tiles_ub, (unsigned)((hd + kBgCols - 1) / kBgCols));
+    const dim3 grid_d(tiles_ub, (unsigned)((d + kBgCols - 1) / kBgCols));
+    bwd_gemm_kernel<0><<<grid_h, kBgThreads, 0, st>>>(b);
     GT_CUDA(cudaGetLastError());
+    if (router) {
+        bwd_gemm_kernel<1><<<grid_d, kBgThreads, 0, st>>>(b);
+        GT_CUDA(cudaGetLastError());
+    }
+    bwd_gemm_kernel<2><<<grid_h, kBgThreads, 0, st>>>(b);
+    GT_CUDA(cudaGetLastError());
+    bwd_gemm_kernel<3><<<grid_d, kBgThreads, 0, st>>>(b);
+    GT_CUDA(cudaGetLastError());
+    note_launches(router ? 6 : 5);
     if (router) {
         bwd_router_kernel<<<grid_for(T, 128), 128, 0, st>>>(zl, za, zg, a.dout, a.rows_y, T, d, k,
                                                              h->bw_lg.as<double>());
@@ -461,7 +599,7 @@ int gtmoe_backward(gtmoe_t h, const void *dout, int dout_dtype, void *dx, int dx
         bwd_dx_kernel<__nv_bfloat16><<<gdx, 256, 0, st>>>(a.rows_dx, lg, a.chosen, wr, T, d, S, k, router,
                                                            (__nv_bfloat16 *)dx_dev);
     GT_CUDA(cudaGetLastError());
-    note_launches(router ? 6 : 4);
+    note_launches(router ? 5 : 3);
 
     // router parameter gradients, added to the caller's
     if (router && (router_weight_grad || router_bias_grad)) {

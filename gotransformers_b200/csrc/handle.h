@@ -128,6 +128,8 @@ struct gtmoe_handle {
     int64_t tr_T = 0;
     DevBuf tr_x, tr_chosen, tr_gates, tr_perm, tr_offsets;
     DevBuf bw_in, bw_dout, bw_dx, bw_rows, bw_y, bw_lg, bw_zag, bw_rw, bw_rb;
+    DevBuf bw_work;  // work rows expert by expert, group offsets, tile prefix
+    DevBuf bw_pgpu;  // gate / up pre-activations, then their gradients (work rows x hidden, twice)
 
     // host-buffer forwards of large batches: chunks whose copies overlap the
     // compute of their neighbours (api.cu, forward_pipelined)
